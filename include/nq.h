@@ -1,0 +1,149 @@
+/*
+ * nq.h -- C ABI of the B200 quantized-matmul library (libnq.so).
+ *
+ * The entry points replace the quantized-linear calls that neurons' models
+ * make into MLX (MLXBackend serves them today):
+ *   nq_quantized_matmul  <- mx::quantized_matmul(x, w, scales, biases,
+ *                           transpose=true, gs, bits, "affine")
+ *                           compute/src/compute/model/mlx_ops.h:28-42 (lin)
+ *   nq_dequantize        <- mx::dequantize(w, scales, biases, gs, bits)
+ *                           compute/src/compute/model/llama_model.cpp:67,
+ *                           gemma_model_mlx.cpp:82, qwen3_moe_model_mlx.cpp:411,
+ *                           qwen3_transformer_moe_model_mlx.cpp:183
+ *   nq_gather_qmm        <- mx::gather_qmm(x, w, scales, biases, lhs=nullopt,
+ *                           rhs=topk_idx, transpose=true, gs, bits)
+ *                           qwen3_transformer_moe_model_mlx.cpp:69-74,
+ *                           qwen3_moe_model_mlx.cpp:356-364
+ *   nq_moe_route         <- router of the switch step (softmax fp32, top-k,
+ *                           renormalise) qwen3_transformer_moe_model_mlx.cpp:36-48
+ *   nq_moe_switch        <- the whole switch-MLP step for T tokens
+ *                           (gate/up gather_qmm, SwiGLU, down gather_qmm,
+ *                           score-weighted sum) qwen3_transformer_moe_model_mlx.cpp:29-79;
+ *                           batched over tokens instead of the token loop at
+ *                           qwen3_transformer_moe_model_mlx.cpp:479-486
+ *   nq_quantize          <- mx::quantize(w, gs, bits) (MLX affine; the
+ *                           reference loads pre-quantized checkpoints and has
+ *                           no call site of its own)
+ *   nq_bits_from_shapes  <- mlx_ops::bits  compute/src/compute/model/mlx_ops.h:20-25
+ *
+ * Conventions
+ *   - Every tensor pointer is a DEVICE pointer (cudaMalloc'd or equivalent),
+ *     row-major and contiguous.  bf16 tensors are passed as uint16_t bit
+ *     patterns.  Packed weights are uint32 words holding 32/bits codes, the
+ *     lowest-index code in the lowest bits (MLX layout).
+ *   - Weight shapes follow MLX's transpose=true layout: w [N, K*bits/32],
+ *     scales and biases [N, K/group_size]; stacked experts prepend [E].
+ *   - bits is 4 or 8; group_size is 32, 64 or 128; K % group_size == 0.
+ *   - stream is a cudaStream_t (NULL = the legacy default stream).  Every call
+ *     is asynchronous on that stream and allocates nothing.
+ *   - Return value: an nq_status.  The message of the last failure on the
+ *     calling thread is available from nq_last_error().
+ */
+#ifndef NQ_H_
+#define NQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Mirrors compute::ErrorCode (compute/src/compute/core/compute_types.h:9-16). */
+typedef enum nq_status {
+    NQ_SUCCESS = 0,
+    NQ_INVALID_INPUT = 1,
+    NQ_INVALID_MODEL = 2,
+    NQ_BACKEND_NOT_AVAILABLE = 3,
+    NQ_COMPUTE_ERROR = 4,
+    NQ_UNKNOWN_ERROR = 5
+} nq_status;
+
+/* Quantization schemes for nq_quantize. */
+#define NQ_SCHEME_MLX_AFFINE 0 /* MLX affine quantizer (edge snapping) */
+#define NQ_SCHEME_MINMAX 1     /* scale=(max-min)/(2^bits-1), bias=min */
+
+/* Input dtypes for nq_quantize. */
+#define NQ_DTYPE_F32 0
+#define NQ_DTYPE_BF16 1
+
+/* Library identity / diagnostics (no reference counterpart: FFI plumbing). */
+int nq_version(void);
+const char *nq_last_error(void);
+/* Number of CUDA devices usable by the library (0 when none); never fails. */
+int nq_device_count(void);
+/* Reads and clears the device-side error word of the current device (set by a
+ * kernel whose bounded wait ran out, or by an out-of-range gather index).
+ * 0 = no error. */
+int nq_take_device_error(unsigned int *err_out);
+
+/* mlx_ops::bits: round(32 * (w_cols / s_cols) / group_size), 4 if not positive. */
+int nq_bits_from_shapes(int64_t w_cols, int64_t s_cols, int group_size);
+
+/* mx::quantize.  w: [rows, K] fp32 or bf16 (w_dtype).  Outputs: wq [rows,
+ * K*bits/32] uint32, scales/biases [rows, K/group_size] bf16. */
+int nq_quantize(const void *w, int w_dtype, int64_t rows, int64_t K, int bits,
+                int group_size, int scheme, uint32_t *wq, uint16_t *scales,
+                uint16_t *biases, void *stream);
+
+/* mx::dequantize.  out: [rows, K] bf16, bit-exact bf16(bf16(s*q) + b). */
+int nq_dequantize(const uint32_t *wq, const uint16_t *scales,
+                  const uint16_t *biases, int64_t rows, int64_t K, int bits,
+                  int group_size, uint16_t *out, void *stream);
+
+/* mx::quantized_matmul(x, w, scales, biases, transpose=true, gs, bits).
+ * x: [M, K] bf16; y: [M, N] bf16.  fp32 accumulation.  biases must be
+ * non-NULL (affine mode).  M may be 0. */
+int nq_quantized_matmul(const uint16_t *x, int64_t M, const uint32_t *wq,
+                        const uint16_t *scales, const uint16_t *biases,
+                        int64_t N, int64_t K, int bits, int group_size,
+                        uint16_t *y, void *stream);
+
+/* mx::gather_qmm(x, w, scales, biases, lhs_indices, rhs_indices,
+ * transpose=true, gs, bits).
+ *   x: [x_batch, M, K] bf16;  w: [E, N, K*bits/32];  scales/biases [E, N, K/gs]
+ *   out[i] ([M, N] slice of y: [n_idx, M, N]) = x[xi] . dequant(w[rhs[i]])^T,
+ *   xi = lhs[i] when lhs_indices != NULL, else i when x_batch == n_idx, else 0
+ *   (x_batch == 1 broadcasts).  Index arrays are DEVICE int32 arrays; indices
+ *   out of range make the affected output rows zero and raise the device error
+ *   word (nq_take_device_error). */
+int nq_gather_qmm(const uint16_t *x, int64_t x_batch, int64_t M,
+                  const int32_t *lhs_indices, const int32_t *rhs_indices,
+                  int64_t n_idx, const uint32_t *wq, const uint16_t *scales,
+                  const uint16_t *biases, int64_t E, int64_t N, int64_t K,
+                  int bits, int group_size, uint16_t *y, void *stream);
+
+/* Router of the MoE switch step.  logits: [T, E] bf16 (the output of the
+ * router linear).  Outputs topk_idx [T, top_k] int32 (descending probability,
+ * ties -> lower expert index) and topk_scores [T, top_k] fp32 (softmax over
+ * all E experts, renormalised over the selected top_k).  top_k <= 32,
+ * E <= 1024. */
+int nq_moe_route(const uint16_t *logits, int64_t T, int64_t E, int64_t top_k,
+                 int32_t *topk_idx, float *topk_scores, void *stream);
+
+/* Workspace bytes nq_moe_switch needs for T tokens. */
+size_t nq_moe_workspace_size(int64_t T, int64_t E, int64_t top_k, int64_t H,
+                             int64_t I);
+
+/* Switch-MLP of one MoE layer for T tokens (batched over tokens):
+ *   y[t] = sum_j bf16(score[t,j]) * down_e( bf16(silu(gate_e(x_t)) * up_e(x_t)) ),
+ *   e = topk_idx[t, j].
+ * x: [T, H] bf16; topk_idx/topk_scores as produced by nq_moe_route;
+ * gate/up: w [E, I, H*bits/32], s/b [E, I, H/gs];
+ * down:    w [E, H, I*bits/32], s/b [E, H, I/gs];  y: [T, H] bf16.
+ * workspace: device buffer of nq_moe_workspace_size() bytes (caller-owned). */
+int nq_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I,
+                  int64_t E, int64_t top_k, const int32_t *topk_idx,
+                  const float *topk_scores, const uint32_t *gate_w,
+                  const uint16_t *gate_s, const uint16_t *gate_b,
+                  const uint32_t *up_w, const uint16_t *up_s,
+                  const uint16_t *up_b, const uint32_t *down_w,
+                  const uint16_t *down_s, const uint16_t *down_b, int bits,
+                  int group_size, void *workspace, size_t workspace_bytes,
+                  uint16_t *y, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NQ_H_ */

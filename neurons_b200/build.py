@@ -1,0 +1,71 @@
+"""Build libnq.so (the C-ABI library) in-tree for sm_100a with nvcc.
+
+    python -m neurons_b200.build [--force] [-v]
+
+Each .cu under csrc/ is compiled to an object with
+`-gencode arch=compute_100a,code=sm_100a -lineinfo -O3`, the C++ backend
+(csrc/cuda_backend.cpp) with g++ -std=c++23, and everything is linked into
+neurons_b200/libnq.so.  Only the CUDA runtime is linked; the driver entry
+point for TMA descriptors is resolved at run time through
+cudaGetDriverEntryPoint.  `-v` prints ptxas register/spill reports.
+"""
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+BUILD = os.path.join(HERE, "_build")
+LIB = os.path.join(HERE, "libnq.so")
+ROOT = os.path.dirname(HERE)
+INCLUDE = os.path.join(ROOT, "include")
+
+CU_SOURCES = ["abi.cu", "quant.cu", "gemv.cu", "gemm_tc.cu", "moe.cu"]
+CPP_SOURCES = ["cuda_backend.cpp"]
+HEADERS = ["nq_common.cuh", "nq_internal.h", "cuda_backend.h", "compute_types.h"]
+
+CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I" + INCLUDE]
+
+
+def _newer(target, deps):
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    hdrs = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(INCLUDE, "nq.h")]
+    objs = []
+    for src in CU_SOURCES:
+        s = os.path.join(CSRC, src)
+        o = os.path.join(BUILD, src + ".o")
+        objs.append(o)
+        if force or verbose or _newer(o, [s] + hdrs):
+            cmd = [NVCC] + ARCH + NVFLAGS + ["-c", s, "-o", o]
+            if verbose:
+                cmd += ["-Xptxas", "-v"]
+            subprocess.run(cmd, check=True)
+    for src in CPP_SOURCES:
+        s = os.path.join(CSRC, src)
+        o = os.path.join(BUILD, src + ".o")
+        objs.append(o)
+        if force or _newer(o, [s] + hdrs):
+            subprocess.run(["g++", "-O2", "-std=c++23", "-fPIC", "-Wall", "-I" + INCLUDE,
+                            "-I" + os.path.join(CUDA_HOME, "include"), "-c", s, "-o", o],
+                           check=True)
+    if force or _newer(LIB, objs):
+        tmp = LIB + ".tmp%d" % os.getpid()
+        subprocess.run([NVCC] + ARCH + ["-shared", "-o", tmp] + objs +
+                       ["-lcudart", "-Xlinker", "-rpath," + os.path.join(CUDA_HOME, "lib64")],
+                       check=True)
+        os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))

@@ -1,0 +1,296 @@
+// abi.cu -- the extern "C" entry points declared in include/nq.h: argument
+// validation on the host, dispatch to the sm_100a kernels, status mapping.
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+
+#include "nq.h"
+#include "nq_internal.h"
+
+namespace nq {
+
+namespace {
+thread_local std::string g_last_error;
+
+// Device error word: one per device, set by kernels (bounded waits, bad
+// gather indices), read and cleared by nq_take_device_error.
+__device__ unsigned int g_device_error;
+
+constexpr int kMaxDevices = 64;
+unsigned int *g_err_ptr[kMaxDevices];
+int g_sms[kMaxDevices];
+std::mutex g_mu;
+
+int current_device() {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return d;
+}
+}  // namespace
+
+void set_error(const std::string &msg) { g_last_error = msg; }
+const char *last_error() { return g_last_error.c_str(); }
+
+unsigned int *device_error_word() {
+    const int d = current_device();
+    if (d < 0 || d >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_err_ptr[d]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_error) == cudaSuccess)
+            g_err_ptr[d] = static_cast<unsigned int *>(p);
+        else
+            cudaGetLastError();
+    }
+    return g_err_ptr[d];
+}
+
+int sm_count() {
+    const int d = current_device();
+    if (d < 0 || d >= kMaxDevices) return 148;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_sms[d]) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, d);
+        g_sms[d] = v > 0 ? v : 148;
+    }
+    return g_sms[d];
+}
+
+}  // namespace nq
+
+using nq::set_error;
+
+namespace {
+
+int fail(nq_status st, const std::string &msg) {
+    set_error(msg);
+    return st;
+}
+
+int from_cuda(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return NQ_SUCCESS;
+    return fail(NQ_COMPUTE_ERROR, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_quant(int64_t rows, int64_t K, int bits, int gs, const char *fn) {
+    if (bits != 4 && bits != 8)
+        return fail(NQ_INVALID_INPUT, std::string(fn) + ": bits must be 4 or 8, got " +
+                                          std::to_string(bits));
+    if (gs != 32 && gs != 64 && gs != 128)
+        return fail(NQ_INVALID_INPUT, std::string(fn) +
+                                          ": group_size must be 32, 64 or 128, got " +
+                                          std::to_string(gs));
+    if (rows < 0 || K <= 0)
+        return fail(NQ_INVALID_INPUT, std::string(fn) + ": shapes must be positive");
+    if (K % gs)
+        return fail(NQ_INVALID_INPUT, std::string(fn) + ": K=" + std::to_string(K) +
+                                          " is not a multiple of group_size=" + std::to_string(gs));
+    return NQ_SUCCESS;
+}
+
+int need_device(const char *fn) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(NQ_BACKEND_NOT_AVAILABLE, std::string(fn) + ": no CUDA device");
+    }
+    return NQ_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" {
+
+int nq_version(void) { return 1; }
+
+const char *nq_last_error(void) { return nq::last_error(); }
+
+int nq_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+int nq_take_device_error(unsigned int *err_out) {
+    if (!err_out) return fail(NQ_INVALID_INPUT, "nq_take_device_error: err_out is NULL");
+    if (int rc = need_device("nq_take_device_error")) return rc;
+    unsigned int v = 0, zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, nq::g_device_error, sizeof(v));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(nq::g_device_error, &zero, sizeof(zero));
+    *err_out = v;
+    return from_cuda(e, "nq_take_device_error");
+}
+
+int nq_bits_from_shapes(int64_t w_cols, int64_t s_cols, int group_size) {
+    if (s_cols <= 0 || group_size <= 0) return 4;
+    const double v = 32.0 * ((double)w_cols / (double)s_cols) / (double)group_size;
+    const int b = (int)(v < 0 ? v - 0.5 : v + 0.5);
+    return b > 0 ? b : 4;
+}
+
+int nq_quantize(const void *w, int w_dtype, int64_t rows, int64_t K, int bits, int group_size,
+                int scheme, uint32_t *wq, uint16_t *scales, uint16_t *biases, void *stream) {
+    if (int rc = check_quant(rows, K, bits, group_size, "nq_quantize")) return rc;
+    if (w_dtype != NQ_DTYPE_F32 && w_dtype != NQ_DTYPE_BF16)
+        return fail(NQ_INVALID_INPUT, "nq_quantize: w_dtype must be NQ_DTYPE_F32 or NQ_DTYPE_BF16");
+    if (scheme != NQ_SCHEME_MLX_AFFINE && scheme != NQ_SCHEME_MINMAX)
+        return fail(NQ_INVALID_INPUT, "nq_quantize: unknown scheme");
+    if (rows == 0) return NQ_SUCCESS;
+    if (!w || !wq || !scales || !biases)
+        return fail(NQ_INVALID_INPUT, "nq_quantize: NULL tensor pointer");
+    if (!aligned16(w) || !aligned16(wq))
+        return fail(NQ_INVALID_INPUT, "nq_quantize: w and wq must be 16-byte aligned");
+    if (int rc = need_device("nq_quantize")) return rc;
+    return from_cuda(nq::launch_quantize(w, w_dtype, rows, K, bits, group_size, scheme, wq, scales,
+                                         biases, static_cast<cudaStream_t>(stream)),
+                     "nq_quantize");
+}
+
+int nq_dequantize(const uint32_t *wq, const uint16_t *scales, const uint16_t *biases, int64_t rows,
+                  int64_t K, int bits, int group_size, uint16_t *out, void *stream) {
+    if (int rc = check_quant(rows, K, bits, group_size, "nq_dequantize")) return rc;
+    if (rows == 0) return NQ_SUCCESS;
+    if (!wq || !scales || !out) return fail(NQ_INVALID_INPUT, "nq_dequantize: NULL tensor pointer");
+    if (!biases)
+        return fail(NQ_INVALID_INPUT,
+                    "nq_dequantize: biases must be provided for affine quantization");
+    if (!aligned16(wq) || !aligned16(out))
+        return fail(NQ_INVALID_INPUT, "nq_dequantize: wq and out must be 16-byte aligned");
+    if (int rc = need_device("nq_dequantize")) return rc;
+    return from_cuda(nq::launch_dequantize(wq, scales, biases, rows, K, bits, group_size, out,
+                                           static_cast<cudaStream_t>(stream)),
+                     "nq_dequantize");
+}
+
+// M at or above which the tcgen05 GEMM replaces the mma.sync GEMV.
+static int64_t tc_threshold() { return 33; }
+
+int nq_quantized_matmul(const uint16_t *x, int64_t M, const uint32_t *wq, const uint16_t *scales,
+                        const uint16_t *biases, int64_t N, int64_t K, int bits, int group_size,
+                        uint16_t *y, void *stream) {
+    if (int rc = check_quant(N, K, bits, group_size, "nq_quantized_matmul")) return rc;
+    if (M < 0) return fail(NQ_INVALID_INPUT, "nq_quantized_matmul: M must be >= 0");
+    if (M == 0 || N == 0) return NQ_SUCCESS;
+    if (!x || !wq || !scales || !y)
+        return fail(NQ_INVALID_INPUT, "nq_quantized_matmul: NULL tensor pointer");
+    if (!biases)
+        return fail(NQ_INVALID_INPUT,
+                    "nq_quantized_matmul: biases must be provided for affine quantization");
+    if (!aligned16(x) || !aligned16(wq))
+        return fail(NQ_INVALID_INPUT, "nq_quantized_matmul: x and wq must be 16-byte aligned");
+    if (N > 16 * 65535LL * 65535LL || M > (1LL << 31) - 1)
+        return fail(NQ_INVALID_INPUT, "nq_quantized_matmul: shape too large");
+    if (int rc = need_device("nq_quantized_matmul")) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (M >= tc_threshold()) {
+        nq::TcGemmArgs a;
+        a.x = x; a.x_ld = K; a.M = M;
+        a.w = wq; a.s = scales; a.b = biases;
+        a.N = N; a.K = K; a.bits = bits; a.gs = group_size;
+        a.y = y; a.y_ld = N;
+        if (nq::tc_gemm_supported(a))
+            return from_cuda(nq::launch_tc_gemm(a, st), "nq_quantized_matmul");
+    }
+    nq::GemvProblems p;
+    p.w = wq; p.s = scales; p.b = biases;
+    p.N = N; p.K = K; p.bits = bits; p.gs = group_size;
+    p.x = x; p.x_ld = K;
+    p.P = 1; p.M = (int)M; p.max_m = (int)M;
+    p.y = y; p.y_ld = N;
+    return from_cuda(nq::launch_gemv(p, st), "nq_quantized_matmul");
+}
+
+int nq_gather_qmm(const uint16_t *x, int64_t x_batch, int64_t M, const int32_t *lhs_indices,
+                  const int32_t *rhs_indices, int64_t n_idx, const uint32_t *wq,
+                  const uint16_t *scales, const uint16_t *biases, int64_t E, int64_t N, int64_t K,
+                  int bits, int group_size, uint16_t *y, void *stream) {
+    if (int rc = check_quant(N, K, bits, group_size, "nq_gather_qmm")) return rc;
+    if (M < 0 || n_idx < 0 || E <= 0 || x_batch <= 0)
+        return fail(NQ_INVALID_INPUT, "nq_gather_qmm: invalid batch/expert sizes");
+    if (!lhs_indices && x_batch != 1 && x_batch != n_idx)
+        return fail(NQ_INVALID_INPUT,
+                    "nq_gather_qmm: without lhs_indices x_batch must be 1 or equal n_idx");
+    if (M == 0 || N == 0 || n_idx == 0) return NQ_SUCCESS;
+    if (n_idx > 65535) return fail(NQ_INVALID_INPUT, "nq_gather_qmm: at most 65535 indices");
+    if (!x || !rhs_indices || !wq || !scales || !y)
+        return fail(NQ_INVALID_INPUT, "nq_gather_qmm: NULL tensor pointer");
+    if (!biases)
+        return fail(NQ_INVALID_INPUT,
+                    "nq_gather_qmm: biases must be provided for affine quantization");
+    if (!aligned16(x) || !aligned16(wq))
+        return fail(NQ_INVALID_INPUT, "nq_gather_qmm: x and wq must be 16-byte aligned");
+    if (int rc = need_device("nq_gather_qmm")) return rc;
+    nq::GemvProblems p;
+    p.w = wq; p.s = scales; p.b = biases;
+    p.N = N; p.K = K; p.bits = bits; p.gs = group_size;
+    p.x = x; p.x_ld = K;
+    p.P = (int)n_idx; p.M = (int)M; p.max_m = (int)M;
+    p.E = (int)E;
+    p.expert = rhs_indices;
+    p.lhs = lhs_indices;
+    p.x_batch = (int)x_batch;
+    p.y = y; p.y_ld = N;
+    return from_cuda(nq::launch_gemv(p, static_cast<cudaStream_t>(stream)), "nq_gather_qmm");
+}
+
+int nq_moe_route(const uint16_t *logits, int64_t T, int64_t E, int64_t top_k, int32_t *topk_idx,
+                 float *topk_scores, void *stream) {
+    if (T < 0 || E <= 0 || E > 1024 || top_k <= 0 || top_k > 32 || top_k > E)
+        return fail(NQ_INVALID_INPUT, "nq_moe_route: need 0 < top_k <= min(E, 32), E <= 1024");
+    if (T == 0) return NQ_SUCCESS;
+    if (!logits || !topk_idx || !topk_scores)
+        return fail(NQ_INVALID_INPUT, "nq_moe_route: NULL tensor pointer");
+    if (int rc = need_device("nq_moe_route")) return rc;
+    return from_cuda(nq::launch_moe_route(logits, T, E, top_k, topk_idx, topk_scores,
+                                          static_cast<cudaStream_t>(stream)),
+                     "nq_moe_route");
+}
+
+size_t nq_moe_workspace_size(int64_t T, int64_t E, int64_t top_k, int64_t H, int64_t I) {
+    if (T < 0 || E <= 0 || top_k <= 0 || H <= 0 || I <= 0) return 0;
+    return nq::moe_workspace_bytes(T, E, top_k, H, I);
+}
+
+int nq_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t top_k,
+                  const int32_t *topk_idx, const float *topk_scores, const uint32_t *gate_w,
+                  const uint16_t *gate_s, const uint16_t *gate_b, const uint32_t *up_w,
+                  const uint16_t *up_s, const uint16_t *up_b, const uint32_t *down_w,
+                  const uint16_t *down_s, const uint16_t *down_b, int bits, int group_size,
+                  void *workspace, size_t workspace_bytes, uint16_t *y, void *stream) {
+    if (int rc = check_quant(I, H, bits, group_size, "nq_moe_switch")) return rc;
+    if (int rc = check_quant(H, I, bits, group_size, "nq_moe_switch")) return rc;
+    if (T < 0 || E <= 0 || E > 1024 || top_k <= 0 || top_k > 32 || top_k > E)
+        return fail(NQ_INVALID_INPUT, "nq_moe_switch: need 0 < top_k <= min(E, 32), E <= 1024");
+    if (H % 4) return fail(NQ_INVALID_INPUT, "nq_moe_switch: H must be a multiple of 4");
+    if (T == 0) return NQ_SUCCESS;
+    if (T * top_k > 65535 * 64)
+        return fail(NQ_INVALID_INPUT, "nq_moe_switch: too many tokens for one call");
+    if (!x || !topk_idx || !topk_scores || !gate_w || !gate_s || !gate_b || !up_w || !up_s ||
+        !up_b || !down_w || !down_s || !down_b || !y || !workspace)
+        return fail(NQ_INVALID_INPUT, "nq_moe_switch: NULL pointer");
+    const size_t need = nq::moe_workspace_bytes(T, E, top_k, H, I);
+    if (workspace_bytes < need)
+        return fail(NQ_INVALID_INPUT, "nq_moe_switch: workspace too small: need " +
+                                          std::to_string(need) + " bytes");
+    if (!aligned16(x) || !aligned16(gate_w) || !aligned16(up_w) || !aligned16(down_w) ||
+        !aligned16(workspace))
+        return fail(NQ_INVALID_INPUT, "nq_moe_switch: tensors must be 16-byte aligned");
+    if (int rc = need_device("nq_moe_switch")) return rc;
+    return from_cuda(nq::launch_moe_switch(x, T, H, I, E, top_k, topk_idx, topk_scores, gate_w,
+                                           gate_s, gate_b, up_w, up_s, up_b, down_w, down_s,
+                                           down_b, bits, group_size, workspace, y,
+                                           static_cast<cudaStream_t>(stream)),
+                     "nq_moe_switch");
+}
+
+}  // extern "C"

@@ -1,0 +1,194 @@
+// cuda_backend.cpp -- CUDABackend, BackendFactory and the cuda_ops helpers.
+// Lifecycle mirrors MLXBackend (compute/src/compute/backends/mlx/mlx_backend.cpp:30-50):
+// initialize() selects the device (mx::set_default_device(gpu) there) and
+// creates the backend's stream; cleanup() releases it (mx::clear_cache there).
+#include "cuda_backend.h"
+
+#include <cuda_runtime.h>
+
+#include "nq.h"
+
+namespace compute {
+
+namespace {
+
+Error nq_error(int st, const std::string &what) {
+    ErrorCode c = ErrorCode::UnknownError;
+    switch (st) {
+        case NQ_INVALID_INPUT: c = ErrorCode::InvalidInput; break;
+        case NQ_INVALID_MODEL: c = ErrorCode::InvalidModel; break;
+        case NQ_BACKEND_NOT_AVAILABLE: c = ErrorCode::BackendNotAvailable; break;
+        case NQ_COMPUTE_ERROR: c = ErrorCode::ComputeError; break;
+        default: break;
+    }
+    return Error{c, what + ": " + nq_last_error()};
+}
+
+uint16_t *bf16p(const DeviceTensor &t) { return static_cast<uint16_t *>(t.data); }
+uint32_t *u32p(const DeviceTensor &t) { return static_cast<uint32_t *>(t.data); }
+
+}  // namespace
+
+// ------------------------------------------------------------ CUDABackend
+
+CUDABackend::CUDABackend(int device) : device_(device) {}
+
+CUDABackend::~CUDABackend() { cleanup(); }
+
+std::string CUDABackend::name() const { return "CUDA (NVIDIA B200, sm_100a)"; }
+
+bool CUDABackend::is_available() const {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    if (device_ < 0 || device_ >= n) return false;
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, device_) != cudaSuccess) return false;
+    return p.major == 10 && p.minor == 0;  // sm_100 (B200)
+}
+
+Result<void> CUDABackend::initialize() {
+    if (initialized_) return {};
+    if (!is_available())
+        return std::unexpected(Error{ErrorCode::BackendNotAvailable,
+                                     "CUDA backend needs an sm_100 (B200) device"});
+    if (cudaSetDevice(device_) != cudaSuccess)
+        return std::unexpected(Error{ErrorCode::ComputeError, "cudaSetDevice failed"});
+    cudaStream_t s = nullptr;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess)
+        return std::unexpected(Error{ErrorCode::ComputeError, "cudaStreamCreate failed"});
+    stream_ = s;
+    initialized_ = true;
+    return {};
+}
+
+void CUDABackend::cleanup() {
+    if (!initialized_) return;
+    cudaStreamSynchronize(static_cast<cudaStream_t>(stream_));
+    cudaStreamDestroy(static_cast<cudaStream_t>(stream_));
+    stream_ = nullptr;
+    initialized_ = false;
+}
+
+Result<void> CUDABackend::synchronize() const {
+    if (!initialized_) return std::unexpected(Error{ErrorCode::ComputeError, "not initialized"});
+    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream_));
+    if (e != cudaSuccess)
+        return std::unexpected(Error{ErrorCode::ComputeError, cudaGetErrorString(e)});
+    unsigned int err = 0;
+    if (nq_take_device_error(&err) != NQ_SUCCESS || err != 0)
+        return std::unexpected(Error{ErrorCode::ComputeError,
+                                     "kernel reported device error " + std::to_string(err)});
+    return {};
+}
+
+// --------------------------------------------------------- BackendFactory
+// Same shape as compute/src/compute/core/compute_backend.cpp:9-32, with the
+// CUDA case added; Auto picks CUDA when an sm_100 device is present.
+
+Result<std::unique_ptr<ComputeBackend>> BackendFactory::create(BackendType type) {
+    switch (type) {
+        case BackendType::Auto:
+        case BackendType::CUDA: {
+            auto be = std::make_unique<CUDABackend>(0);
+            if (!be->is_available())
+                return std::unexpected(Error{ErrorCode::BackendNotAvailable, "CUDA not available"});
+            auto r = be->initialize();
+            if (!r)
+                return std::unexpected(Error{ErrorCode::BackendNotAvailable,
+                                             "CUDA backend failed to initialize: " +
+                                                 r.error().message});
+            return std::unique_ptr<ComputeBackend>(std::move(be));
+        }
+        case BackendType::MLX:
+            return std::unexpected(Error{ErrorCode::BackendNotAvailable,
+                                         "MLX backend only available on Apple Silicon with MLX "
+                                         "enabled"});
+        default:
+            return std::unexpected(Error{ErrorCode::UnknownError, "Unknown backend type"});
+    }
+}
+
+std::vector<BackendType> BackendFactory::available_backends() {
+    std::vector<BackendType> v;
+    if (CUDABackend(0).is_available()) v.push_back(BackendType::CUDA);
+    return v;
+}
+
+BackendType BackendFactory::best_available_backend() {
+    auto v = available_backends();
+    return v.empty() ? BackendType::Auto : v[0];
+}
+
+// ----------------------------------------------------------------- ops
+
+namespace cuda_ops {
+
+int bits(const DeviceTensor &w, const DeviceTensor &s, int gs) {
+    return nq_bits_from_shapes(w.dim(-1), s.dim(-1), gs);
+}
+
+Result<void> lin(const DeviceTensor &x, const std::string &key, const WeightMap &wm, int gs,
+                 DeviceTensor &y, void *stream) {
+    auto wit = wm.find(key + ".weight");
+    if (wit == wm.end())
+        return std::unexpected(Error{ErrorCode::InvalidModel, "missing weight " + key + ".weight"});
+    const DeviceTensor &w = wit->second;
+    auto sit = wm.find(key + ".scales");
+    if (sit == wm.end())
+        return std::unexpected(Error{ErrorCode::InvalidModel,
+                                     key + ": unquantized (dense) weights are not served by the "
+                                           "quantized-matmul backend"});
+    const DeviceTensor &s = sit->second;
+    auto bit = wm.find(key + ".biases");
+    const DeviceTensor *b = bit == wm.end() ? nullptr : &bit->second;
+    const int nb = bits(w, s, gs);
+    const int64_t K = x.dim(-1);
+    const int64_t M = x.numel() / K;
+    const int64_t N = w.dim(0);
+    if (w.dim(-1) * 32 / nb != K)
+        return std::unexpected(Error{ErrorCode::InvalidInput, key + ": x/W inner dimension mismatch"});
+    if (y.numel() != M * N)
+        return std::unexpected(Error{ErrorCode::InvalidInput, key + ": output has the wrong size"});
+    const int st = nq_quantized_matmul(bf16p(x), M, u32p(w), bf16p(s), b ? bf16p(*b) : nullptr, N,
+                                       K, nb, gs, bf16p(y), stream);
+    if (st != NQ_SUCCESS) return std::unexpected(nq_error(st, "lin(" + key + ")"));
+    return {};
+}
+
+Result<void> dequantize(const DeviceTensor &w, const DeviceTensor &scales,
+                        const DeviceTensor &biases, int gs, int bits, DeviceTensor &out,
+                        void *stream) {
+    const int64_t rows = w.numel() / w.dim(-1);
+    const int64_t K = w.dim(-1) * 32 / bits;
+    if (out.numel() != rows * K)
+        return std::unexpected(Error{ErrorCode::InvalidInput, "dequantize: wrong output size"});
+    const int st = nq_dequantize(u32p(w), bf16p(scales), bf16p(biases), rows, K, bits, gs,
+                                 bf16p(out), stream);
+    if (st != NQ_SUCCESS) return std::unexpected(nq_error(st, "dequantize"));
+    return {};
+}
+
+Result<void> gather_qmm(const DeviceTensor &x, const DeviceTensor &w, const DeviceTensor &scales,
+                        const DeviceTensor &biases, const std::optional<DeviceTensor> &lhs,
+                        const DeviceTensor &rhs, int gs, int bits, DeviceTensor &out,
+                        void *stream) {
+    if (w.shape.size() != 3)
+        return std::unexpected(Error{ErrorCode::InvalidInput, "gather_qmm: w must be [E, N, K/pack]"});
+    const int64_t E = w.dim(0), N = w.dim(1), K = w.dim(2) * 32 / bits;
+    const int64_t M = x.shape.size() >= 2 ? x.dim(-2) : 1;
+    const int64_t xb = x.numel() / (M * K);
+    const int64_t n = rhs.numel();
+    if (out.numel() != n * M * N)
+        return std::unexpected(Error{ErrorCode::InvalidInput, "gather_qmm: wrong output size"});
+    const int st = nq_gather_qmm(bf16p(x), xb, M, lhs ? static_cast<int32_t *>(lhs->data) : nullptr,
+                                 static_cast<int32_t *>(rhs.data), n, u32p(w), bf16p(scales),
+                                 bf16p(biases), E, N, K, bits, gs, bf16p(out), stream);
+    if (st != NQ_SUCCESS) return std::unexpected(nq_error(st, "gather_qmm"));
+    return {};
+}
+
+}  // namespace cuda_ops
+}  // namespace compute

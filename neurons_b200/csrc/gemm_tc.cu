@@ -1,0 +1,361 @@
+// gemm_tc.cu -- prefill quantized GEMM on the 5th-generation tensor cores.
+//
+//   y[m, n] = sum_k x[m, k] * w_hat[n, k]   (w_hat = MLX dequantized bf16)
+//
+// Tile: 128 weight rows (the UMMA M side) x BM tokens (the UMMA N side) per
+// CTA, K consumed 64 codes per pipeline stage.  Roles (10 warps):
+//   warp 8      TMA producer: per stage one box of activations
+//               [BM rows x 64 bf16] (128-byte swizzle, the canonical K-major
+//               UMMA layout) and one box of packed codes [128 rows x 32 or
+//               64 bytes] (32/64-byte swizzle so that the dequant reads are
+//               bank-conflict free);
+//   warps 0..7  dequantizers: lane r of warp w owns weight row 32*(w%4)+r and
+//               half w/4 of the stage's 64 codes; the codes become exact MLX
+//               bf16 values in registers and go straight into tensor memory
+//               with tcgen05.st -- the weights are the MMA's A operand *in
+//               TMEM*, so they never round-trip through shared memory;
+//   warp 9      TMEM allocator and the single MMA-issuing thread:
+//               tcgen05.mma.cta_group::1.kind::f16, A from TMEM, B (tokens)
+//               from shared memory, fp32 accumulator (128 lanes x BM columns)
+//               in TMEM; tcgen05.commit releases stages back to the producer.
+//   Epilogue: warps 0..7 read the accumulator with tcgen05.ld (lane = weight
+//   row, column = token) and store bf16 y.
+// Every mbarrier wait is bounded; on a timeout the CTA raises the device
+// error word, stops issuing work, lets in-flight operations drain and frees
+// its TMEM before returning.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "nq_common.cuh"
+#include "nq_internal.h"
+
+namespace nq {
+namespace {
+
+constexpr int kBlockW = 128;     // weight rows per CTA (UMMA M)
+constexpr int kBlockK = 64;      // codes per stage
+constexpr int kDequantWarps = 8;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 320;
+
+template <int BITS, int BM>
+struct TcCfg {
+    static constexpr int kXStageBytes = BM * kBlockK * 2;             // bf16 tokens
+    static constexpr int kWStageBytes = kBlockW * kBlockK * BITS / 8;  // packed codes
+    static constexpr int kStageBytes = kXStageBytes + kWStageBytes;
+    static constexpr int kStages = (BM == 256) ? (BITS == 4 ? 6 : 5) : (BM == 128 ? 8 : 10);
+    static constexpr int kACol0 = BM;                                  // first A-stage column
+    static constexpr int kTmemCols = 512;
+    static_assert(kACol0 + kStages * 32 <= kTmemCols, "TMEM budget");
+    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+    static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+struct TcParams {
+    int64_t M, N, K, x_ld, y_ld;
+    int gs;
+    int num_kb;
+    const uint16_t *s, *b;
+    uint16_t *y;
+    unsigned int *err;
+};
+
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                              unsigned int *err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_timer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            *abort = 1;
+            atomicOr(err, kErrWaitTimeout);
+            return false;
+        }
+    }
+}
+
+template <int BITS, int BM>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_qgemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                    const __grid_constant__ CUtensorMap tmap_w, const TcParams prm) {
+    using Cfg = TcCfg<BITS, BM>;
+    constexpr int S = Cfg::kStages;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                ~uintptr_t(1023));
+    uint8_t *xs = smem;                               // S x [BM][128 B]
+    uint8_t *ws = smem + S * Cfg::kXStageBytes;       // S x [128][32|64 B]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ws + S * Cfg::kWStageBytes);
+    uint64_t *full = bars;            // TMA landed (x + w)
+    uint64_t *empty = bars + S;       // stage free: MMA done (1) + dequant read (8)
+    uint64_t *afull = bars + 2 * S;   // A written to TMEM (8 warps)
+    uint64_t *accfull = bars + 3 * S; // accumulator complete
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * S + 1);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t n0 = (int64_t)blockIdx.x * kBlockW;
+    const int64_t m0 = (int64_t)blockIdx.y * BM;
+    const int num_kb = prm.num_kb;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1 + kDequantWarps);
+            mbar_init(&afull[s], kDequantWarps);
+        }
+        mbar_init(accfull, 1);
+        *abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == kProducerWarp && lane == 0) {
+        prefetch_tmap(&tmap_x);
+        prefetch_tmap(&tmap_w);
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(tmem_holder, Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            const uint32_t bytes = Cfg::kXStageBytes + Cfg::kWStageBytes;
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % S;
+                const uint32_t ph = (uint32_t)(kb / S) & 1u;
+                if (!wait_or_abort(&empty[s], ph ^ 1u, abort, prm.err)) break;
+                mbar_expect_tx(&full[s], bytes);
+                tma_load_2d(xs + s * Cfg::kXStageBytes, &tmap_x, &full[s], kb * kBlockK, (int32_t)m0);
+                tma_load_2d(ws + s * Cfg::kWStageBytes, &tmap_w, &full[s],
+                            kb * (kBlockK * BITS / 32), (int32_t)n0);
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16_f32(kBlockW, BM);
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % S;
+                const uint32_t ph = (uint32_t)(kb / S) & 1u;
+                if (!wait_or_abort(&full[s], ph, abort, prm.err)) break;
+                if (!wait_or_abort(&afull[s], ph, abort, prm.err)) break;
+                tc_fence_after();
+                const uint64_t bdesc = smem_desc_k_sw128(smem_u32(xs + s * Cfg::kXStageBytes));
+#pragma unroll
+                for (int j = 0; j < kBlockK / 16; ++j) {
+                    const uint32_t a_tmem = tmem_base + (uint32_t)(Cfg::kACol0 + s * 32 + j * 8);
+                    // +32 bytes per 16 bf16 of K inside the 128-byte swizzled row
+                    umma_ts(tmem_base, a_tmem, bdesc + (uint64_t)(j * 2), idesc,
+                            (kb > 0 || j > 0) ? 1u : 0u);
+                }
+                umma_commit(&empty[s]);
+            }
+            umma_commit(accfull);
+        }
+    } else {
+        // ------------------------------------------------ dequantizers
+        const int q = warp & 3;          // TMEM lane quadrant
+        const int h = warp >> 2;         // which 32 codes of the stage
+        const int r = q * 32 + lane;     // weight row inside the tile
+        const int64_t n = n0 + r;
+        const bool row_ok = n < prm.N;
+        const int64_t G = prm.K / prm.gs;
+        const uint16_t *srow = prm.s + (row_ok ? n : 0) * G;
+        const uint16_t *brow = prm.b + (row_ok ? n : 0) * G;
+        auto load_sb = [&](int kb, uint16_t &sv, uint16_t &bv) {
+            const int64_t k = (int64_t)kb * kBlockK + 32 * h;
+            sv = 0;
+            bv = 0;
+            if (row_ok && kb < num_kb && k < prm.K) {
+                sv = srow[k / prm.gs];
+                bv = brow[k / prm.gs];
+            }
+        };
+        uint16_t s_cur, b_cur, s_nxt, b_nxt;
+        load_sb(0, s_cur, b_cur);
+        load_sb(1, s_nxt, b_nxt);
+        const uint32_t t_lane = (uint32_t)(q * 32) << 16;
+        for (int kb = 0; kb < num_kb; ++kb) {
+            const int s = kb % S;
+            const uint32_t ph = (uint32_t)(kb / S) & 1u;
+            if (!wait_or_abort(&full[s], ph, abort, prm.err)) break;
+            tc_fence_after();
+            uint32_t out[16];
+            const uint8_t *wst = ws + s * Cfg::kWStageBytes;
+            if constexpr (BITS == 4) {
+                // row r: 32 bytes; chunk h, 32-byte swizzle: chunk ^= (r >> 2) & 1
+                const uint4 v = *reinterpret_cast<const uint4 *>(
+                    wst + r * 32 + 16 * (h ^ ((r >> 2) & 1)));
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+                const Dq4 d = make_dq4(s_cur, b_cur);
+                const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t d0 = dq4_pair(q4_pair_biased(words[i], 0), d);  // (w0, w4)
+                    const uint32_t d1 = dq4_pair(q4_pair_biased(words[i], 1), d);  // (w1, w5)
+                    const uint32_t d2 = dq4_pair(q4_pair_biased(words[i], 2), d);  // (w2, w6)
+                    const uint32_t d3 = dq4_pair(q4_pair_biased(words[i], 3), d);  // (w3, w7)
+                    out[4 * i + 0] = prmt(d0, d1, 0x5410u);  // (w0, w1)
+                    out[4 * i + 1] = prmt(d2, d3, 0x5410u);  // (w2, w3)
+                    out[4 * i + 2] = prmt(d0, d1, 0x7632u);  // (w4, w5)
+                    out[4 * i + 3] = prmt(d2, d3, 0x7632u);  // (w6, w7)
+                }
+            } else {
+                // row r: 64 bytes; chunks 2h, 2h+1, 64-byte swizzle: chunk ^= (r >> 1) & 3
+                const int x = (r >> 1) & 3;
+                const uint4 v0 = *reinterpret_cast<const uint4 *>(wst + r * 64 + 16 * ((2 * h) ^ x));
+                const uint4 v1 =
+                    *reinterpret_cast<const uint4 *>(wst + r * 64 + 16 * ((2 * h + 1) ^ x));
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+                const Dq8 d = make_dq8(s_cur, b_cur);
+                const uint32_t words[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    out[2 * i + 0] = dq8_pair(words[i], 0, 1, d);
+                    out[2 * i + 1] = dq8_pair(words[i], 2, 3, d);
+                }
+            }
+            tmem_st_32x32b_x16(tmem_base + t_lane + (uint32_t)(Cfg::kACol0 + s * 32 + 16 * h), out);
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&afull[s]);
+            s_cur = s_nxt;
+            b_cur = b_nxt;
+            load_sb(kb + 2, s_nxt, b_nxt);
+        }
+        // ------------------------------------------------ epilogue
+        if (wait_or_abort(accfull, 0, abort, prm.err) && !*abort) {
+            tc_fence_after();
+            const int64_t nrow = n0 + r;
+            for (int c0 = h * (BM / 2); c0 < (h + 1) * (BM / 2); c0 += 32) {
+                uint32_t acc[32];
+                tmem_ld_32x32b_x32(tmem_base + t_lane + (uint32_t)c0, acc);
+                tmem_ld_wait();
+                if (nrow < prm.N) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int64_t m = m0 + c0 + j;
+                        if (m < prm.M)
+                            prm.y[m * prm.y_ld + nrow] = f32_to_bf16(__uint_as_float(acc[j]));
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        if (*abort) {
+            // let any tensor-core work still in flight finish before freeing TMEM
+            const unsigned long long t0 = global_timer_ns();
+            while (global_timer_ns() - t0 < 10000000ull) {
+            }
+        }
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------- host side
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+bool make_map_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t inner,
+                 uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle sw) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BITS, int BM>
+cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
+    using Cfg = TcCfg<BITS, BM>;
+    CUtensorMap mx, mw;
+    const uint64_t Kw = (uint64_t)a.K * BITS / 32;
+    if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M,
+                     (uint64_t)a.x_ld * 2, kBlockK, BM, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    if (!make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w, Kw, (uint64_t)a.N, Kw * 4,
+                     kBlockK * BITS / 32, kBlockW,
+                     BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
+        return cudaErrorInvalidValue;
+    TcParams prm;
+    prm.M = a.M;
+    prm.N = a.N;
+    prm.K = a.K;
+    prm.x_ld = a.x_ld;
+    prm.y_ld = a.y_ld;
+    prm.gs = a.gs;
+    prm.num_kb = (int)((a.K + kBlockK - 1) / kBlockK);
+    prm.s = a.s;
+    prm.b = a.b;
+    prm.y = a.y;
+    prm.err = device_error_word();
+    auto kern = tc_qgemm_kernel<BITS, BM>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    dim3 grid((unsigned)((a.N + kBlockW - 1) / kBlockW), (unsigned)((a.M + BM - 1) / BM), 1);
+    kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(mx, mw, prm);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool tc_gemm_supported(const TcGemmArgs &a) {
+    if (a.M <= 0 || a.N <= 0 || a.K <= 0) return false;
+    if (a.bits != 4 && a.bits != 8) return false;
+    // TMA: 16-byte aligned bases and row strides
+    if ((reinterpret_cast<uintptr_t>(a.x) & 15) || (reinterpret_cast<uintptr_t>(a.w) & 15))
+        return false;
+    if ((a.x_ld * 2) % 16 || (a.K * a.bits / 8) % 16) return false;
+    if (a.M > ((int64_t)1 << 31) - 1 || a.N > ((int64_t)1 << 31) - 1) return false;
+    return encode_fn() != nullptr;
+}
+
+cudaError_t launch_tc_gemm(const TcGemmArgs &a, cudaStream_t stream) {
+    if (!tc_gemm_supported(a)) return cudaErrorNotSupported;
+    if (a.M <= 64) return a.bits == 4 ? launch_bm<4, 64>(a, stream) : launch_bm<8, 64>(a, stream);
+    if (a.M <= 128)
+        return a.bits == 4 ? launch_bm<4, 128>(a, stream) : launch_bm<8, 128>(a, stream);
+    return a.bits == 4 ? launch_bm<4, 256>(a, stream) : launch_bm<8, 256>(a, stream);
+}
+
+}  // namespace nq

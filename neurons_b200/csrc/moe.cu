@@ -1,0 +1,272 @@
+// moe.cu -- Qwen3-MoE switch step on B200: router top-k, expert grouping,
+// SwiGLU gate/up + down projections through the quantized matmul kernels,
+// and the score-weighted combine.
+//
+// Restates compute/src/compute/model/qwen3_transformer_moe_model_mlx.cpp:29-79
+// (router :36-48, gather_qmm :69-74, SwiGLU :71, weighted sum :77-78), batched
+// over T tokens instead of the per-token loop at :479-486.
+#include <algorithm>
+
+#include "nq_common.cuh"
+#include "nq_internal.h"
+
+namespace nq {
+namespace {
+
+constexpr int kMaxTopK = 32;
+
+// One warp per token.  Selection compares the logits (softmax is monotonic);
+// equal logits prefer the lower expert index; output in descending order.
+__global__ void route_kernel(const uint16_t *__restrict__ logits, int64_t T, int E, int top_k,
+                             int32_t *__restrict__ idx, float *__restrict__ scores) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= T) return;
+    const uint16_t *l = logits + t * E;
+    float mx = -INFINITY;
+    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, bf16_to_f32(l[e]));
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.0f;
+    for (int e = lane; e < E; e += 32) sum += expf(bf16_to_f32(l[e]) - mx);
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    // experts already selected, as a bitmask over this lane's experts
+    // (E <= 1024 -> at most 32 per lane)
+    uint32_t taken = 0;
+    int sel[kMaxTopK];
+    float psel[kMaxTopK];
+    float psum = 0.0f;
+    for (int j = 0; j < top_k; ++j) {
+        float bv = -INFINITY;
+        int be = 0x7fffffff;
+        for (int i = 0, e = lane; e < E; ++i, e += 32) {
+            if (taken & (1u << i)) continue;
+            const float v = bf16_to_f32(l[e]);
+            if (be == 0x7fffffff || v > bv || (v == bv && e < be)) {
+                bv = v;
+                be = e;
+            }
+        }
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+            if (oe != 0x7fffffff && (be == 0x7fffffff || ov > bv || (ov == bv && oe < be))) {
+                bv = ov;
+                be = oe;
+            }
+        }
+        sel[j] = be;
+        if ((be & 31) == lane) taken |= 1u << (be >> 5);
+        psel[j] = expf(bv - mx) / sum;
+        psum += psel[j];
+    }
+    if (lane == 0) {
+        for (int j = 0; j < top_k; ++j) {
+            idx[t * top_k + j] = sel[j];
+            scores[t * top_k + j] = psel[j] / psum;
+        }
+    }
+}
+
+// counts[e] = number of (token, slot) pairs routed to expert e
+__global__ void count_kernel(const int32_t *__restrict__ idx, int64_t pairs, int E,
+                             int32_t *__restrict__ counts, unsigned int *err) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= pairs) return;
+    const int e = idx[i];
+    if (e < 0 || e >= E) {
+        atomicOr(err, kErrBadIndex);
+        return;
+    }
+    atomicAdd(&counts[e], 1);
+}
+
+// exclusive prefix sum over experts (single block, E <= 1024); clears cursors
+__global__ void scan_kernel(const int32_t *__restrict__ counts, int E, int32_t *__restrict__ offsets,
+                            int32_t *__restrict__ cursor) {
+    __shared__ int32_t buf[1024];
+    const int t = threadIdx.x;
+    buf[t] = t < E ? counts[t] : 0;
+    __syncthreads();
+    for (int o = 1; o < 1024; o <<= 1) {
+        const int32_t v = t >= o ? buf[t - o] : 0;
+        __syncthreads();
+        buf[t] += v;
+        __syncthreads();
+    }
+    if (t < E) {
+        offsets[t] = buf[t] - counts[t];
+        cursor[t] = 0;
+    }
+}
+
+// place every pair at offsets[e] + rank; the rank order inside an expert does
+// not change any result (each output row depends on its own input row only)
+__global__ void fill_kernel(const int32_t *__restrict__ idx, int64_t pairs, int top_k, int E,
+                            const int32_t *__restrict__ offsets, int32_t *__restrict__ cursor,
+                            int32_t *__restrict__ pos_token, int32_t *__restrict__ pos_pair) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= pairs) return;
+    const int e = idx[i];
+    if (e < 0 || e >= E) return;
+    const int32_t pos = offsets[e] + atomicAdd(&cursor[e], 1);
+    pos_token[pos] = (int32_t)(i / top_k);
+    pos_pair[pos] = (int32_t)i;
+}
+
+__global__ void pair_token_kernel(int64_t pairs, int top_k, int32_t *__restrict__ tok) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < pairs) tok[i] = (int32_t)(i / top_k);
+}
+
+// y[t, n] = bf16( sum_j bf16(score[t, j]) * d[t*k + j, n] ), slot order 0..k-1
+__global__ void combine_kernel(const float *__restrict__ d, const float *__restrict__ scores,
+                               int64_t T, int64_t H, int top_k, uint16_t *__restrict__ y) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over T * H / 4
+    if (i >= T * (H / 4)) return;
+    const int64_t t = i / (H / 4);
+    const int64_t n = (i % (H / 4)) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < top_k; ++j) {
+        const float sc = bf16_to_f32(f32_to_bf16(scores[t * top_k + j]));
+        const float4 v = *reinterpret_cast<const float4 *>(d + (t * top_k + j) * H + n);
+        acc.x = __fmaf_rn(sc, v.x, acc.x);
+        acc.y = __fmaf_rn(sc, v.y, acc.y);
+        acc.z = __fmaf_rn(sc, v.z, acc.z);
+        acc.w = __fmaf_rn(sc, v.w, acc.w);
+    }
+    uint2 out;
+    out.x = (uint32_t)f32_to_bf16(acc.x) | ((uint32_t)f32_to_bf16(acc.y) << 16);
+    out.y = (uint32_t)f32_to_bf16(acc.z) | ((uint32_t)f32_to_bf16(acc.w) << 16);
+    *reinterpret_cast<uint2 *>(y + t * H + n) = out;
+}
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Workspace layout (each region 256-byte aligned), P = T * top_k pairs:
+//   counts[E], offsets[E], cursor[E], pos_token[P], pos_pair[P]   int32
+//   h[P, I]  bf16      (SwiGLU activations, grouped or pair order)
+//   d[P, H]  fp32      (down-projection sums, pair order)
+struct MoeWorkspace {
+    int32_t *counts, *offsets, *cursor, *pos_token, *pos_pair;
+    uint16_t *h;
+    float *d;
+    size_t bytes;
+};
+
+MoeWorkspace carve(void *base, int64_t T, int64_t E, int64_t top_k, int64_t H, int64_t I) {
+    MoeWorkspace w;
+    const int64_t P = T * top_k;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        char *p = static_cast<char *>(base) + off;
+        off += align256(bytes);
+        return p;
+    };
+    w.counts = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * E));
+    w.offsets = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * E));
+    w.cursor = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * E));
+    w.pos_token = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * P));
+    w.pos_pair = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * P));
+    w.h = reinterpret_cast<uint16_t *>(take(sizeof(uint16_t) * P * I));
+    w.d = reinterpret_cast<float *>(take(sizeof(float) * P * H));
+    w.bytes = off;
+    return w;
+}
+
+}  // namespace
+
+cudaError_t launch_moe_route(const uint16_t *logits, int64_t T, int64_t E, int64_t top_k,
+                             int32_t *idx, float *scores, cudaStream_t stream) {
+    if (T == 0) return cudaSuccess;
+    const int warps = 8;
+    route_kernel<<<(unsigned)((T + warps - 1) / warps), warps * 32, 0, stream>>>(
+        logits, T, (int)E, (int)top_k, idx, scores);
+    return cudaGetLastError();
+}
+
+size_t moe_workspace_bytes(int64_t T, int64_t E, int64_t top_k, int64_t H, int64_t I) {
+    return carve(nullptr, T, E, top_k, H, I).bytes;
+}
+
+// Pairs routed to one expert are processed together ("grouped" mode) once
+// there are more pairs than experts; below that every pair is its own
+// problem ("pair" mode: no grouping kernels, one weight stream per pair).
+cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I, int64_t E,
+                              int64_t top_k, const int32_t *idx, const float *scores,
+                              const uint32_t *gw, const uint16_t *gs_, const uint16_t *gb,
+                              const uint32_t *uw, const uint16_t *us, const uint16_t *ub,
+                              const uint32_t *dw, const uint16_t *ds, const uint16_t *db, int bits,
+                              int gsz, void *workspace, uint16_t *y, cudaStream_t stream) {
+    if (T == 0) return cudaSuccess;
+    const int64_t P = T * top_k;
+    MoeWorkspace ws = carve(workspace, T, E, top_k, H, I);
+    unsigned int *err = device_error_word();
+    const int thr = 256;
+    const unsigned pblocks = (unsigned)((P + thr - 1) / thr);
+    const bool grouped = P > E;
+    cudaError_t e;
+
+    GemvProblems up;
+    up.w = gw; up.s = gs_; up.b = gb;
+    up.w2 = uw; up.s2 = us; up.b2 = ub;
+    up.N = I; up.K = H; up.bits = bits; up.gs = gsz;
+    up.x = x; up.x_ld = H;
+    up.E = (int)E;
+    up.y = ws.h; up.y_ld = I;
+    up.swiglu = 1;
+
+    GemvProblems dn;
+    dn.w = dw; dn.s = ds; dn.b = db;
+    dn.N = H; dn.K = I; dn.bits = bits; dn.gs = gsz;
+    dn.x = ws.h; dn.x_ld = I;
+    dn.E = (int)E;
+    dn.y = ws.d; dn.y_ld = H;
+    dn.out_f32 = 1;
+
+    if (grouped) {
+        if ((e = cudaMemsetAsync(ws.counts, 0, sizeof(int32_t) * E, stream)) != cudaSuccess)
+            return e;
+        count_kernel<<<pblocks, thr, 0, stream>>>(idx, P, (int)E, ws.counts, err);
+        scan_kernel<<<1, 1024, 0, stream>>>(ws.counts, (int)E, ws.offsets, ws.cursor);
+        fill_kernel<<<pblocks, thr, 0, stream>>>(idx, P, (int)top_k, (int)E, ws.offsets, ws.cursor,
+                                                  ws.pos_token, ws.pos_pair);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        // gate/up: problem = expert, its tokens gathered from x, h rows in grouped order
+        up.P = (int)E;
+        up.expert_is_p = true;
+        up.m_count = ws.counts;
+        up.m_offset = ws.offsets;
+        up.x_rows = ws.pos_token;
+        up.max_m = (int)std::min<int64_t>(P, 32);
+        // down: problem = expert, rows of h in grouped order, d rows by pair id
+        dn.P = (int)E;
+        dn.expert_is_p = true;
+        dn.m_count = ws.counts;
+        dn.m_offset = ws.offsets;
+        dn.x_from_offset = true;
+        dn.y_rows = ws.pos_pair;
+        dn.max_m = up.max_m;
+    } else {
+        pair_token_kernel<<<pblocks, thr, 0, stream>>>(P, (int)top_k, ws.pos_token);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        up.P = (int)P;
+        up.M = 1;
+        up.expert = idx;
+        up.lhs = ws.pos_token;
+        up.x_batch = (int)T;
+        up.max_m = 1;
+        dn.P = (int)P;
+        dn.M = 1;
+        dn.expert = idx;
+        dn.x_batch = (int)P;
+        dn.max_m = 1;
+    }
+    if ((e = launch_gemv(up, stream)) != cudaSuccess) return e;
+    if ((e = launch_gemv(dn, stream)) != cudaSuccess) return e;
+    const int64_t n4 = T * (H / 4);
+    combine_kernel<<<(unsigned)((n4 + thr - 1) / thr), thr, 0, stream>>>(ws.d, scores, T, H,
+                                                                          (int)top_k, y);
+    return cudaGetLastError();
+}
+
+}  // namespace nq

@@ -1,0 +1,94 @@
+// nq_internal.h -- host-side interfaces between the C ABI (abi.cu) and the
+// kernel launchers.  Not part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace nq {
+
+// Thread-local last-error message behind nq_last_error().
+void set_error(const std::string &msg);
+const char *last_error();
+
+// Device error word of the current device (a static __device__ variable;
+// its address is looked up once per device).
+unsigned int *device_error_word();
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// A skinny (<= 32 tokens per pass) quantized matmul problem set.
+// Problem p multiplies tokens of x against expert e_p of a stacked weight
+// tensor; see gemv.cu for the addressing rules.
+struct GemvProblems {
+    const uint32_t *w = nullptr;   // [E, N, K*bits/32]
+    const uint16_t *s = nullptr;   // [E, N, K/gs]
+    const uint16_t *b = nullptr;
+    const uint32_t *w2 = nullptr;  // second weight set (gate/up pair), same shape
+    const uint16_t *s2 = nullptr;
+    const uint16_t *b2 = nullptr;
+    int64_t N = 0, K = 0;
+    int bits = 4, gs = 64;
+    const uint16_t *x = nullptr;
+    int64_t x_ld = 0;                  // elements between x rows
+    int P = 1;                         // number of problems
+    int M = 1;                         // tokens per problem when m_count == nullptr
+    int E = 1;                         // number of experts (index range check)
+    const int32_t *expert = nullptr;   // [P] expert of problem p; nullptr -> 0
+    bool expert_is_p = false;          // expert of problem p is p
+    const int32_t *m_count = nullptr;  // [P] tokens of problem p
+    const int32_t *m_offset = nullptr; // [P] first entry of problem p in the row lists
+    const int32_t *x_rows = nullptr;   // x row of (p, m); nullptr -> see x_from_offset
+    bool x_from_offset = false;        // x row of (p, m) = off(p) + m (else xi(p)*M + m)
+    const int32_t *lhs = nullptr;      // [P] x batch of problem p (gather_qmm lhs)
+    int x_batch = 1;
+    void *y = nullptr;
+    int64_t y_ld = 0;                  // elements between y rows
+    const int32_t *y_rows = nullptr;   // y row of (p, m); nullptr -> off(p) + m,
+                                       // off(p) = m_offset[p] or p*M
+    int out_f32 = 0;                   // 1: fp32 output, 0: bf16 output
+    int swiglu = 0;                    // 1: y = bf16(silu(x.w^T) * (x.w2^T))
+    int max_m = 1;                     // upper bound of tokens per problem
+};
+
+cudaError_t launch_gemv(const GemvProblems &p, cudaStream_t stream);
+
+// Dense path for larger M: TMA + tcgen05 GEMM with in-TMEM dequant.
+struct TcGemmArgs {
+    const uint16_t *x = nullptr;   // [M, K] bf16 (row stride x_ld)
+    int64_t x_ld = 0;
+    int64_t M = 0;
+    const uint32_t *w = nullptr;   // [N, K*bits/32]
+    const uint16_t *s = nullptr;
+    const uint16_t *b = nullptr;
+    int64_t N = 0, K = 0;
+    int bits = 4, gs = 64;
+    uint16_t *y = nullptr;         // [M, N] bf16 (row stride y_ld)
+    int64_t y_ld = 0;
+};
+
+bool tc_gemm_supported(const TcGemmArgs &a);
+cudaError_t launch_tc_gemm(const TcGemmArgs &a, cudaStream_t stream);
+
+cudaError_t launch_quantize(const void *w, int w_dtype, int64_t rows, int64_t K, int bits,
+                            int gs, int scheme, uint32_t *wq, uint16_t *s, uint16_t *b,
+                            cudaStream_t stream);
+cudaError_t launch_dequantize(const uint32_t *wq, const uint16_t *s, const uint16_t *b,
+                              int64_t rows, int64_t K, int bits, int gs, uint16_t *out,
+                              cudaStream_t stream);
+
+size_t moe_workspace_bytes(int64_t T, int64_t E, int64_t top_k, int64_t H, int64_t I);
+cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I, int64_t E,
+                              int64_t top_k, const int32_t *idx, const float *scores,
+                              const uint32_t *gw, const uint16_t *gs_, const uint16_t *gb,
+                              const uint32_t *uw, const uint16_t *us, const uint16_t *ub,
+                              const uint32_t *dw, const uint16_t *ds, const uint16_t *db, int bits,
+                              int gsz, void *workspace, uint16_t *y, cudaStream_t stream);
+
+cudaError_t launch_moe_route(const uint16_t *logits, int64_t T, int64_t E, int64_t top_k,
+                             int32_t *idx, float *scores, cudaStream_t stream);
+
+}  // namespace nq

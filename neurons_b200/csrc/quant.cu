@@ -1,0 +1,191 @@
+// quant.cu -- MLX-affine quantize/pack and dequantize kernels, sm_100a.
+//
+// Both are HBM-bound streaming kernels: every thread owns 16 contiguous
+// bytes of the narrower side (8 input values for quantize, 4 packed words for
+// dequantize), loads and stores are 128-bit and coalesced across the warp,
+// and a quantization group (32/64/128 values) is spread over 4/8/16
+// consecutive lanes that reduce min/max with shuffles.
+//
+// Arithmetic is written with explicit round-to-nearest intrinsics so that the
+// compiler cannot contract or reassociate it: the codes, scales and biases
+// (quantize) and the dequantized bf16 values (dequantize) are bit-identical
+// to MLX's CPU semantics as restated by the oracle.
+#include "nq_common.cuh"
+#include "nq_internal.h"
+
+namespace nq {
+namespace {
+
+// Quantize: one thread per 8 consecutive values along K.
+template <int BITS, bool IN_BF16>
+__global__ void __launch_bounds__(256) quantize_kernel(const void *__restrict__ w, int64_t rows,
+                                                       int64_t K, int gs, int scheme,
+                                                       uint32_t *__restrict__ wq,
+                                                       uint16_t *__restrict__ scales,
+                                                       uint16_t *__restrict__ biases) {
+    const int64_t chunks_per_row = K / 8;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t total = rows * chunks_per_row;
+    // Lanes of a group are consecutive and a group never straddles a row, so
+    // out-of-range lanes form whole groups: they compute on a valid address
+    // and do not store.
+    const bool active = t < total;
+    const int64_t tt = active ? t : total - 1;
+    const int64_t row = tt / chunks_per_row;
+    const int64_t chunk = tt % chunks_per_row;
+
+    float v[8];
+    if (IN_BF16) {
+        const uint4 raw = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(w) +
+                                                            row * K + chunk * 8);
+        const uint32_t r[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            v[2 * i] = __uint_as_float(r[i] << 16);
+            v[2 * i + 1] = __uint_as_float(r[i] & 0xFFFF0000u);
+        }
+    } else {
+        const float4 *src = reinterpret_cast<const float4 *>(static_cast<const float *>(w) +
+                                                             row * K + chunk * 8);
+        const float4 a = src[0], b = src[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+    float w_max = v[0], w_min = v[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) {
+        w_max = fmaxf(w_max, v[i]);
+        w_min = fminf(w_min, v[i]);
+    }
+    const int lanes = gs / 8;  // 4, 8 or 16
+    for (int o = 1; o < lanes; o <<= 1) {
+        w_max = fmaxf(w_max, __shfl_xor_sync(0xffffffffu, w_max, o));
+        w_min = fminf(w_min, __shfl_xor_sync(0xffffffffu, w_min, o));
+    }
+    const float n_bins = (float)((1 << BITS) - 1);
+    float scale, bias;
+    if (scheme == 0) {
+        const float eps = 1e-7f;
+        const bool mask = fabsf(w_min) > fabsf(w_max);
+        scale = fmaxf(__fdiv_rn(__fsub_rn(w_max, w_min), n_bins), eps);
+        scale = mask ? scale : -scale;
+        const float edge = mask ? w_min : w_max;
+        const float q0 = rintf(__fdiv_rn(edge, scale));
+        bias = 0.0f;
+        if (q0 != 0.0f) {
+            scale = __fdiv_rn(edge, q0);
+            bias = edge;
+        }
+    } else {
+        scale = __fdiv_rn(__fsub_rn(w_max, w_min), n_bins);
+        bias = w_min;
+    }
+    uint32_t q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float qq = 0.0f;
+        if (scale != 0.0f) {
+            qq = rintf(__fdiv_rn(__fsub_rn(v[i], bias), scale));
+            qq = fminf(fmaxf(qq, 0.0f), n_bins);
+        }
+        q[i] = (uint32_t)qq;
+    }
+    if (!active) return;
+    if (BITS == 4) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) word |= q[i] << (4 * i);
+        wq[row * (K / 8) + chunk] = word;
+    } else {
+        const uint32_t w0 = q[0] | (q[1] << 8) | (q[2] << 16) | (q[3] << 24);
+        const uint32_t w1 = q[4] | (q[5] << 8) | (q[6] << 16) | (q[7] << 24);
+        *reinterpret_cast<uint2 *>(wq + row * (K / 4) + chunk * 2) = make_uint2(w0, w1);
+    }
+    if ((chunk % lanes) == 0) {
+        const int64_t gidx = row * (K / gs) + chunk / lanes;
+        scales[gidx] = f32_to_bf16(scale);
+        biases[gidx] = f32_to_bf16(bias);
+    }
+}
+
+// MLX CPU dequantize of one code: bf16(bf16(s*q) + b), each step one rounding.
+__device__ __forceinline__ uint16_t dq_one(float s, float b, uint32_t q) {
+    const float p = bf16_to_f32(f32_to_bf16(__fmul_rn(s, (float)q)));
+    return f32_to_bf16(__fadd_rn(p, b));
+}
+
+// Dequantize: one thread per 16 bytes of packed words (32 codes at 4 bits,
+// 16 codes at 8 bits); output 64 or 32 contiguous bytes.
+template <int BITS>
+__global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t *__restrict__ wq,
+                                                         const uint16_t *__restrict__ scales,
+                                                         const uint16_t *__restrict__ biases,
+                                                         int64_t rows, int64_t K, int gs,
+                                                         uint16_t *__restrict__ out) {
+    constexpr int kCodes = 4 * 32 / BITS;  // codes per thread (4 words)
+    const int64_t Kw = K * BITS / 32;
+    const int64_t vec_per_row = Kw / 4;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= rows * vec_per_row) return;
+    const int64_t row = t / vec_per_row;
+    const int64_t vec = t % vec_per_row;
+    const uint4 raw = *reinterpret_cast<const uint4 *>(wq + row * Kw + vec * 4);
+    const int64_t k0 = vec * kCodes;
+    const int64_t gidx = row * (K / gs) + k0 / gs;
+    const float s = bf16_to_f32(scales[gidx]);
+    const float b = bf16_to_f32(biases[gidx]);
+    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+    uint32_t outw[kCodes / 2];
+#pragma unroll
+    for (int i = 0; i < kCodes / 2; ++i) {
+        constexpr int per = 32 / BITS;
+        constexpr uint32_t mask = (1u << BITS) - 1u;
+        const int c0 = 2 * i, c1 = 2 * i + 1;
+        const uint32_t q0 = (words[c0 / per] >> (BITS * (c0 % per))) & mask;
+        const uint32_t q1 = (words[c1 / per] >> (BITS * (c1 % per))) & mask;
+        outw[i] = (uint32_t)dq_one(s, b, q0) | ((uint32_t)dq_one(s, b, q1) << 16);
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(out + row * K + k0);
+#pragma unroll
+    for (int i = 0; i < kCodes / 8; ++i)
+        dst[i] = make_uint4(outw[4 * i], outw[4 * i + 1], outw[4 * i + 2], outw[4 * i + 3]);
+}
+
+}  // namespace
+
+cudaError_t launch_quantize(const void *w, int w_dtype, int64_t rows, int64_t K, int bits,
+                            int gs, int scheme, uint32_t *wq, uint16_t *s, uint16_t *b,
+                            cudaStream_t stream) {
+    const int64_t total = rows * (K / 8);
+    if (total == 0) return cudaSuccess;
+    const int threads = 256;
+    const dim3 grid((unsigned)((total + threads - 1) / threads));
+    if (bits == 4) {
+        if (w_dtype == 1)
+            quantize_kernel<4, true><<<grid, threads, 0, stream>>>(w, rows, K, gs, scheme, wq, s, b);
+        else
+            quantize_kernel<4, false><<<grid, threads, 0, stream>>>(w, rows, K, gs, scheme, wq, s, b);
+    } else {
+        if (w_dtype == 1)
+            quantize_kernel<8, true><<<grid, threads, 0, stream>>>(w, rows, K, gs, scheme, wq, s, b);
+        else
+            quantize_kernel<8, false><<<grid, threads, 0, stream>>>(w, rows, K, gs, scheme, wq, s, b);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequantize(const uint32_t *wq, const uint16_t *s, const uint16_t *b,
+                              int64_t rows, int64_t K, int bits, int gs, uint16_t *out,
+                              cudaStream_t stream) {
+    const int64_t total = rows * (K * bits / 32 / 4);
+    if (total == 0) return cudaSuccess;
+    const int threads = 256;
+    const dim3 grid((unsigned)((total + threads - 1) / threads));
+    if (bits == 4)
+        dequantize_kernel<4><<<grid, threads, 0, stream>>>(wq, s, b, rows, K, gs, out);
+    else
+        dequantize_kernel<8><<<grid, threads, 0, stream>>>(wq, s, b, rows, K, gs, out);
+    return cudaGetLastError();
+}
+
+}  // namespace nq

@@ -1,0 +1,112 @@
+"""CPU tests of the C ABI: the library loads, exports every entry point that
+include/nq.h declares, and validates arguments (status codes mirror
+compute::ErrorCode) before touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "nq.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(nq_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    for name in ("nq_quantized_matmul", "nq_dequantize", "nq_quantize", "nq_gather_qmm",
+                 "nq_moe_route", "nq_moe_switch", "nq_bits_from_shapes"):
+        assert name in syms
+
+
+def test_library_exports_every_declared_symbol(nqlib):
+    for name in declared_symbols():
+        assert hasattr(nqlib, name), name
+
+
+def test_python_signatures_cover_header():
+    from neurons_b200._lib import SIGNATURES
+    assert sorted(SIGNATURES) == declared_symbols()
+
+
+def test_version_and_device_count(nqlib):
+    assert nqlib.nq_version() >= 1
+    assert nqlib.nq_device_count() >= 0
+
+
+@pytest.mark.parametrize("w_cols,s_cols,gs", [(512, 64, 64), (1024, 64, 64), (96, 12, 64),
+                                              (192, 12, 64), (0, 64, 64), (1024, 32, 128)])
+def test_bits_from_shapes_matches_oracle(nqlib, oracle, w_cols, s_cols, gs):
+    assert nqlib.nq_bits_from_shapes(w_cols, s_cols, gs) == \
+        oracle.bits_from_shapes(w_cols, s_cols, gs)
+
+
+DUMMY = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+
+
+@pytest.mark.parametrize("bits,gs,K", [(3, 64, 128), (4, 48, 96), (4, 64, 96), (8, 16, 64)])
+def test_qmm_rejects_bad_quant_params(nqlib, bits, gs, K):
+    rc = nqlib.nq_quantized_matmul(DUMMY, 1, DUMMY, DUMMY, DUMMY, 8, K, bits, gs, DUMMY, None)
+    assert rc == 1  # InvalidInput
+    assert nqlib.nq_last_error()
+
+
+def test_qmm_requires_biases(nqlib):
+    rc = nqlib.nq_quantized_matmul(DUMMY, 1, DUMMY, DUMMY, None, 8, 64, 4, 64, DUMMY, None)
+    assert rc == 1
+    assert b"biases" in nqlib.nq_last_error()
+
+
+def test_qmm_rejects_unaligned(nqlib):
+    rc = nqlib.nq_quantized_matmul(ctypes.c_void_p(18), 1, DUMMY, DUMMY, DUMMY, 8, 64, 4, 64,
+                                   DUMMY, None)
+    assert rc == 1
+    assert b"aligned" in nqlib.nq_last_error()
+
+
+def test_empty_shapes_are_noops(nqlib):
+    assert nqlib.nq_quantized_matmul(None, 0, None, None, None, 8, 64, 4, 64, None, None) == 0
+    assert nqlib.nq_dequantize(None, None, None, 0, 64, 4, 64, None, None) == 0
+    assert nqlib.nq_moe_route(None, 0, 128, 8, None, None, None) == 0
+
+
+def test_gather_rejects_bad_batch(nqlib):
+    rc = nqlib.nq_gather_qmm(DUMMY, 3, 1, None, DUMMY, 8, DUMMY, DUMMY, DUMMY, 16, 32, 64, 4, 32,
+                             DUMMY, None)
+    assert rc == 1
+
+
+def test_moe_rejects_bad_topk(nqlib):
+    assert nqlib.nq_moe_route(DUMMY, 4, 128, 0, DUMMY, DUMMY, None) == 1
+    assert nqlib.nq_moe_route(DUMMY, 4, 4, 8, DUMMY, DUMMY, None) == 1
+    assert nqlib.nq_moe_route(DUMMY, 4, 2048, 8, DUMMY, DUMMY, None) == 1
+
+
+def test_moe_workspace_too_small(nqlib):
+    need = nqlib.nq_moe_workspace_size(64, 128, 8, 2048, 768)
+    assert need > 64 * 8 * 768 * 2
+    rc = nqlib.nq_moe_switch(DUMMY, 64, 2048, 768, 128, 8, DUMMY, DUMMY, DUMMY, DUMMY, DUMMY,
+                             DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, DUMMY, 4, 64, DUMMY, need - 1,
+                             DUMMY, None)
+    assert rc == 1
+    assert b"workspace" in nqlib.nq_last_error()
+
+
+def test_no_device_is_backend_not_available(nqlib):
+    if nqlib.nq_device_count() > 0:
+        pytest.skip("a CUDA device is present")
+    rc = nqlib.nq_quantized_matmul(DUMMY, 1, DUMMY, DUMMY, DUMMY, 8, 64, 4, 64, DUMMY, None)
+    assert rc == 3  # BackendNotAvailable
+
+
+def test_python_errors_carry_error_code():
+    import torch
+    from neurons_b200 import NQError, quantized_matmul
+    with pytest.raises(NQError) as ei:
+        quantized_matmul(torch.zeros(1, 64, dtype=torch.bfloat16), None, None)
+    assert ei.value.code == "InvalidInput"
