@@ -1,0 +1,133 @@
+"""GPU parity: gather_qmm, the MoE router and the batched switch step through
+the C ABI against the oracle (Qwen3-30B-A3B layer dims: E=128, top-8,
+hidden 2048, moe_intermediate 768, 4-bit g64)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from _util import (acts, assert_close, dev_bf16, dev_f32, dev_i32, dev_u32, host_u16,
+                   weights)
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def experts(oracle, rng, E, rows, cols, bits=4, gs=64):
+    wq, s, b = oracle.quantize(weights(rng, E * rows, cols), bits, gs, 0)
+    return wq.reshape(E, rows, -1), s.reshape(E, rows, -1), b.reshape(E, rows, -1)
+
+
+def dev3(t):
+    return dev_u32(t[0]), dev_bf16(t[1]), dev_bf16(t[2])
+
+
+def test_golden_gather(nqlib):
+    import neurons_b200 as nb
+    g = np.load(os.path.join(GOLDEN, "seeded_small.npz"))
+    out = nb.gather_qmm(dev_bf16(g["gq_x"]), dev_u32(g["moe_gate_wq"]), dev_bf16(g["moe_gate_s"]),
+                        dev_bf16(g["moe_gate_b"]), None, dev_i32(g["gq_rhs"]), True, 32, 4)
+    assert_close(host_u16(out), g["gq_out"], "golden gather")
+
+
+def test_gather_decode_shape(oracle, nqlib):
+    """x [1, 2048] against 8 of 128 experts [768, 2048] (the reference's decode call)."""
+    import neurons_b200 as nb
+    rng = np.random.default_rng(0)
+    W = experts(oracle, rng, 128, 768, 2048)
+    x = acts(rng, 1, 2048)[None]
+    rhs = rng.choice(128, 8, replace=False).astype(np.int32)
+    out = nb.gather_qmm(dev_bf16(x), *dev3(W), None, dev_i32(rhs), True, 64, 4)
+    ref = oracle.gather_qmm(x, *W, rhs, bits=4, group_size=64)
+    torch.cuda.synchronize()
+    assert nb.take_device_error() == 0
+    for i in range(8):
+        _, r32 = oracle.qmm(x[0], W[0][rhs[i]], W[1][rhs[i]], W[2][rhs[i]], 4, 64, want_f32=True)
+        assert_close(host_u16(out)[i], r32, f"slot {i}")
+    assert_close(host_u16(out), ref, "gather vs oracle bf16")
+
+
+def test_gather_batched_x_and_lhs(oracle, nqlib):
+    import neurons_b200 as nb
+    rng = np.random.default_rng(1)
+    W = experts(oracle, rng, 6, 40, 256, 8, 32)
+    x = acts(rng, 4 * 3, 256).reshape(4, 3, 256)       # x_batch 4, M 3
+    rhs = np.array([5, 0, 3, 3], np.int32)
+    out = nb.gather_qmm(dev_bf16(x), *dev3(W), None, dev_i32(rhs), True, 32, 8)
+    ref = oracle.gather_qmm(x, *W, rhs, bits=8, group_size=32)
+    assert_close(host_u16(out), ref, "x_batch == n_idx")
+    lhs = np.array([2, 2, 0, 1, 3], np.int32)
+    rhs2 = np.array([1, 4, 4, 0, 5], np.int32)
+    out2 = nb.gather_qmm(dev_bf16(x), *dev3(W), dev_i32(lhs), dev_i32(rhs2), True, 32, 8)
+    ref2 = oracle.gather_qmm(x, *W, rhs2, lhs=lhs, bits=8, group_size=32)
+    assert_close(host_u16(out2), ref2, "lhs indices")
+
+
+def test_gather_bad_index_zeroes_and_flags(oracle, nqlib):
+    import neurons_b200 as nb
+    rng = np.random.default_rng(2)
+    W = experts(oracle, rng, 4, 32, 128, 4, 32)
+    x = acts(rng, 1, 128)[None]
+    nb.take_device_error()
+    out = nb.gather_qmm(dev_bf16(x), *dev3(W), None, dev_i32(np.array([1, 9], np.int32)),
+                        True, 32, 4)
+    torch.cuda.synchronize()
+    assert nb.take_device_error() & 2
+    assert (host_u16(out)[1] == 0).all()
+    ref = oracle.gather_qmm(x, *W, np.array([1], np.int32), bits=4, group_size=32)
+    assert_close(host_u16(out)[:1], ref, "valid slot")
+
+
+@pytest.mark.parametrize("T", [1, 7, 64, 2048])
+def test_route_matches_oracle(oracle, nqlib, T):
+    import neurons_b200 as nb
+    rng = np.random.default_rng(T)
+    logits = acts(rng, T, 128)
+    idx, sc = nb.moe_route(dev_bf16(logits), 8)
+    ridx, rsc = oracle.moe_route(logits, 8)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ridx)
+    np.testing.assert_allclose(sc.cpu().numpy(), rsc, rtol=2e-6, atol=1e-7)
+
+
+def test_route_ties(oracle, nqlib):
+    import neurons_b200 as nb
+    logits = oracle.f32_to_bf16(np.array([[0.5, 1.0, 1.0, 0.25, 1.0] * 8], np.float32))
+    idx, sc = nb.moe_route(dev_bf16(logits), 4)
+    ridx, rsc = oracle.moe_route(logits, 4)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ridx)
+
+
+def test_golden_switch(oracle, nqlib):
+    import neurons_b200 as nb
+    g = np.load(os.path.join(GOLDEN, "seeded_small.npz"))
+    mats = [(dev_u32(g[f"moe_{n}_wq"]), dev_bf16(g[f"moe_{n}_s"]), dev_bf16(g[f"moe_{n}_b"]))
+            for n in ("gate", "up", "down")]
+    y = nb.moe_switch(dev_bf16(g["moe_x"]), dev_i32(g["moe_idx"]), dev_f32(g["moe_scores"]),
+                      *mats, 32, 4)
+    assert_close(host_u16(y), g["moe_y_fused"], "golden switch (fused rounding points)")
+
+
+@pytest.mark.parametrize("T,E,k,H,I", [(1, 128, 8, 2048, 768), (20, 128, 8, 2048, 768),
+                                       (3, 16, 4, 256, 128), (64, 16, 4, 256, 128),
+                                       (100, 8, 2, 128, 64)])
+def test_switch_matches_oracle(oracle, nqlib, T, E, k, H, I):
+    """pair mode (T*k <= E) and grouped mode (T*k > E) against the oracle's fused
+    rounding points; the MLX op-chain rounding is checked normwise."""
+    import neurons_b200 as nb
+    rng = np.random.default_rng(T * 31 + E)
+    gate = experts(oracle, rng, E, I, H)
+    up = experts(oracle, rng, E, I, H)
+    down = experts(oracle, rng, E, H, I)
+    x = acts(rng, T, H)
+    logits = acts(rng, T, E)
+    idx, sc = oracle.moe_route(logits, k)
+    y = nb.moe_switch(dev_bf16(x), dev_i32(idx), dev_f32(sc), dev3(gate), dev3(up), dev3(down),
+                      64, 4)
+    torch.cuda.synchronize()
+    assert nb.take_device_error() == 0
+    ref = oracle.moe_switch(x, idx, sc, gate, up, down, 4, 64, rounding=1)
+    assert_close(host_u16(y), ref, f"switch T={T}")
+    ref_mlx = oracle.bf16_to_f32(oracle.moe_switch(x, idx, sc, gate, up, down, 4, 64, rounding=0))
+    yy = oracle.bf16_to_f32(host_u16(y))
+    assert np.linalg.norm(yy - ref_mlx) / np.linalg.norm(ref_mlx) < 1e-2

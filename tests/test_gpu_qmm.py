@@ -1,0 +1,159 @@
+"""GPU parity: quantized_matmul through the C ABI against the oracle, on both
+kernel paths (mma.sync GEMV for M <= 32, TMA + tcgen05 GEMM above), ragged
+shapes, both bit widths and every group size, the golden fixtures, and the
+full-size workloads (decode 4096x4096 at M=1; prefill 2048x14336x4096)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from _util import (acts, assert_close, dev_bf16, dev_u32, host_u16, weights)
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def run_case(oracle, M, N, K, bits, gs, seed=0, scheme=0):
+    import neurons_b200 as nb
+    rng = np.random.default_rng(seed)
+    wq, s, b = oracle.quantize(weights(rng, N, K), bits, gs, scheme)
+    x = acts(rng, M, K)
+    _, ref = oracle.qmm(x, wq, s, b, bits, gs, want_f32=True)
+    y = nb.quantized_matmul(dev_bf16(x), dev_u32(wq), dev_bf16(s), dev_bf16(b), True, gs, bits)
+    torch.cuda.synchronize()
+    assert nb.take_device_error() == 0
+    return assert_close(host_u16(y), ref, f"M={M} N={N} K={K} bits={bits} gs={gs}")
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 9, 16, 17, 24, 31, 32])
+def test_gemv_path_m_sweep(oracle, nqlib, M):
+    run_case(oracle, M, 80, 512, 4, 64, seed=M)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("gs", [32, 64, 128])
+@pytest.mark.parametrize("M", [1, 7])
+def test_gemv_path_bits_groups(oracle, nqlib, bits, gs, M):
+    run_case(oracle, M, 48, 1024, bits, gs, seed=bits + gs)
+
+
+@pytest.mark.parametrize("N,K", [(16, 32), (40, 96), (100, 160), (17, 4096), (1, 128),
+                                 (3072, 3072), (1024, 3072), (3072, 8192)])
+def test_gemv_path_ragged(oracle, nqlib, N, K):
+    run_case(oracle, 1, N, K, 4, 32, seed=N)
+
+
+@pytest.mark.parametrize("M", [33, 64, 65, 100, 128, 129, 200, 256, 257, 512])
+def test_tc_path_m_sweep(oracle, nqlib, M):
+    run_case(oracle, M, 256, 512, 4, 64, seed=M)
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("gs", [32, 64, 128])
+def test_tc_path_bits_groups(oracle, nqlib, bits, gs):
+    run_case(oracle, 300, 384, 1024, bits, gs, seed=bits * gs)
+
+
+@pytest.mark.parametrize("N,K", [(1, 64), (130, 96), (200, 160), (128, 4096), (257, 2048)])
+def test_tc_path_ragged(oracle, nqlib, N, K):
+    run_case(oracle, 96, N, K, 4, 32, seed=N + K)
+
+
+def test_golden_seeded_qmm(nqlib):
+    import neurons_b200 as nb
+    g = np.load(os.path.join(GOLDEN, "seeded_small.npz"))
+    for bits in (4, 8):
+        for gs in (32, 64, 128):
+            for scheme in (0, 1):
+                tag = f"b{bits}_g{gs}_s{scheme}"
+                y = nb.quantized_matmul(dev_bf16(g[f"{tag}_x"]), dev_u32(g[f"{tag}_wq"]),
+                                        dev_bf16(g[f"{tag}_s"]), dev_bf16(g[f"{tag}_b"]), True,
+                                        gs, bits)
+                assert_close(host_u16(y), g[f"{tag}_y"], tag)
+
+
+def test_decode_config_full_size(oracle, nqlib):
+    """M=1, N=K=4096, 4-bit g64, minmax scheme as the decode workload defines it."""
+    run_case(oracle, 1, 4096, 4096, 4, 64, seed=0, scheme=1)
+
+
+def test_prefill_config_full_size(oracle, nqlib):
+    """M=2048, N=14336, K=4096, 4-bit g64: every output against a torch fp32 matmul
+    of the bit-exact dequantized weights, plus 64 sampled weight rows against the
+    oracle itself."""
+    import neurons_b200 as nb
+    M, N, K = 2048, 14336, 4096
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w = torch.randn(N, K, device="cuda", generator=g) * 0.02
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    wq, s, b = nb.quantize(w, 64, 4, 1)
+    y = nb.quantized_matmul(x, wq, s, b, True, 64, 4)
+    wh = nb.dequantize(wq, s, b, 64, 4)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref = x.float() @ wh.float().T
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    torch.cuda.synchronize()
+    assert nb.take_device_error() == 0
+    assert_close(host_u16(y), ref.cpu().numpy(), "prefill vs torch fp32")
+    rows = np.random.default_rng(1).choice(N, 64, replace=False)
+    wq_h = wq.cpu().view(torch.int32).numpy().view(np.uint32)[rows]
+    s_h, b_h = host_u16(s)[rows], host_u16(b)[rows]
+    _, ref_o = oracle.qmm(host_u16(x), wq_h, s_h, b_h, 4, 64, want_f32=True)
+    assert_close(host_u16(y)[:, rows], ref_o, "prefill vs oracle rows")
+    np.testing.assert_array_equal(host_u16(wh)[rows], oracle.dequantize(wq_h, s_h, b_h, 4, 64))
+
+
+def test_square_prefill_and_8bit(oracle, nqlib):
+    """M=2048, N=K=4096 at 4 and 8 bits (sampled rows against the oracle)."""
+    import neurons_b200 as nb
+    M, N, K = 2048, 4096, 4096
+    rng = np.random.default_rng(5)
+    x = acts(rng, M, K)
+    for bits in (4, 8):
+        wq, s, b = oracle.quantize(weights(rng, N, K), bits, 64, 0)
+        y = host_u16(nb.quantized_matmul(dev_bf16(x), dev_u32(wq), dev_bf16(s), dev_bf16(b),
+                                          True, 64, bits))
+        rows = rng.choice(N, 96, replace=False)
+        _, ref = oracle.qmm(x, wq[rows], s[rows], b[rows], bits, 64, want_f32=True)
+        assert_close(y[:, rows], ref, f"square bits={bits}")
+
+
+def test_lin_mirrors_mlx_ops(oracle, nqlib):
+    """lin() infers bits from the shapes exactly as mlx_ops::lin does."""
+    import neurons_b200 as nb
+    rng = np.random.default_rng(3)
+    for bits in (4, 8):
+        wq, s, b = oracle.quantize(weights(rng, 64, 512), bits, 64, 0)
+        wm = {"q_proj.weight": dev_u32(wq), "q_proj.scales": dev_bf16(s),
+              "q_proj.biases": dev_bf16(b)}
+        x = acts(rng, 3, 512)
+        y = nb.lin(dev_bf16(x), "q_proj", wm, 64)
+        _, ref = oracle.qmm(x, wq, s, b, bits, 64, want_f32=True)
+        assert_close(host_u16(y), ref, f"lin bits={bits}")
+    with pytest.raises(nb.NQError) as ei:
+        nb.lin(dev_bf16(x), "dense", {"dense.weight": dev_bf16(x)}, 64)
+    assert ei.value.code == "InvalidModel"
+
+
+def test_back_to_back_launches_are_ordered(oracle, nqlib):
+    """Programmatic dependent launch must not let a projection read an input the
+    previous projection is still writing: chain y1 = W1 x, y2 = W2 y1."""
+    import neurons_b200 as nb
+    rng = np.random.default_rng(9)
+    w1 = oracle.quantize(weights(rng, 512, 512), 4, 64, 0)
+    w2 = oracle.quantize(weights(rng, 512, 512), 4, 64, 0)
+    x = acts(rng, 1, 512)
+    d1 = [dev_u32(w1[0]), dev_bf16(w1[1]), dev_bf16(w1[2])]
+    d2 = [dev_u32(w2[0]), dev_bf16(w2[1]), dev_bf16(w2[2])]
+    xd = dev_bf16(x)
+    for _ in range(20):
+        y1 = nb.quantized_matmul(xd, *d1, True, 64, 4)
+        y2 = nb.quantized_matmul(y1, *d2, True, 64, 4)
+    _, ref1 = oracle.qmm(x, *w1, 4, 64, want_f32=True)
+    assert_close(host_u16(y1), ref1, "chained stage 1")
+    _, ref2 = oracle.qmm(host_u16(y1), *w2, 4, 64, want_f32=True)
+    assert_close(host_u16(y2), ref2, "chained stage 2")
