@@ -1,0 +1,396 @@
+"""Benchmark of the quantized-matmul path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload prefill|square|decode]
+
+Workloads (4-bit, group size 64, MLX affine layout, weights N(0, 0.02)
+quantized with the min/max scheme, activations N(0, 1) in bf16, seeded):
+  prefill  x [2048, 4096] . W[14336, 4096]^T   (the headline, TFLOP/s)
+  square   x [2048, 4096] . W[4096, 4096]^T    (TFLOP/s)
+  decode   x [1, 4096]    . W[4096, 4096]^T    (GB/s of algorithmic bytes)
+A step is one quantized_matmul call through the C ABI.  Each rank runs its
+own full step on its own GPU (token batches are independent: no collective on
+the data path, weak scaling); the timed region is bracketed by a barrier and a
+device synchronize, timed with CUDA events on the launching stream, and the
+reported time is the max over ranks.  L2: every step reads a different one of
+R input sets whose combined size is well above the 126 MB L2.
+
+The line also carries: the decode (M=1) figure of the same run, the roofline
+of the dominant kernel (CUDA-event duration per launch, algorithmic flops or
+bytes, measured peaks), the CPU baseline (the oracle on the host cores, a
+bounded sample of the same workload), the end-to-end figure through the
+public API with host buffers (pinned host -> device copy of x, device -> host
+copy of y inside the timed region), SM clocks sampled during the timed region,
+and the number of this library's kernel launches in the timed region.
+
+--impl reference runs the reference arm: the reference's CPU implementation of
+this path is MLX, which cannot be built here, so the arm times the oracle's
+restatement of it (oracle/nq_oracle.c) on all host threads; rank 0 only.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "4-bit g64 qmm: M=1 GB/s (% HBM peak), M=2048 TFLOP/s (% bf16 peak), 1–8 GPU"
+
+WORKLOADS = {
+    "prefill": dict(M=2048, N=14336, K=4096),
+    "square": dict(M=2048, N=4096, K=4096),
+    "decode": dict(M=1, N=4096, K=4096),
+}
+BITS, GS = 4, 64
+L2_BYTES = 126 * 1024 * 1024
+
+
+def algo_bytes(M, N, K, bits=BITS, gs=GS):
+    return N * K * bits // 8 + N * (K // gs) * 4 + M * K * 2 + M * N * 2
+
+
+def algo_flops(M, N, K):
+    return 2 * M * N * K
+
+
+def peaks():
+    p = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        p = {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+             "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+             "source": "measured"}
+    return p
+
+
+def ncu_traffic(workload):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary
+    (profiles/traffic.txt: lines '<workload> <bytes per launch>'), or None."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == workload:
+            return float(parts[1])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) == 8 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, v in zip(names, r[4:8]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]),
+                "samples": len(rows), "reasons": sorted(reasons)}
+
+
+def dist_setup(n_gpus):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_inputs(M, N, K, sets, seed):
+    """R independent (x, W) sets quantized on the device (min/max scheme)."""
+    import torch
+    import neurons_b200 as nb
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    out = []
+    for _ in range(sets):
+        w = torch.randn(N, K, device="cuda", generator=g) * 0.02
+        wq, s, b = nb.quantize(w, GS, BITS, nb.SCHEME_MINMAX)
+        del w
+        x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+        y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        out.append((x, wq, s, b, y))
+    torch.cuda.synchronize()
+    return out
+
+
+def time_device(M, N, K, steps, warmup, world, seed):
+    """Device-resident inputs; returns (seconds for `steps` launches max over ranks,
+    mean per-launch event duration of this rank, sets used)."""
+    import torch
+    import neurons_b200 as nb
+    per_set = algo_bytes(M, N, K) + M * N * 2
+    sets = max(2, -(-3 * L2_BYTES // per_set))
+    sets = min(sets, 64)
+    data = make_inputs(M, N, K, sets, seed)
+    stream = torch.cuda.current_stream()
+    for i in range(warmup):
+        x, wq, s, b, y = data[i % sets]
+        nb.quantized_matmul(x, wq, s, b, True, GS, BITS, out=y)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(steps):
+        x, wq, s, b, y = data[i % sets]
+        ev[i][0].record(stream)
+        nb.quantized_matmul(x, wq, s, b, True, GS, BITS, out=y)
+        ev[i][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    total = t0.elapsed_time(t1) / 1e3
+    per_launch = statistics.mean(a.elapsed_time(b) for a, b in ev) / 1e3
+    assert nb.take_device_error() == 0
+    return max_over_ranks(total, world), per_launch, sets
+
+
+def time_e2e(M, N, K, steps, warmup, world, seed):
+    """Through the public API with host buffers: pinned x -> device, qmm, y -> pinned host."""
+    import torch
+    import neurons_b200 as nb
+    data = make_inputs(M, N, K, 1, seed + 1)
+    _, wq, s, b, y = data[0]
+    xh = torch.randn(M, K, generator=torch.Generator().manual_seed(seed)).to(
+        torch.bfloat16).pin_memory()
+    yh = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        xd.copy_(xh, non_blocking=True)
+        nb.quantized_matmul(xd, wq, s, b, True, GS, BITS, out=y)
+        yh.copy_(y, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    total = max_over_ranks(t0.elapsed_time(t1) / 1e3, world)
+    return total, M * K * 2, M * N * 2
+
+
+def cpu_baseline(M, N, K, target_s=12.0):
+    """The oracle's qmm on every host thread, on a bounded sample of the workload:
+    all M tokens against a slice of the weight rows, sized for ~target_s seconds."""
+    import numpy as np
+    from oracle import oracle as O
+    rng = np.random.default_rng(0)
+    threads = O.max_threads()
+    x = O.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+
+    def run(rows):
+        wq, s, b = O.quantize((rng.standard_normal((rows, K)) * 0.02).astype(np.float32),
+                              BITS, GS, O.SCHEME_MINMAX)
+        t = time.perf_counter()
+        O.qmm(x, wq, s, b, BITS, GS, nthreads=threads)
+        return time.perf_counter() - t
+
+    probe_rows = 8 if M > 1 else 512
+    dt = run(probe_rows)
+    rows = int(min(N, max(probe_rows, probe_rows * target_s / max(dt, 1e-6))))
+    dt = run(rows)
+    flops = algo_flops(M, rows, K)
+    byts = algo_bytes(M, rows, K)
+    return {"rows": rows, "seconds": dt, "threads": threads, "tflops": flops / dt / 1e12,
+            "gbs": byts / dt / 1e9}
+
+
+def ours(args):
+    import torch
+    world, rank, local = dist_setup(args.gpus)
+    import neurons_b200 as nb
+    nb.lib()
+    wl = WORKLOADS[args.workload]
+    M, N, K = wl["M"], wl["N"], wl["K"]
+    pk = peaks()
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_dev, per_launch, sets = time_device(M, N, K, args.steps, args.warmup, world, seed=rank)
+    clk = clocks.stop()
+    flops, byts = algo_flops(M, N, K), algo_bytes(M, N, K)
+    launches = args.steps
+    if M > 1:
+        value = world * flops * args.steps / t_dev / 1e12
+        unit = "TFLOP/s"
+        achieved = flops / per_launch / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
+                "peak_source": pk["source"] + " (burst bf16 GEMM)",
+                "algorithmic_flops_per_launch": flops}
+    else:
+        value = world * byts * args.steps / t_dev / 1e9
+        unit = "GB/s"
+        achieved = byts / per_launch / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"], "peak_source": pk["source"],
+                "algorithmic_bytes_per_launch": byts}
+    roof["traffic"] = ncu_traffic(args.workload)
+    line = {"metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t_dev / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) weights quantized 4-bit g64, N(0,1) bf16 x)",
+            "config": {"workload": args.workload, "M": M, "N": N, "K": K, "bits": BITS,
+                       "group_size": GS, "parallelism": f"replicas x{world} (token batches)",
+                       "l2": f"rotating {sets} input sets of "
+                             f"{(algo_bytes(M, N, K) + M * N * 2) / 2**20:.0f} MiB (> L2)"},
+            "roofline": roof, "gpu_launches": launches, "clocks": clk}
+    if args.workload != "decode" and not args.no_decode:
+        d = WORKLOADS["decode"]
+        dsteps = max(50, args.steps * 10)
+        t_d, pl_d, _ = time_device(d["M"], d["N"], d["K"], dsteps, max(args.warmup, 10), world,
+                                   seed=rank + 100)
+        db = algo_bytes(d["M"], d["N"], d["K"])
+        line["decode"] = {"workload": "decode M=1 N=K=4096", "unit": "GB/s",
+                          "value": world * db * dsteps / t_d / 1e9,
+                          "kernel_gbs": db / pl_d / 1e9, "frac": db / pl_d / 1e9 / pk["hbm_gbs"],
+                          "us_per_launch": pl_d * 1e6, "algorithmic_bytes_per_launch": db}
+        line["gpu_launches"] += dsteps
+    t_e, h2d, d2h = time_e2e(M, N, K, args.steps, args.warmup, world, seed=rank)
+    e2e_val = world * (flops if M > 1 else byts) * args.steps / t_e / (1e12 if M > 1 else 1e9)
+    line["e2e"] = {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": h2d,
+                   "d2h_bytes_per_step": d2h}
+    line["gpu_launches"] += args.steps
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cb = cpu_baseline(M, N, K)
+        line["cpu_baseline"] = {
+            "value": cb["tflops"] if M > 1 else cb["gbs"], "unit": unit, "cores": cb["threads"],
+            "kind": "port",
+            "sample": f"oracle qmm (fp64 accumulation) over all {M} tokens x {cb['rows']} of "
+                      f"{N} weight rows, K={K}, {cb['seconds']:.1f} s"}
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    wl = WORKLOADS[args.workload]
+    M, N, K = wl["M"], wl["N"], wl["K"]
+    samples = []
+    cb = None
+    for i in range(args.warmup + args.steps):
+        cb = cpu_baseline(M, N, K, target_s=4.0 if i >= args.warmup else 1.0)
+        if i >= args.warmup:
+            samples.append(cb)
+    unit = "TFLOP/s" if M > 1 else "GB/s"
+    v = statistics.mean(c["tflops"] if M > 1 else c["gbs"] for c in samples)
+    sec = statistics.mean(c["seconds"] for c in samples)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": {"workload": args.workload, "M": M, "N": N, "K": K,
+                                            "bits": BITS, "group_size": GS},
+            "cpu_baseline": {"value": v, "unit": unit, "cores": cb["threads"], "kind": "port",
+                             "sample": f"each step: oracle qmm over all {M} tokens x "
+                                       f"{cb['rows']} of {N} weight rows, K={K} (the "
+                                       "reference's MLX CPU path cannot be built here)"},
+            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="prefill", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-line")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        reference(args)
+    else:
+        ours(args)
+
+
+if __name__ == "__main__":
+    main()

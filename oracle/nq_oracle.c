@@ -356,9 +356,9 @@ int or_moe_route(const uint16_t *logits, int64_t T, int64_t E, int64_t top_k,
 
 static float silu_f32(float g) { return g / (1.0f + expf(-g)); }
 
-/* Switch-MLP of one MoE layer for T tokens, given the routing.
- * x: [T,H] bf16; idx/scores: [T,top_k]; gate/up: [E,I,H*bits/32] (+ [E,I,H/gs]
- * scales/biases); down: [E,H,I*bits/32] (+ [E,H,I/gs]); y: [T,H] bf16.
+/* Switch-MLP of one MoE layer for T tokens, given the routing, in two
+ * stages.  x: [T,H] bf16; idx/scores: [T,top_k]; gate/up: [E,I,H*bits/32]
+ * (+ [E,I,H/gs] scales/biases); down: [E,H,I*bits/32] (+ [E,H,I/gs]).
  *
  * rounding == 0 follows MLX's op chain (qwen3_transformer_moe_model_mlx.cpp:69-78):
  *   gate_k, up_k, down_k rounded to bf16 (gather_qmm outputs),
@@ -367,24 +367,19 @@ static float silu_f32(float g) { return g / (1.0f + expf(-g)); }
  * rounding == 1 states the fused GPU kernel's rounding points:
  *   gate/up sums kept in fp32, h = bf16(silu(g) * u) in fp32,
  *   down sums kept in fp32, y = bf16(sum_k bf16(score_k) * down_k). */
-int or_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I,
-                  int64_t E, int64_t top_k, const int32_t *idx,
-                  const float *scores, const uint32_t *wg, const uint16_t *sg,
-                  const uint16_t *bg, const uint32_t *wu, const uint16_t *su,
-                  const uint16_t *bu, const uint32_t *wd, const uint16_t *sd,
-                  const uint16_t *bd, int bits, int gs, int rounding,
-                  uint16_t *y, int nthreads) {
-    if (check_quant_params(I, H, bits, gs) || check_quant_params(H, I, bits, gs) ||
-        T < 0 || E <= 0 || top_k <= 0)
+
+/* Stage 1: h[T*top_k, I] (bf16 bits) for every (token, slot) pair. */
+int or_moe_hidden(const uint16_t *x, int64_t T, int64_t H, int64_t I, int64_t E,
+                  int64_t top_k, const int32_t *idx, const uint32_t *wg,
+                  const uint16_t *sg, const uint16_t *bg, const uint32_t *wu,
+                  const uint16_t *su, const uint16_t *bu, int bits, int gs,
+                  int rounding, uint16_t *h, int nthreads) {
+    if (check_quant_params(I, H, bits, gs) || T < 0 || E <= 0 || top_k <= 0)
         return OR_INVALID;
     for (int64_t i = 0; i < T * top_k; ++i)
         if (idx[i] < 0 || idx[i] >= E) return OR_INVALID;
     set_threads(nthreads);
-    const int64_t wgu = H * bits / 32, ggu = H / gs;   /* gate/up row words, groups */
-    const int64_t wdn = I * bits / 32, gdn = I / gs;   /* down row words, groups */
-    float *acc = (float *)calloc((size_t)(T * H + 1), sizeof(float));
-    float *h = (float *)malloc(sizeof(float) * (size_t)(T * top_k * I + 1));
-    /* gate/up and SwiGLU */
+    const int64_t wgu = H * bits / 32, ggu = H / gs;
 #pragma omp parallel
     {
         float *rg = (float *)malloc(sizeof(float) * (size_t)H);
@@ -407,14 +402,29 @@ int or_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I,
                     float sg_ = round_bf16(1.0f / (1.0f + expf(-g)));
                     hv = round_bf16(round_bf16(sg_ * g) * u);
                 } else {
-                    hv = round_bf16(silu_f32(g) * u);
+                    hv = silu_f32(g) * u;
                 }
-                h[tk * I + n] = hv;
+                h[tk * I + n] = or_f32_to_bf16(hv);
             }
         }
         free(rg); free(ru); free(xf);
     }
-    /* down projection and the score-weighted sum, slot order 0..top_k-1 */
+    return OR_OK;
+}
+
+/* Stage 2: y[T,H] = combine over slots of the down projection of h. */
+int or_moe_combine(const uint16_t *h, int64_t T, int64_t H, int64_t I, int64_t E,
+                   int64_t top_k, const int32_t *idx, const float *scores,
+                   const uint32_t *wd, const uint16_t *sd, const uint16_t *bd,
+                   int bits, int gs, int rounding, uint16_t *y, int nthreads) {
+    if (check_quant_params(H, I, bits, gs) || T < 0 || E <= 0 || top_k <= 0)
+        return OR_INVALID;
+    for (int64_t i = 0; i < T * top_k; ++i)
+        if (idx[i] < 0 || idx[i] >= E) return OR_INVALID;
+    set_threads(nthreads);
+    const int64_t wdn = I * bits / 32, gdn = I / gs;
+    float *hf = (float *)malloc(sizeof(float) * (size_t)(T * top_k * I + 1));
+    for (int64_t i = 0; i < T * top_k * I; ++i) hf[i] = or_bf16_to_f32(h[i]);
 #pragma omp parallel
     {
         float *rd = (float *)malloc(sizeof(float) * (size_t)I);
@@ -426,18 +436,33 @@ int or_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I,
                     int64_t tk = t * top_k + j, e = idx[tk];
                     int64_t row = e * H + n;
                     dequant_row_f32(wd + row * wdn, sd + row * gdn, bd + row * gdn, I, bits, gs, rd);
-                    float d = (float)dot_f32_f64(h + tk * I, rd, I);
+                    float d = (float)dot_f32_f64(hf + tk * I, rd, I);
                     float sc = round_bf16(scores[tk]);
                     if (rounding == 0) sum += (double)round_bf16(round_bf16(d) * sc);
                     else sum += (double)sc * (double)d;
                 }
-                acc[t * H + n] = (float)sum;
+                y[t * H + n] = or_f32_to_bf16((float)sum);
             }
         }
         free(rd);
     }
-    for (int64_t i = 0; i < T * H; ++i) y[i] = or_f32_to_bf16(acc[i]);
-    free(acc);
-    free(h);
+    free(hf);
     return OR_OK;
+}
+
+int or_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I,
+                  int64_t E, int64_t top_k, const int32_t *idx,
+                  const float *scores, const uint32_t *wg, const uint16_t *sg,
+                  const uint16_t *bg, const uint32_t *wu, const uint16_t *su,
+                  const uint16_t *bu, const uint32_t *wd, const uint16_t *sd,
+                  const uint16_t *bd, int bits, int gs, int rounding,
+                  uint16_t *y, int nthreads) {
+    uint16_t *h = (uint16_t *)malloc(sizeof(uint16_t) * (size_t)(T * top_k * I + 1));
+    int rc = or_moe_hidden(x, T, H, I, E, top_k, idx, wg, sg, bg, wu, su, bu, bits, gs,
+                           rounding, h, nthreads);
+    if (!rc)
+        rc = or_moe_combine(h, T, H, I, E, top_k, idx, scores, wd, sd, bd, bits, gs,
+                            rounding, y, nthreads);
+    free(h);
+    return rc;
 }

@@ -35,6 +35,10 @@ def lib():
         _lib.or_moe_route.argtypes = [P, I64, I64, I64, P, P]
         _lib.or_moe_switch.argtypes = [P, I64, I64, I64, I64, I64, P, P,
                                        P, P, P, P, P, P, P, P, P, I, I, I, P, I]
+        _lib.or_moe_hidden.argtypes = [P, I64, I64, I64, I64, I64, P, P, P, P, P, P, P,
+                                       I, I, I, P, I]
+        _lib.or_moe_combine.argtypes = [P, I64, I64, I64, I64, I64, P, P, P, P, P,
+                                        I, I, I, P, I]
         _lib.or_max_threads.argtypes = []
     return _lib
 
@@ -145,6 +149,37 @@ def moe_switch(x, idx, scores, gate, up, down, bits=4, group_size=64, rounding=1
                                _p(wg), _p(sg), _p(bg), _p(wu), _p(su), _p(bu),
                                _p(wd), _p(sd), _p(bd), bits, group_size, rounding,
                                _p(y), nthreads), "moe_switch")
+    return y
+
+
+def moe_hidden(x, idx, gate, up, bits=4, group_size=64, rounding=1, nthreads=0):
+    """Stage 1 of the switch step: h [T*top_k, I] bf16 bits, pair order t*top_k + j."""
+    x = _c(x, np.uint16)
+    idx = _c(idx, np.int32)
+    T, H = x.shape
+    top_k = idx.shape[1]
+    wg, sg, bg = (_c(gate[0], np.uint32), _c(gate[1], np.uint16), _c(gate[2], np.uint16))
+    wu, su, bu = (_c(up[0], np.uint32), _c(up[1], np.uint16), _c(up[2], np.uint16))
+    E, I = wg.shape[0], wg.shape[1]
+    h = np.zeros((T * top_k, I), np.uint16)
+    _check(lib().or_moe_hidden(_p(x), T, H, I, E, top_k, _p(idx), _p(wg), _p(sg), _p(bg),
+                               _p(wu), _p(su), _p(bu), bits, group_size, rounding, _p(h),
+                               nthreads), "moe_hidden")
+    return h
+
+
+def moe_combine(h, idx, scores, down, bits=4, group_size=64, rounding=1, nthreads=0):
+    """Stage 2 of the switch step: y [T, H] from h [T*top_k, I] (pair order)."""
+    h = _c(h, np.uint16)
+    idx, scores = _c(idx, np.int32), _c(scores, np.float32)
+    T, top_k = idx.shape
+    wd, sd, bd = (_c(down[0], np.uint32), _c(down[1], np.uint16), _c(down[2], np.uint16))
+    E, H = wd.shape[0], wd.shape[1]
+    I = h.shape[1]
+    y = np.zeros((T, H), np.uint16)
+    _check(lib().or_moe_combine(_p(h), T, H, I, E, top_k, _p(idx), _p(scores), _p(wd),
+                                _p(sd), _p(bd), bits, group_size, rounding, _p(y), nthreads),
+           "moe_combine")
     return y
 
 

@@ -21,7 +21,8 @@ def rel_errors(y, ref):
 
 
 def assert_close(y_bits, ref, what=""):
-    """y_bits: bf16 bit patterns from the GPU; ref: oracle sums (fp32/fp64) or bf16 bits."""
+    """y_bits: bf16 bit patterns from the GPU; ref: the oracle's bf16 output (bit
+    patterns) -- both sides rounded to bf16 as the contract's "bf16 out" says."""
     y = O.bf16_to_f32(y_bits)
     r = O.bf16_to_f32(ref) if np.asarray(ref).dtype == np.uint16 else np.asarray(ref)
     rel = rel_errors(y, r)

@@ -19,7 +19,7 @@ def run_case(oracle, M, N, K, bits, gs, seed=0, scheme=0):
     rng = np.random.default_rng(seed)
     wq, s, b = oracle.quantize(weights(rng, N, K), bits, gs, scheme)
     x = acts(rng, M, K)
-    _, ref = oracle.qmm(x, wq, s, b, bits, gs, want_f32=True)
+    ref = oracle.qmm(x, wq, s, b, bits, gs)
     y = nb.quantized_matmul(dev_bf16(x), dev_u32(wq), dev_bf16(s), dev_bf16(b), True, gs, bits)
     torch.cuda.synchronize()
     assert nb.take_device_error() == 0
@@ -98,11 +98,11 @@ def test_prefill_config_full_size(oracle, nqlib):
         torch.backends.cuda.matmul.allow_tf32 = prev
     torch.cuda.synchronize()
     assert nb.take_device_error() == 0
-    assert_close(host_u16(y), ref.cpu().numpy(), "prefill vs torch fp32")
+    assert_close(host_u16(y), oracle.f32_to_bf16(ref.cpu().numpy()), "prefill vs torch fp32")
     rows = np.random.default_rng(1).choice(N, 64, replace=False)
     wq_h = wq.cpu().view(torch.int32).numpy().view(np.uint32)[rows]
     s_h, b_h = host_u16(s)[rows], host_u16(b)[rows]
-    _, ref_o = oracle.qmm(host_u16(x), wq_h, s_h, b_h, 4, 64, want_f32=True)
+    ref_o = oracle.qmm(host_u16(x), wq_h, s_h, b_h, 4, 64)
     assert_close(host_u16(y)[:, rows], ref_o, "prefill vs oracle rows")
     np.testing.assert_array_equal(host_u16(wh)[rows], oracle.dequantize(wq_h, s_h, b_h, 4, 64))
 
@@ -118,7 +118,7 @@ def test_square_prefill_and_8bit(oracle, nqlib):
         y = host_u16(nb.quantized_matmul(dev_bf16(x), dev_u32(wq), dev_bf16(s), dev_bf16(b),
                                           True, 64, bits))
         rows = rng.choice(N, 96, replace=False)
-        _, ref = oracle.qmm(x, wq[rows], s[rows], b[rows], bits, 64, want_f32=True)
+        ref = oracle.qmm(x, wq[rows], s[rows], b[rows], bits, 64)
         assert_close(y[:, rows], ref, f"square bits={bits}")
 
 
@@ -132,8 +132,7 @@ def test_lin_mirrors_mlx_ops(oracle, nqlib):
               "q_proj.biases": dev_bf16(b)}
         x = acts(rng, 3, 512)
         y = nb.lin(dev_bf16(x), "q_proj", wm, 64)
-        _, ref = oracle.qmm(x, wq, s, b, bits, 64, want_f32=True)
-        assert_close(host_u16(y), ref, f"lin bits={bits}")
+        assert_close(host_u16(y), oracle.qmm(x, wq, s, b, bits, 64), f"lin bits={bits}")
     with pytest.raises(nb.NQError) as ei:
         nb.lin(dev_bf16(x), "dense", {"dense.weight": dev_bf16(x)}, 64)
     assert ei.value.code == "InvalidModel"
@@ -153,7 +152,6 @@ def test_back_to_back_launches_are_ordered(oracle, nqlib):
     for _ in range(20):
         y1 = nb.quantized_matmul(xd, *d1, True, 64, 4)
         y2 = nb.quantized_matmul(y1, *d2, True, 64, 4)
-    _, ref1 = oracle.qmm(x, *w1, 4, 64, want_f32=True)
-    assert_close(host_u16(y1), ref1, "chained stage 1")
-    _, ref2 = oracle.qmm(host_u16(y1), *w2, 4, 64, want_f32=True)
+    assert_close(host_u16(y1), oracle.qmm(x, *w1, 4, 64), "chained stage 1")
+    ref2 = oracle.qmm(host_u16(y1), *w2, 4, 64)
     assert_close(host_u16(y2), ref2, "chained stage 2")
