@@ -142,6 +142,30 @@ int nq_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I,
                   int group_size, void *workspace, size_t workspace_bytes,
                   uint16_t *y, void *stream);
 
+/* nq_moe_switch without a workspace argument, for callers that cannot
+ * allocate device memory themselves (an FFI host or a runtime that only
+ * hands over the tensors it owns and exposes no allocator).  No counterpart
+ * in the reference: it exists for those callers only.
+ * Same arguments and result as nq_moe_switch; the scratch comes from a
+ * static 4 MiB block inside the library (4,194,304 bytes; every GPU that
+ * loads the library keeps that block until the process exits), so calls
+ * whose nq_moe_workspace_size() exceeds it fail with NQ_INVALID_INPUT (at
+ * the Qwen3-30B-A3B layer dims that allows up to ~50 tokens per call).  The
+ * call allocates nothing.  The first call on a device looks up the block's
+ * address (cudaGetSymbolAddress); make that first call before any stream
+ * capture.  All calls on a device share the one block and it keeps the last
+ * call's contents (the parts that must start at zero are cleared by each
+ * call): calls that overlap on the GPU -- on different streams, or from
+ * different threads -- race on it, so serialise them. */
+int nq_moe_switch_static(const uint16_t *x, int64_t T, int64_t H, int64_t I,
+                         int64_t E, int64_t top_k, const int32_t *topk_idx,
+                         const float *topk_scores, const uint32_t *gate_w,
+                         const uint16_t *gate_s, const uint16_t *gate_b,
+                         const uint32_t *up_w, const uint16_t *up_s,
+                         const uint16_t *up_b, const uint32_t *down_w,
+                         const uint16_t *down_s, const uint16_t *down_b,
+                         int bits, int group_size, uint16_t *y, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,6 +34,8 @@ SIGNATURES = {
     "nq_moe_workspace_size": (U64, [I64, I64, I64, I64, I64]),
     "nq_moe_switch": (I, [P, I64, I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, P, I, I, P,
                           U64, P, P]),
+    "nq_moe_switch_static": (I, [P, I64, I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, P, I,
+                                 I, P, P]),
 }
 
 

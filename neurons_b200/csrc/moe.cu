@@ -6,7 +6,10 @@
 // (router :36-48, gather_qmm :69-74, SwiGLU :71, weighted sum :77-78), batched
 // over T tokens instead of the per-token loop at :479-486.
 #include <algorithm>
+#include <mutex>
+#include <string>
 
+#include "nq.h"
 #include "nq_common.cuh"
 #include "nq_internal.h"
 
@@ -270,3 +273,89 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
 }
 
 }  // namespace nq
+
+// ---------------------------------------------------------------------------
+// nq_moe_switch_static: the switch step without a caller-provided workspace.
+//
+// Some callers cannot allocate device memory on their own: a runtime that
+// hands the library only the tensors it already owns (a pre-planned memory
+// arena, an embedding through an FFI that exposes no allocator), or a caller
+// that must not trigger an allocation while it runs.  For them the scratch
+// that nq_moe_switch takes as `workspace` lives instead in the array below,
+// a fixed-size block in the library's own device memory.  Every device that
+// loads the library holds it until the process exits.
+//
+// The array's name is only meaningful to device code.  In host code it is a
+// stand-in symbol, not a device address, so the host looks up the real
+// address once per device with cudaGetSymbolAddress (with that device
+// current) and passes that address to the kernels.
+// ---------------------------------------------------------------------------
+namespace nq {
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;  // 4 MiB
+static __device__ __align__(256) unsigned char g_moe_scratch[kStaticScratchBytes];
+
+constexpr int kScratchMaxDevices = 64;
+void *g_scratch_ptr[kScratchMaxDevices];
+std::mutex g_scratch_mu;
+
+// Address of g_moe_scratch on the current device; the first call on a device
+// performs the lookup.  Returns the CUDA error of the lookup.
+cudaError_t static_scratch(void **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kScratchMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_scratch_ptr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_moe_scratch);
+        if (e != cudaSuccess) return e;
+        g_scratch_ptr[dev] = p;
+    }
+    *out = g_scratch_ptr[dev];
+    return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace nq
+
+static int static_fail(int status, const std::string &msg) {
+    nq::set_error(msg);
+    return status;
+}
+
+extern "C" int nq_moe_switch_static(const uint16_t *x, int64_t T, int64_t H, int64_t I,
+                                    int64_t E, int64_t top_k, const int32_t *topk_idx,
+                                    const float *topk_scores, const uint32_t *gate_w,
+                                    const uint16_t *gate_s, const uint16_t *gate_b,
+                                    const uint32_t *up_w, const uint16_t *up_s,
+                                    const uint16_t *up_b, const uint32_t *down_w,
+                                    const uint16_t *down_s, const uint16_t *down_b, int bits,
+                                    int group_size, uint16_t *y, void *stream) {
+    if (T < 0 || E <= 0 || E > 1024 || top_k <= 0 || top_k > 32 || top_k > E || H <= 0 || I <= 0)
+        return static_fail(NQ_INVALID_INPUT,
+                           "nq_moe_switch_static: need 0 < top_k <= min(E, 32), E <= 1024, "
+                           "H > 0, I > 0");
+    const size_t need = nq::moe_workspace_bytes(T, E, top_k, H, I);
+    if (need > nq::kStaticScratchBytes)
+        return static_fail(NQ_INVALID_INPUT,
+                           "nq_moe_switch_static: this call needs " + std::to_string(need) +
+                               " bytes of scratch but the library's static scratch holds " +
+                               std::to_string(nq::kStaticScratchBytes) +
+                               " bytes; pass fewer tokens per call, or use nq_moe_switch "
+                               "with a caller-provided workspace");
+    if (nq_device_count() == 0)
+        return static_fail(NQ_BACKEND_NOT_AVAILABLE, "nq_moe_switch_static: no CUDA device");
+    void *scratch = nullptr;
+    const cudaError_t e = nq::static_scratch(&scratch);
+    if (e != cudaSuccess)
+        return static_fail(NQ_COMPUTE_ERROR,
+                           std::string("nq_moe_switch_static: cudaGetSymbolAddress failed: ") +
+                               cudaGetErrorString(e));
+    // The same validation and kernels as nq_moe_switch, on the static block.
+    return nq_moe_switch(x, T, H, I, E, top_k, topk_idx, topk_scores, gate_w, gate_s, gate_b,
+                         up_w, up_s, up_b, down_w, down_s, down_b, bits, group_size, scratch,
+                         nq::kStaticScratchBytes, y, stream);
+}
