@@ -31,9 +31,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -83,53 +81,56 @@ def ncu_traffic(workload):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason sampling during the timed region."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons of one GPU, sampled every 5 ms by NVML from a
+    background thread while the timed region runs."""
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
-        self.proc = None
-        self.file = None
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
 
     def start(self):
+        import threading
         try:
-            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=self.file, stderr=subprocess.DEVNULL)
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
         except Exception:
-            self.proc = None
+            return
+        names = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+                 "sw_power_cap": 0x4}
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append(float(pynvml.nvmlDeviceGetClockInfo(
+                        h, pynvml.NVML_CLOCK_SM)))
+                    r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    for n, bit in names.items():
+                        if r & bit:
+                            self.reasons.add(n)
+                except Exception:
+                    pass
+                self._stop.wait(0.005)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
 
     def stop(self):
-        if self.proc is None:
+        if self._thread is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.file.flush()
-        rows = []
-        with open(self.file.name) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) == 8 and parts[1].replace(".", "").isdigit():
-                    rows.append(parts)
-        os.unlink(self.file.name)
-        if not rows:
+        self._stop.set()
+        self._thread.join()
+        if not self.samples:
             return None
-        sm = [float(r[1]) for r in rows]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            for name, v in zip(names, r[4:8]):
-                if v.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]),
-                "samples": len(rows), "reasons": sorted(reasons)}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "samples": len(self.samples), "reasons": sorted(self.reasons),
+                "source": "NVML, 5 ms period, during the timed region"}
 
 
 def dist_setup(n_gpus):
@@ -181,9 +182,15 @@ def make_inputs(M, N, K, sets, seed):
     return out
 
 
-def time_device(M, N, K, steps, warmup, world, seed):
-    """Device-resident inputs; returns (seconds for `steps` launches max over ranks,
-    mean per-launch event duration of this rank, sets used)."""
+def time_device(M, N, K, steps, warmup, world, seed, clocks=None):
+    """Device-resident inputs.  Returns (seconds for `steps` launches, max over
+    ranks; mean seconds per launch on this rank; input sets used).
+
+    Prefill-size steps are launched from the host one by one (the host runs far
+    ahead of 0.1 ms kernels).  Decode-size steps (a few microseconds) are
+    captured in one CUDA graph of `steps` launches and replayed, so that host
+    submission is not part of what is timed -- the same way a decode loop
+    replays a captured step."""
     import torch
     import neurons_b200 as nb
     per_set = algo_bytes(M, N, K) + M * N * 2
@@ -195,25 +202,37 @@ def time_device(M, N, K, steps, warmup, world, seed):
         x, wq, s, b, y = data[i % sets]
         nb.quantized_matmul(x, wq, s, b, True, GS, BITS, out=y)
     torch.cuda.synchronize()
+    graph = None
+    if M <= 32:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(steps):
+                x, wq, s, b, y = data[i % sets]
+                nb.quantized_matmul(x, wq, s, b, True, GS, BITS, out=y)
+        for _ in range(max(1, warmup // steps + 1)):
+            graph.replay()
+        torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(steps)]
+    if clocks is not None:
+        clocks.start()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
-    for i in range(steps):
-        x, wq, s, b, y = data[i % sets]
-        ev[i][0].record(stream)
-        nb.quantized_matmul(x, wq, s, b, True, GS, BITS, out=y)
-        ev[i][1].record(stream)
+    if graph is not None:
+        graph.replay()
+    else:
+        for i in range(steps):
+            x, wq, s, b, y = data[i % sets]
+            nb.quantized_matmul(x, wq, s, b, True, GS, BITS, out=y)
     t1.record(stream)
     torch.cuda.synchronize()
+    clk = clocks.stop() if clocks is not None else None
     barrier(world)
     total = t0.elapsed_time(t1) / 1e3
-    per_launch = statistics.mean(a.elapsed_time(b) for a, b in ev) / 1e3
     assert nb.take_device_error() == 0
-    return max_over_ranks(total, world), per_launch, sets
+    del graph
+    return max_over_ranks(total, world), total / steps, sets, clk
 
 
 def time_e2e(M, N, K, steps, warmup, world, seed):
@@ -283,10 +302,8 @@ def ours(args):
     wl = WORKLOADS[args.workload]
     M, N, K = wl["M"], wl["N"], wl["K"]
     pk = peaks()
-    clocks = ClockSampler(local)
-    clocks.start()
-    t_dev, per_launch, sets = time_device(M, N, K, args.steps, args.warmup, world, seed=rank)
-    clk = clocks.stop()
+    t_dev, per_launch, sets, clk = time_device(M, N, K, args.steps, args.warmup, world,
+                                               seed=rank, clocks=ClockSampler(local))
     flops, byts = algo_flops(M, N, K), algo_bytes(M, N, K)
     launches = args.steps
     if M > 1:
@@ -317,20 +334,21 @@ def ours(args):
             "roofline": roof, "gpu_launches": launches, "clocks": clk}
     if args.workload != "decode" and not args.no_decode:
         d = WORKLOADS["decode"]
-        dsteps = max(50, args.steps * 10)
-        t_d, pl_d, _ = time_device(d["M"], d["N"], d["K"], dsteps, max(args.warmup, 10), world,
-                                   seed=rank + 100)
+        dsteps = 2000
+        t_d, pl_d, _, _ = time_device(d["M"], d["N"], d["K"], dsteps, max(args.warmup, 10), world,
+                                      seed=rank + 100)
         db = algo_bytes(d["M"], d["N"], d["K"])
         line["decode"] = {"workload": "decode M=1 N=K=4096", "unit": "GB/s",
                           "value": world * db * dsteps / t_d / 1e9,
                           "kernel_gbs": db / pl_d / 1e9, "frac": db / pl_d / 1e9 / pk["hbm_gbs"],
                           "us_per_launch": pl_d * 1e6, "algorithmic_bytes_per_launch": db}
         line["gpu_launches"] += dsteps
-    t_e, h2d, d2h = time_e2e(M, N, K, args.steps, args.warmup, world, seed=rank)
-    e2e_val = world * (flops if M > 1 else byts) * args.steps / t_e / (1e12 if M > 1 else 1e9)
+    t_e, h2d, d2h = time_e2e(M, N, K, min(args.steps, 50), args.warmup, world, seed=rank)
+    e2e_val = world * (flops if M > 1 else byts) * min(args.steps, 50) / t_e / (
+        1e12 if M > 1 else 1e9)
     line["e2e"] = {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": h2d,
                    "d2h_bytes_per_step": d2h}
-    line["gpu_launches"] += args.steps
+    line["gpu_launches"] += min(args.steps, 50)
     if rank == 0 and world == 1 and not args.no_cpu:
         cb = cpu_baseline(M, N, K)
         line["cpu_baseline"] = {
@@ -377,7 +395,7 @@ def reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="prefill", choices=sorted(WORKLOADS))

@@ -3,23 +3,26 @@
 //   y[m, n] = sum_k x[m, k] * w_hat[n, k]   (w_hat = MLX dequantized bf16)
 //
 // Tile: 128 weight rows (the UMMA M side) x BM tokens (the UMMA N side) per
-// CTA, K consumed 64 codes per pipeline stage.  Roles (10 warps):
-//   warp 8      TMA producer: per stage one box of activations
+// CTA, K consumed 64 codes per pipeline stage.  Roles (18 warps):
+//   warp 16     TMA producer: per stage one box of activations
 //               [BM rows x 64 bf16] (128-byte swizzle, the canonical K-major
 //               UMMA layout) and one box of packed codes [128 rows x 32 or
 //               64 bytes] (32/64-byte swizzle so that the dequant reads are
 //               bank-conflict free);
-//   warps 0..7  dequantizers: lane r of warp w owns weight row 32*(w%4)+r and
-//               half w/4 of the stage's 64 codes; the codes become exact MLX
-//               bf16 values in registers and go straight into tensor memory
-//               with tcgen05.st -- the weights are the MMA's A operand *in
-//               TMEM*, so they never round-trip through shared memory;
-//   warp 9      TMEM allocator and the single MMA-issuing thread:
+//   warps 0..15 dequantizers: lane r of warp w owns weight row 32*(w%4)+r,
+//               half (w/4)%2 of the stage's 64 codes, and the stages of parity
+//               w/8 (two stages are dequantized at once, so the per-stage
+//               latency of the smem read -> dequant -> tcgen05.st chain is
+//               hidden behind the MMA of the previous stage); the codes become
+//               exact MLX bf16 values in registers and go straight into tensor
+//               memory with tcgen05.st -- the weights are the MMA's A operand
+//               *in TMEM*, so they never round-trip through shared memory;
+//   warp 17     TMEM allocator and the single MMA-issuing thread:
 //               tcgen05.mma.cta_group::1.kind::f16, A from TMEM, B (tokens)
 //               from shared memory, fp32 accumulator (128 lanes x BM columns)
 //               in TMEM; tcgen05.commit releases stages back to the producer.
-//   Epilogue: warps 0..7 read the accumulator with tcgen05.ld (lane = weight
-//   row, column = token) and store bf16 y.
+//   Epilogue: warps 0..15 read the accumulator with tcgen05.ld (lane = weight
+//   row, column = token; a quarter of the columns each) and store bf16 y.
 // Every mbarrier wait is bounded; on a timeout the CTA raises the device
 // error word, stops issuing work, lets in-flight operations drain and frees
 // its TMEM before returning.
@@ -35,10 +38,11 @@ namespace {
 
 constexpr int kBlockW = 128;     // weight rows per CTA (UMMA M)
 constexpr int kBlockK = 64;      // codes per stage
-constexpr int kDequantWarps = 8;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kThreads = 320;
+constexpr int kDequantWarps = 16;
+constexpr int kStageArrivals = 8;   // dequant warps working on any one stage
+constexpr int kProducerWarp = 16;
+constexpr int kMmaWarp = 17;
+constexpr int kThreads = 576;
 
 template <int BITS, int BM>
 struct TcCfg {
@@ -55,7 +59,7 @@ struct TcCfg {
 
 struct TcParams {
     int64_t M, N, K, x_ld, y_ld;
-    int gs;
+    int gs_shift;  // log2(group size)
     int num_kb;
     const uint16_t *s, *b;
     uint16_t *y;
@@ -90,7 +94,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *ws = smem + S * Cfg::kXStageBytes;       // S x [128][32|64 B]
     uint64_t *bars = reinterpret_cast<uint64_t *>(ws + S * Cfg::kWStageBytes);
     uint64_t *full = bars;            // TMA landed (x + w)
-    uint64_t *empty = bars + S;       // stage free: MMA done (1) + dequant read (8)
+    uint64_t *empty = bars + S;       // stage free: MMA done (1) + dequant read (8 warps)
     uint64_t *afull = bars + 2 * S;   // A written to TMEM (8 warps)
     uint64_t *accfull = bars + 3 * S; // accumulator complete
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * S + 1);
@@ -105,8 +109,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1 + kDequantWarps);
-            mbar_init(&afull[s], kDequantWarps);
+            mbar_init(&empty[s], 1 + kStageArrivals);
+            mbar_init(&afull[s], kStageArrivals);
         }
         mbar_init(accfull, 1);
         *abort = 0;
@@ -162,27 +166,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ------------------------------------------------ dequantizers
         const int q = warp & 3;          // TMEM lane quadrant
-        const int h = warp >> 2;         // which 32 codes of the stage
+        const int h = (warp >> 2) & 1;   // which 32 codes of the stage
+        const int par = warp >> 3;       // which stages: kb % 2 == par
         const int r = q * 32 + lane;     // weight row inside the tile
         const int64_t n = n0 + r;
         const bool row_ok = n < prm.N;
-        const int64_t G = prm.K / prm.gs;
+        const int64_t G = prm.K >> prm.gs_shift;
         const uint16_t *srow = prm.s + (row_ok ? n : 0) * G;
         const uint16_t *brow = prm.b + (row_ok ? n : 0) * G;
         auto load_sb = [&](int kb, uint16_t &sv, uint16_t &bv) {
-            const int64_t k = (int64_t)kb * kBlockK + 32 * h;
+            const int k = kb * kBlockK + 32 * h;
             sv = 0;
             bv = 0;
             if (row_ok && kb < num_kb && k < prm.K) {
-                sv = srow[k / prm.gs];
-                bv = brow[k / prm.gs];
+                sv = srow[k >> prm.gs_shift];
+                bv = brow[k >> prm.gs_shift];
             }
         };
         uint16_t s_cur, b_cur, s_nxt, b_nxt;
-        load_sb(0, s_cur, b_cur);
-        load_sb(1, s_nxt, b_nxt);
+        load_sb(par, s_cur, b_cur);
+        load_sb(par + 2, s_nxt, b_nxt);
         const uint32_t t_lane = (uint32_t)(q * 32) << 16;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = par; kb < num_kb; kb += 2) {
             const int s = kb % S;
             const uint32_t ph = (uint32_t)(kb / S) & 1u;
             if (!wait_or_abort(&full[s], ph, abort, prm.err)) break;
@@ -231,19 +236,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(&afull[s]);
             s_cur = s_nxt;
             b_cur = b_nxt;
-            load_sb(kb + 2, s_nxt, b_nxt);
+            load_sb(kb + 4, s_nxt, b_nxt);
         }
         // ------------------------------------------------ epilogue
         if (wait_or_abort(accfull, 0, abort, prm.err) && !*abort) {
             tc_fence_after();
             const int64_t nrow = n0 + r;
-            for (int c0 = h * (BM / 2); c0 < (h + 1) * (BM / 2); c0 += 32) {
-                uint32_t acc[32];
-                tmem_ld_32x32b_x32(tmem_base + t_lane + (uint32_t)c0, acc);
+            const int part = warp >> 2;  // quarter of the accumulator columns
+            for (int c0 = part * (BM / 4); c0 < (part + 1) * (BM / 4); c0 += 16) {
+                uint32_t acc[16];
+                tmem_ld_32x32b_x16(tmem_base + t_lane + (uint32_t)c0, acc);
                 tmem_ld_wait();
                 if (nrow < prm.N) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
+                    for (int j = 0; j < 16; ++j) {
                         const int64_t m = m0 + c0 + j;
                         if (m < prm.M)
                             prm.y[m * prm.y_ld + nrow] = f32_to_bf16(__uint_as_float(acc[j]));
@@ -322,7 +328,7 @@ cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
     prm.K = a.K;
     prm.x_ld = a.x_ld;
     prm.y_ld = a.y_ld;
-    prm.gs = a.gs;
+    prm.gs_shift = a.gs == 32 ? 5 : (a.gs == 64 ? 6 : 7);
     prm.num_kb = (int)((a.K + kBlockK - 1) / kBlockK);
     prm.s = a.s;
     prm.b = a.b;

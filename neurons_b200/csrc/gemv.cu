@@ -40,7 +40,7 @@ struct GemvParams {
     const uint32_t *w, *w2;
     const uint16_t *s, *b, *s2, *b2;
     int64_t N, K, Kw, G;  // out rows, in features, words per row, groups per row
-    int gs;
+    int gs_shift;         // log2(group size): group sizes are 32, 64 or 128
     const uint16_t *x;
     int64_t x_ld;
     int P, M, E, x_batch;
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(256) qgemv_kernel(const GemvParams prm) {
                 const int kb = kb0 + u;
                 const int64_t wbase = (int64_t)kb * 16 + 4 * c;
                 kv[u] = kb < kb_hi && wbase < prm.Kw;
-                const int64_t grp = (wbase * kCodesPerWord) / prm.gs;
+                const int64_t grp = (wbase * kCodesPerWord) >> prm.gs_shift;
 #pragma unroll
                 for (int a = 0; a < NACC; ++a) {
                     const uint32_t *W = a ? prm.w2 : prm.w;
@@ -399,7 +399,7 @@ cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
     prm.K = q.K;
     prm.Kw = q.K * q.bits / 32;
     prm.G = q.K / q.gs;
-    prm.gs = q.gs;
+    prm.gs_shift = q.gs == 32 ? 5 : (q.gs == 64 ? 6 : 7);
     prm.x = q.x;
     prm.x_ld = q.x_ld;
     prm.P = q.P;
