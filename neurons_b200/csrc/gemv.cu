@@ -49,7 +49,9 @@ struct GemvParams {
     void *y;
     int64_t y_ld;
     int out_f32, swiglu;
-    int kb_total;
+    int kb_total;   // k-blocks per row (16 words each), the last one possibly partial
+    int kb_full;    // complete k-blocks per row
+    int s_cta;      // K slices handled by the warps of one CTA (1, 2 or 4)
     unsigned int *err;
 };
 
@@ -90,73 +92,174 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-constexpr int kUnroll = 2;  // k-blocks whose weight loads are in flight together
+// Registers of one k-block of work for one warp: RT row tiles x rows {g, g+8}
+// x NACC weight sets.  Scales and biases are kept as zero-extended 16-bit values.
+template <int RT, int NACC>
+struct KBlock {
+    uint4 w[RT][2][NACC];
+    uint32_t s[RT][2][NACC], b[RT][2][NACC];
+};
 
-// One k-block of one weight matrix against NT token tiles.
-//   4 bits: word i of this lane holds codes k0+8i .. k0+8i+7; the two mma
-//   steps use pairs (q0,q4),(q1,q5) and (q2,q6),(q3,q7), the activations the
-//   same pairs of x.
-//   8 bits: word i holds codes k0+4i .. k0+4i+3; one mma step.
-template <int BITS, int NT>
-__device__ __forceinline__ void kblock_mma(float (&acc)[NT][4], const uint4 &wa, const uint4 &wb,
-                                           uint16_t sa, uint16_t ba, uint16_t sb, uint16_t bb,
-                                           const uint16_t *const (&xrow)[NT], int64_t kcode0,
-                                           bool kvalid) {
-    const uint32_t wA[4] = {wa.x, wa.y, wa.z, wa.w};
-    const uint32_t wB[4] = {wb.x, wb.y, wb.z, wb.w};
+// Row pointers of one warp (per row tile, row g / g+8, weight set).
+template <int RT, int NACC>
+struct RowPtrs {
+    const uint4 *w[RT][2][NACC];      // packed words of the row, advanced to this lane's chunk
+    const uint16_t *s[RT][2][NACC];   // group scales of the row
+    const uint16_t *b[RT][2][NACC];
+};
+
+__device__ __forceinline__ uint32_t ldg_u16z(const uint16_t *p) {
+    uint16_t r;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+    return (uint32_t)r;
+}
+
+// Loads one k-block.  kb is the k-block index; grp the group index of this
+// lane's codes in it.  No predicates: every row pointer is valid memory.
+template <int RT, int NACC>
+__device__ __forceinline__ void load_kblock(KBlock<RT, NACC> &blk, const RowPtrs<RT, NACC> &rp,
+                                            int kb, int grp) {
+#pragma unroll
+    for (int t = 0; t < RT; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int a = 0; a < NACC; ++a) {
+                blk.w[t][h][a] = ldg_stream16(rp.w[t][h][a] + (size_t)kb * 4);
+                blk.s[t][h][a] = ldg_u16z(rp.s[t][h][a] + grp);
+                blk.b[t][h][a] = ldg_u16z(rp.b[t][h][a] + grp);
+            }
+}
+
+// The tail k-block (fewer than 16 words left in every row): chunks past the
+// end of the row get zero codes and zero scale/bias, i.e. weight 0.
+template <int RT, int NACC>
+__device__ __forceinline__ void load_kblock_tail(KBlock<RT, NACC> &blk,
+                                                 const RowPtrs<RT, NACC> &rp, int kb, int grp,
+                                                 bool valid) {
+#pragma unroll
+    for (int t = 0; t < RT; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int a = 0; a < NACC; ++a) {
+                blk.w[t][h][a] = make_uint4(0, 0, 0, 0);
+                blk.s[t][h][a] = blk.b[t][h][a] = 0;
+                if (valid) {
+                    blk.w[t][h][a] = ldg_stream16(rp.w[t][h][a] + (size_t)kb * 4);
+                    blk.s[t][h][a] = ldg_u16z(rp.s[t][h][a] + grp);
+                    blk.b[t][h][a] = ldg_u16z(rp.b[t][h][a] + grp);
+                }
+            }
+}
+
+// Dequantizes and multiplies one k-block.  xoff: element offset of this lane's
+// codes in the activation rows (k of its first code); xrow[nt]: the token row
+// this lane supplies to n-tile nt.
+//   4 bits: word i holds codes xoff+8i .. +7; the two mma steps use the pairs
+//   (q0,q4),(q1,q5) and (q2,q6),(q3,q7), the activations the same pairs of x.
+//   8 bits: word i holds codes xoff+4i .. +3; one mma step.
+template <int BITS, int NT, int RT, int NACC>
+__device__ __forceinline__ void compute_kblock(float (&acc)[RT][NACC][NT][4],
+                                               const KBlock<RT, NACC> &blk,
+                                               const uint16_t *const (&xrow)[NT], int xoff) {
     if constexpr (BITS == 4) {
-        const Dq4 da = make_dq4(sa, ba), db = make_dq4(sb, bb);
+        Dq4 dq[RT][2][NACC];
+#pragma unroll
+        for (int t = 0; t < RT; ++t)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int a = 0; a < NACC; ++a) {
+                    Dq4 &d = dq[t][h][a];
+                    d.s2 = prmt(blk.s[t][h][a], 0u, 0x1010u);
+                    d.b2 = prmt(blk.b[t][h][a], 0u, 0x1010u);
+                    d.n2 = bf2_fma(d.s2, 0xC300C300u, 0x80008000u);  // exact -128*s
+                }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const uint32_t a00 = dq4_pair(q4_pair_biased(wA[i], 0), da);
-            const uint32_t a01 = dq4_pair(q4_pair_biased(wB[i], 0), db);
-            const uint32_t a02 = dq4_pair(q4_pair_biased(wA[i], 1), da);
-            const uint32_t a03 = dq4_pair(q4_pair_biased(wB[i], 1), db);
-            const uint32_t a10 = dq4_pair(q4_pair_biased(wA[i], 2), da);
-            const uint32_t a11 = dq4_pair(q4_pair_biased(wB[i], 2), db);
-            const uint32_t a12 = dq4_pair(q4_pair_biased(wA[i], 3), da);
-            const uint32_t a13 = dq4_pair(q4_pair_biased(wB[i], 3), db);
+            uint32_t bx[NT][4];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                uint4 xv = make_uint4(0, 0, 0, 0);
-                if (xrow[nt] != nullptr && kvalid) xv = ldg16(xrow[nt] + kcode0 + 8 * i);
-                // (x0,x4) (x1,x5) (x2,x6) (x3,x7)
-                const uint32_t b00 = prmt(xv.x, xv.z, 0x5410u), b01 = prmt(xv.x, xv.z, 0x7632u);
-                const uint32_t b10 = prmt(xv.y, xv.w, 0x5410u), b11 = prmt(xv.y, xv.w, 0x7632u);
-                mma16816(acc[nt], a00, a01, a02, a03, b00, b01);
-                mma16816(acc[nt], a10, a11, a12, a13, b10, b11);
+                const uint4 xv = ldg16(xrow[nt] + xoff + 8 * i);
+                bx[nt][0] = prmt(xv.x, xv.z, 0x5410u);  // (x0, x4)
+                bx[nt][1] = prmt(xv.x, xv.z, 0x7632u);  // (x1, x5)
+                bx[nt][2] = prmt(xv.y, xv.w, 0x5410u);  // (x2, x6)
+                bx[nt][3] = prmt(xv.y, xv.w, 0x7632u);  // (x3, x7)
             }
+#pragma unroll
+            for (int t = 0; t < RT; ++t)
+#pragma unroll
+                for (int a = 0; a < NACC; ++a) {
+                    const uint32_t wa = (&blk.w[t][0][a].x)[i];
+                    const uint32_t wb = (&blk.w[t][1][a].x)[i];
+                    const uint32_t wa4 = wa >> 4, wb4 = wb >> 4;
+                    const uint32_t a0 = dq4_pair(lop3_and_or(wa, 0x000F000Fu, 0x43004300u), dq[t][0][a]);
+                    const uint32_t a1 = dq4_pair(lop3_and_or(wb, 0x000F000Fu, 0x43004300u), dq[t][1][a]);
+                    const uint32_t a2 = dq4_pair(lop3_and_or(wa4, 0x000F000Fu, 0x43004300u), dq[t][0][a]);
+                    const uint32_t a3 = dq4_pair(lop3_and_or(wb4, 0x000F000Fu, 0x43004300u), dq[t][1][a]);
+                    const uint32_t c0 = dq4_pair(lop3_and_or(wa >> 8, 0x000F000Fu, 0x43004300u), dq[t][0][a]);
+                    const uint32_t c1 = dq4_pair(lop3_and_or(wb >> 8, 0x000F000Fu, 0x43004300u), dq[t][1][a]);
+                    const uint32_t c2 = dq4_pair(lop3_and_or(wa4 >> 8, 0x000F000Fu, 0x43004300u), dq[t][0][a]);
+                    const uint32_t c3 = dq4_pair(lop3_and_or(wb4 >> 8, 0x000F000Fu, 0x43004300u), dq[t][1][a]);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        mma16816(acc[t][a][nt], a0, a1, a2, a3, bx[nt][0], bx[nt][1]);
+                        mma16816(acc[t][a][nt], c0, c1, c2, c3, bx[nt][2], bx[nt][3]);
+                    }
+                }
         }
     } else {
-        const Dq8 da = make_dq8(sa, ba), db = make_dq8(sb, bb);
+        Dq8 dq[RT][2][NACC];
+#pragma unroll
+        for (int t = 0; t < RT; ++t)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int a = 0; a < NACC; ++a)
+                    dq[t][h][a] = make_dq8((uint16_t)blk.s[t][h][a], (uint16_t)blk.b[t][h][a]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const uint32_t a0 = dq8_pair(wA[i], 0, 1, da);
-            const uint32_t a1 = dq8_pair(wB[i], 0, 1, db);
-            const uint32_t a2 = dq8_pair(wA[i], 2, 3, da);
-            const uint32_t a3 = dq8_pair(wB[i], 2, 3, db);
+            uint2 bx[NT];
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                uint2 xv = make_uint2(0, 0);
-                if (xrow[nt] != nullptr && kvalid) xv = ldg8(xrow[nt] + kcode0 + 4 * i);
-                mma16816(acc[nt], a0, a1, a2, a3, xv.x, xv.y);
-            }
+            for (int nt = 0; nt < NT; ++nt) bx[nt] = ldg8(xrow[nt] + xoff + 4 * i);
+#pragma unroll
+            for (int t = 0; t < RT; ++t)
+#pragma unroll
+                for (int a = 0; a < NACC; ++a) {
+                    const uint32_t wa = (&blk.w[t][0][a].x)[i];
+                    const uint32_t wb = (&blk.w[t][1][a].x)[i];
+                    const uint32_t a0 = dq8_pair(wa, 0, 1, dq[t][0][a]);
+                    const uint32_t a1 = dq8_pair(wb, 0, 1, dq[t][1][a]);
+                    const uint32_t a2 = dq8_pair(wa, 2, 3, dq[t][0][a]);
+                    const uint32_t a3 = dq8_pair(wb, 2, 3, dq[t][1][a]);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+                        mma16816(acc[t][a][nt], a0, a1, a2, a3, bx[nt].x, bx[nt].y);
+                }
         }
     }
 }
 
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
 
-template <int BITS, int NT, bool DUAL>
-__global__ void __launch_bounds__(256) qgemv_kernel(const GemvParams prm) {
+// Launch geometry chosen on the host (see launch_gemv):
+//   blockDim 128 (4 warps).  A warp owns RT 16-row tiles ("a row group") of one
+//   problem and one K slice.  s_cta warps of a CTA share a row group and split
+//   its K (reduced in shared memory); gridDim.y CTAs of a cluster split it
+//   further (reduced through distributed shared memory).
+template <int BITS, int NT, int RT, bool DUAL>
+__global__ void __launch_bounds__(128) qgemv_kernel(const GemvParams prm) {
     constexpr int NACC = DUAL ? 2 : 1;
-    extern __shared__ float red[];  // [warps][NACC][NT][4][32]
+    constexpr int kCodesPerKb = 16 * 32 / BITS;     // codes of one k-block (per row)
+    constexpr int kCodesPerLane = 4 * 32 / BITS;    // codes of one lane's 16 bytes
+    extern __shared__ float red[];                  // [4 warps][RT][NACC][NT][4][32]
 
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    const int warps = blockDim.x >> 5;
     const int g = lane >> 2, c = lane & 3;
     const int p = blockIdx.z;
+    const int s_cta = prm.s_cta;
 
     pdl_launch_dependents();
 
@@ -179,183 +282,182 @@ __global__ void __launch_bounds__(256) qgemv_kernel(const GemvParams prm) {
     }
     if (bad && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0)
         atomicOr(prm.err, kErrBadIndex);
-    if (Mp <= 0) return;  // uniform over the cluster (same problem)
+    if (Mp <= 0) return;  // uniform over the CTA and the cluster (same problem)
 
-    const int64_t n0 = (int64_t)blockIdx.x * 16;
-    const int64_t ra = n0 + g, rb = n0 + g + 8;
-    const bool va = ra < prm.N && !bad, vb = rb < prm.N && !bad;
-    const int64_t wrow_a = ((int64_t)e * prm.N + ra) * prm.Kw;
-    const int64_t wrow_b = ((int64_t)e * prm.N + rb) * prm.Kw;
-    const int64_t srow_a = ((int64_t)e * prm.N + ra) * prm.G;
-    const int64_t srow_b = ((int64_t)e * prm.N + rb) * prm.G;
+    const int slice_local = warp % s_cta;
+    const int64_t rg = (int64_t)blockIdx.x * (4 / s_cta) + warp / s_cta;
+    const int ksplit = gridDim.y * s_cta;
+    const int slice = blockIdx.y * s_cta + slice_local;
+    const int kb_lo = (int)(((int64_t)slice * prm.kb_total) / ksplit);
+    const int kb_hi = (int)(((int64_t)(slice + 1) * prm.kb_total) / ksplit);
+    const int kb_full_hi = min(kb_hi, prm.kb_full);
 
-    const int tw = gridDim.y * warps;
-    const int gw = blockIdx.y * warps + warp;
-    const int kb_lo = (int)(((int64_t)gw * prm.kb_total) / tw);
-    const int kb_hi = (int)(((int64_t)(gw + 1) * prm.kb_total) / tw);
-    constexpr int kCodesPerWord = 32 / BITS;
+    // row pointers (rows past N are clamped to N-1: valid memory, never stored)
+    RowPtrs<RT, NACC> rp;
+    int64_t rows[RT][2];
+#pragma unroll
+    for (int t = 0; t < RT; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            rows[t][h] = rg * (16 * RT) + 16 * t + 8 * h + g;
+            const int64_t rc = min(rows[t][h], prm.N - 1) + (int64_t)e * prm.N;
+#pragma unroll
+            for (int a = 0; a < NACC; ++a) {
+                const uint32_t *W = a ? prm.w2 : prm.w;
+                rp.w[t][h][a] = reinterpret_cast<const uint4 *>(W + rc * prm.Kw) + c;
+                rp.s[t][h][a] = (a ? prm.s2 : prm.s) + rc * prm.G;
+                rp.b[t][h][a] = (a ? prm.b2 : prm.b) + rc * prm.G;
+            }
+        }
 
     bool waited = indexed;
-
     for (int m0 = 0; m0 < Mp; m0 += 8 * NT) {
-        float acc[NACC][NT][4];
+        float acc[RT][NACC][NT][4];
 #pragma unroll
-        for (int a = 0; a < NACC; ++a)
+        for (int t = 0; t < RT; ++t)
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
+            for (int a = 0; a < NACC; ++a)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[a][nt][j] = 0.0f;
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[t][a][nt][j] = 0.0f;
 
-        const uint16_t *xrow[NT];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) xrow[nt] = nullptr;
-
-        for (int kb0 = kb_lo; kb0 < kb_hi; kb0 += kUnroll) {
-            uint4 wa[NACC][kUnroll], wb[NACC][kUnroll];
-            uint16_t sa[NACC][kUnroll], ba[NACC][kUnroll], sb[NACC][kUnroll], bb[NACC][kUnroll];
-            bool kv[kUnroll];
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                const int kb = kb0 + u;
-                const int64_t wbase = (int64_t)kb * 16 + 4 * c;
-                kv[u] = kb < kb_hi && wbase < prm.Kw;
-                const int64_t grp = (wbase * kCodesPerWord) >> prm.gs_shift;
-#pragma unroll
-                for (int a = 0; a < NACC; ++a) {
-                    const uint32_t *W = a ? prm.w2 : prm.w;
-                    const uint16_t *S = a ? prm.s2 : prm.s;
-                    const uint16_t *B = a ? prm.b2 : prm.b;
-                    wa[a][u] = make_uint4(0, 0, 0, 0);
-                    wb[a][u] = make_uint4(0, 0, 0, 0);
-                    sa[a][u] = ba[a][u] = sb[a][u] = bb[a][u] = 0;
-                    if (kv[u] && va) {
-                        wa[a][u] = ldg_stream16(W + wrow_a + wbase);
-                        sa[a][u] = ldg_u16(S + srow_a + grp);
-                        ba[a][u] = ldg_u16(B + srow_a + grp);
-                    }
-                    if (kv[u] && vb) {
-                        wb[a][u] = ldg_stream16(W + wrow_b + wbase);
-                        sb[a][u] = ldg_u16(S + srow_b + grp);
-                        bb[a][u] = ldg_u16(B + srow_b + grp);
-                    }
-                }
-            }
+        if (!bad) {
+            const uint16_t *xrow[NT];
+            KBlock<RT, NACC> A, B;
+            int kb = kb_lo;
+            if (kb < kb_full_hi) load_kblock(A, rp, kb, (kb * kCodesPerKb + c * kCodesPerLane) >> prm.gs_shift);
             if (!waited) {
                 pdl_wait();
                 waited = true;
             }
-            // token rows for the B fragments of this pass
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                const int m = m0 + 8 * nt + g;
-                xrow[nt] = nullptr;
-                if (m < Mp) {
-                    const int64_t row = prm.x_rows ? (int64_t)prm.x_rows[off + m]
-                                        : (prm.x_from_offset ? (int64_t)off + m
-                                                             : (int64_t)xi * prm.M + m);
-                    xrow[nt] = prm.x + row * prm.x_ld;
-                }
+                const int m = min(m0 + 8 * nt + g, Mp - 1);
+                const int64_t row = prm.x_rows ? (int64_t)prm.x_rows[off + m]
+                                    : (prm.x_from_offset ? (int64_t)off + m
+                                                         : (int64_t)xi * prm.M + m);
+                xrow[nt] = prm.x + row * prm.x_ld;
             }
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                const int64_t kcode0 = ((int64_t)(kb0 + u) * 16 + 4 * c) * kCodesPerWord;
-#pragma unroll
-                for (int a = 0; a < NACC; ++a)
-                    kblock_mma<BITS, NT>(acc[a], wa[a][u], wb[a][u], sa[a][u], ba[a][u], sb[a][u],
-                                         bb[a][u], xrow, kcode0, kv[u]);
+            // main loop: full k-blocks, double-buffered in registers
+            for (; kb < kb_full_hi; kb += 2) {
+                if (kb + 1 < kb_full_hi)
+                    load_kblock(B, rp, kb + 1, ((kb + 1) * kCodesPerKb + c * kCodesPerLane) >> prm.gs_shift);
+                compute_kblock<BITS, NT, RT, NACC>(acc, A, xrow, kb * kCodesPerKb + c * kCodesPerLane);
+                if (kb + 1 >= kb_full_hi) break;
+                if (kb + 2 < kb_full_hi)
+                    load_kblock(A, rp, kb + 2, ((kb + 2) * kCodesPerKb + c * kCodesPerLane) >> prm.gs_shift);
+                compute_kblock<BITS, NT, RT, NACC>(acc, B, xrow, (kb + 1) * kCodesPerKb + c * kCodesPerLane);
             }
-        }
-        if (!waited) {
+            // the partial last k-block, if this slice holds it
+            if (kb_hi > prm.kb_full) {
+                const int kt = prm.kb_full;
+                const bool valid = (int64_t)kt * 16 + 4 * c + 4 <= prm.Kw;
+                const int code0 = kt * kCodesPerKb + c * kCodesPerLane;
+                load_kblock_tail(A, rp, kt, code0 >> prm.gs_shift, valid);
+                compute_kblock<BITS, NT, RT, NACC>(acc, A, xrow, valid ? code0 : 0);
+            }
+        } else if (!waited) {
             pdl_wait();
             waited = true;
         }
 
-        // ---- reduce over the warps of this CTA
-        float *mine = red + (size_t)warp * NACC * NT * 128;
+        // ---- reduce the K slices of the CTA (shared memory)
+        constexpr int kVals = RT * NACC * NT * 4;
+        if (s_cta > 1) {
+            float *mine = red + (size_t)warp * kVals * 32;
 #pragma unroll
-        for (int a = 0; a < NACC; ++a)
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) mine[((a * NT + nt) * 4 + j) * 32 + lane] = acc[a][nt][j];
-        __syncthreads();
-        if (warp == 0) {
-            for (int w = 1; w < warps; ++w) {
-                const float *o = red + (size_t)w * NACC * NT * 128;
+            for (int t = 0; t < RT; ++t)
 #pragma unroll
                 for (int a = 0; a < NACC; ++a)
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                         for (int j = 0; j < 4; ++j)
-                            acc[a][nt][j] += o[((a * NT + nt) * 4 + j) * 32 + lane];
+                            mine[(((t * NACC + a) * NT + nt) * 4 + j) * 32 + lane] = acc[t][a][nt][j];
+            __syncthreads();
+            if (slice_local == 0) {
+                for (int w = 1; w < s_cta; ++w) {
+                    const float *o = red + (size_t)(warp + w) * kVals * 32;
+#pragma unroll
+                    for (int t = 0; t < RT; ++t)
+#pragma unroll
+                        for (int a = 0; a < NACC; ++a)
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                                for (int j = 0; j < 4; ++j)
+                                    acc[t][a][nt][j] += o[(((t * NACC + a) * NT + nt) * 4 + j) * 32 + lane];
+                }
             }
         }
-        // ---- reduce over the CTAs of the cluster (split K) via DSMEM
+        // ---- reduce across the CTAs of the cluster (distributed shared memory)
         if (gridDim.y > 1) {
             cg::cluster_group cl = cg::this_cluster();
-            __syncthreads();
-            if (warp == 0) {
+            if (s_cta > 1) __syncthreads();
+            float *mine = red + (size_t)warp * kVals * 32;
+            if (slice_local == 0) {
 #pragma unroll
-                for (int a = 0; a < NACC; ++a)
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            red[((a * NT + nt) * 4 + j) * 32 + lane] = acc[a][nt][j];
-            }
-            cl.sync();
-            if (blockIdx.y == 0 && warp == 0) {
-                for (unsigned r = 1; r < gridDim.y; ++r) {
-                    const float *o = cl.map_shared_rank(red, r);
+                for (int t = 0; t < RT; ++t)
 #pragma unroll
                     for (int a = 0; a < NACC; ++a)
 #pragma unroll
                         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                             for (int j = 0; j < 4; ++j)
-                                acc[a][nt][j] += o[((a * NT + nt) * 4 + j) * 32 + lane];
+                                mine[(((t * NACC + a) * NT + nt) * 4 + j) * 32 + lane] = acc[t][a][nt][j];
+            }
+            cl.sync();
+            if (blockIdx.y == 0 && slice_local == 0) {
+                for (unsigned r = 1; r < gridDim.y; ++r) {
+                    const float *o = cl.map_shared_rank(mine, r);
+#pragma unroll
+                    for (int t = 0; t < RT; ++t)
+#pragma unroll
+                        for (int a = 0; a < NACC; ++a)
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                                for (int j = 0; j < 4; ++j)
+                                    acc[t][a][nt][j] += o[(((t * NACC + a) * NT + nt) * 4 + j) * 32 + lane];
                 }
             }
             cl.sync();
         }
         // ---- store
-        if (blockIdx.y == 0 && warp == 0) {
+        if (blockIdx.y == 0 && slice_local == 0) {
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
+            for (int t = 0; t < RT; ++t)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int m = m0 + 8 * nt + 2 * c + (j & 1);
-                    const int64_t n = (j < 2) ? ra : rb;
-                    if (m >= Mp || n >= prm.N) continue;
-                    float v = acc[0][nt][j];
-                    if (DUAL && prm.swiglu) v = silu_f32(v) * acc[NACC - 1][nt][j];
-                    const int64_t row = prm.y_rows ? (int64_t)prm.y_rows[off + m] : (int64_t)off + m;
-                    if (prm.out_f32)
-                        static_cast<float *>(prm.y)[row * prm.y_ld + n] = v;
-                    else
-                        static_cast<uint16_t *>(prm.y)[row * prm.y_ld + n] = f32_to_bf16(v);
-                }
-            }
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int m = m0 + 8 * nt + 2 * c + (j & 1);
+                        const int64_t n = rows[t][j >> 1];
+                        if (m >= Mp || n >= prm.N) continue;
+                        float v = acc[t][0][nt][j];
+                        if (DUAL && prm.swiglu) v = silu_f32(v) * acc[t][NACC - 1][nt][j];
+                        const int64_t row = prm.y_rows ? (int64_t)prm.y_rows[off + m] : (int64_t)off + m;
+                        if (prm.out_f32)
+                            static_cast<float *>(prm.y)[row * prm.y_ld + n] = v;
+                        else
+                            static_cast<uint16_t *>(prm.y)[row * prm.y_ld + n] = f32_to_bf16(v);
+                    }
         }
-        __syncthreads();
+        if (s_cta > 1 && m0 + 8 * NT < Mp) __syncthreads();
     }
 }
 
-template <int BITS, int NT, bool DUAL>
-cudaError_t launch_variant(const GemvParams &prm, dim3 grid, int threads, int cluster,
-                           cudaStream_t stream) {
+template <int BITS, int NT, int RT, bool DUAL>
+cudaError_t launch_variant(const GemvParams &prm, dim3 grid, int cluster, cudaStream_t stream) {
     constexpr int NACC = DUAL ? 2 : 1;
-    const size_t smem = (size_t)(threads / 32) * NACC * NT * 128 * sizeof(float);
-    auto kern = qgemv_kernel<BITS, NT, DUAL>;
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-    }
+    const size_t smem = (prm.s_cta > 1 || cluster > 1)
+                            ? (size_t)4 * RT * NACC * NT * 4 * 32 * sizeof(float)
+                            : 0;
+    auto kern = qgemv_kernel<BITS, NT, RT, DUAL>;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.blockDim = dim3(128, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attrs[2];
@@ -376,13 +478,13 @@ cudaError_t launch_variant(const GemvParams &prm, dim3 grid, int threads, int cl
 }
 
 template <int BITS, bool DUAL>
-cudaError_t dispatch_nt(const GemvParams &prm, int nt, dim3 grid, int threads, int cluster,
-                        cudaStream_t stream) {
-    switch (nt) {
-        case 1: return launch_variant<BITS, 1, DUAL>(prm, grid, threads, cluster, stream);
-        case 2: return launch_variant<BITS, 2, DUAL>(prm, grid, threads, cluster, stream);
-        default: return launch_variant<BITS, 4, DUAL>(prm, grid, threads, cluster, stream);
-    }
+cudaError_t dispatch(const GemvParams &prm, int nt, int rt, dim3 grid, int cluster,
+                     cudaStream_t stream) {
+    if (nt == 1)
+        return rt == 2 ? launch_variant<BITS, 1, 2, DUAL>(prm, grid, cluster, stream)
+                       : launch_variant<BITS, 1, 1, DUAL>(prm, grid, cluster, stream);
+    if (nt == 2) return launch_variant<BITS, 2, 1, DUAL>(prm, grid, cluster, stream);
+    return launch_variant<BITS, 4, 1, DUAL>(prm, grid, cluster, stream);
 }
 
 }  // namespace
@@ -419,28 +521,31 @@ cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
     prm.out_f32 = q.out_f32;
     prm.swiglu = q.swiglu;
     prm.kb_total = (int)((prm.Kw + 15) / 16);
+    prm.kb_full = (int)(prm.Kw / 16);
     prm.err = device_error_word();
 
-    const int64_t row_tiles = (q.N + 15) / 16;
-    const int sms = sm_count();
-    // Warps per CTA and CTAs per cluster (split K): aim for >= 2 CTAs of work
-    // per SM while keeping >= 2 k-blocks per warp.
-    int warps = 8;
-    while (warps > 2 && prm.kb_total < warps * 2) warps >>= 1;
-    int cluster = 1;
-    const int64_t ctas = row_tiles * (int64_t)q.P;
-    while (cluster < 8 && ctas * cluster < 2 * sms &&
-           prm.kb_total >= (int64_t)warps * cluster * 2 * 2)
-        cluster <<= 1;
+    const bool dual = q.w2 != nullptr;
     const int max_m = std::max(1, q.max_m);
     const int nt = max_m <= 8 ? 1 : (max_m <= 16 ? 2 : 4);
-    dim3 grid((unsigned)row_tiles, (unsigned)cluster, (unsigned)q.P);
-    const bool dual = q.w2 != nullptr;
+    const int rt = (!dual && nt == 1 && q.N >= 64) ? 2 : 1;
+    const int64_t row_groups = (q.N + 16 * rt - 1) / (16 * rt);
+    const int64_t tasks = row_groups * (int64_t)q.P;
+    // Split K until there are ~16 warps of work per SM, keeping >= 2 k-blocks
+    // per warp (the register double buffer) and at most 8 CTAs per cluster.
+    const int64_t target = (int64_t)sm_count() * 16;
+    int ksplit = 1;
+    while (ksplit < 32 && tasks * ksplit < target && prm.kb_total >= ksplit * 4) ksplit <<= 1;
+    const int s_cta = std::min(ksplit, 4);
+    const int cluster = ksplit / s_cta;
+    prm.s_cta = s_cta;
+    const int groups_per_cta = 4 / s_cta;
+    dim3 grid((unsigned)((row_groups + groups_per_cta - 1) / groups_per_cta), (unsigned)cluster,
+              (unsigned)q.P);
     if (q.bits == 4)
-        return dual ? dispatch_nt<4, true>(prm, nt, grid, warps * 32, cluster, stream)
-                    : dispatch_nt<4, false>(prm, nt, grid, warps * 32, cluster, stream);
-    return dual ? dispatch_nt<8, true>(prm, nt, grid, warps * 32, cluster, stream)
-                : dispatch_nt<8, false>(prm, nt, grid, warps * 32, cluster, stream);
+        return dual ? dispatch<4, true>(prm, nt, rt, grid, cluster, stream)
+                    : dispatch<4, false>(prm, nt, rt, grid, cluster, stream);
+    return dual ? dispatch<8, true>(prm, nt, rt, grid, cluster, stream)
+                : dispatch<8, false>(prm, nt, rt, grid, cluster, stream);
 }
 
 }  // namespace nq
