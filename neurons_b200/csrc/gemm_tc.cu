@@ -38,8 +38,7 @@ namespace {
 
 constexpr int kBlockW = 128;     // weight rows per CTA (UMMA M)
 constexpr int kBlockK = 64;      // codes per stage
-constexpr int kDequantWarps = 16;
-constexpr int kStageArrivals = 8;   // dequant warps working on any one stage
+constexpr int kStageArrivals = 8;   // of the 16 dequant warps, those working on one stage
 constexpr int kProducerWarp = 16;
 constexpr int kMmaWarp = 17;
 constexpr int kThreads = 576;
@@ -275,6 +274,41 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------- host side
 
+template <int BITS, int BM>
+cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
+    using Cfg = TcCfg<BITS, BM>;
+    CUtensorMap mx, mw;
+    const uint64_t Kw = (uint64_t)a.K * BITS / 32;
+    if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M,
+                     (uint64_t)a.x_ld * 2, kBlockK, BM, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    if (!make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w, Kw, (uint64_t)a.N, Kw * 4,
+                     kBlockK * BITS / 32, kBlockW,
+                     BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
+        return cudaErrorInvalidValue;
+    TcParams prm;
+    prm.M = a.M;
+    prm.N = a.N;
+    prm.K = a.K;
+    prm.x_ld = a.x_ld;
+    prm.y_ld = a.y_ld;
+    prm.gs_shift = a.gs == 32 ? 5 : (a.gs == 64 ? 6 : 7);
+    prm.num_kb = (int)((a.K + kBlockK - 1) / kBlockK);
+    prm.s = a.s;
+    prm.b = a.b;
+    prm.y = a.y;
+    prm.err = device_error_word();
+    auto kern = tc_qgemm_kernel<BITS, BM>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    dim3 grid((unsigned)((a.N + kBlockW - 1) / kBlockW), (unsigned)((a.M + BM - 1) / BM), 1);
+    kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(mx, mw, prm);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                    const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                    const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -310,40 +344,6 @@ bool make_map_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint6
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BITS, int BM>
-cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
-    using Cfg = TcCfg<BITS, BM>;
-    CUtensorMap mx, mw;
-    const uint64_t Kw = (uint64_t)a.K * BITS / 32;
-    if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M,
-                     (uint64_t)a.x_ld * 2, kBlockK, BM, CU_TENSOR_MAP_SWIZZLE_128B))
-        return cudaErrorInvalidValue;
-    if (!make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w, Kw, (uint64_t)a.N, Kw * 4,
-                     kBlockK * BITS / 32, kBlockW,
-                     BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
-        return cudaErrorInvalidValue;
-    TcParams prm;
-    prm.M = a.M;
-    prm.N = a.N;
-    prm.K = a.K;
-    prm.x_ld = a.x_ld;
-    prm.y_ld = a.y_ld;
-    prm.gs_shift = a.gs == 32 ? 5 : (a.gs == 64 ? 6 : 7);
-    prm.num_kb = (int)((a.K + kBlockK - 1) / kBlockK);
-    prm.s = a.s;
-    prm.b = a.b;
-    prm.y = a.y;
-    prm.err = device_error_word();
-    auto kern = tc_qgemm_kernel<BITS, BM>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    dim3 grid((unsigned)((a.N + kBlockW - 1) / kBlockW), (unsigned)((a.M + BM - 1) / BM), 1);
-    kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(mx, mw, prm);
-    return cudaGetLastError();
-}
-
-}  // namespace
 
 bool tc_gemm_supported(const TcGemmArgs &a) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0) return false;

@@ -26,7 +26,10 @@
 //     stream of one with the tail of the previous.
 #include <cooperative_groups.h>
 
+#include <cuda.h>
+
 #include <algorithm>
+#include <mutex>
 
 #include "nq_common.cuh"
 #include "nq_internal.h"
@@ -74,12 +77,6 @@ __device__ __forceinline__ uint4 ldg16(const void *p) {
 __device__ __forceinline__ uint2 ldg8(const void *p) {
     uint2 r;
     asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
-    return r;
-}
-
-__device__ __forceinline__ uint16_t ldg_u16(const uint16_t *p) {
-    uint16_t r;
-    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
     return r;
 }
 
@@ -487,6 +484,316 @@ cudaError_t dispatch(const GemvParams &prm, int nt, int rt, dim3 grid, int clust
     return launch_variant<BITS, 4, 1, DUAL>(prm, grid, cluster, stream);
 }
 
+// ----------------------------------------------------------------------------
+// TMA-fed variant (the default path).  A CTA owns 64 weight rows (4 consumer
+// warps x 16 rows) of one problem and one K slice.  Warp 4 streams the rows'
+// packed words into a 4-stage shared-memory ring with cp.async.bulk.tensor
+// (boxes of 32 words x 64 rows, 128-byte swizzle), so the bytes in flight no
+// longer depend on registers: 32 KB per CTA (64 KB for the gate/up pair).
+// Consumer warps read their rows with 128-bit shared loads (the swizzle keeps
+// them at most 2-way bank conflicted), dequantize and multiply exactly as the
+// register path does, and release each stage right after reading it.
+// ----------------------------------------------------------------------------
+constexpr int kTRows = 64;         // weight rows per CTA
+constexpr int kTStageWords = 32;   // packed words per row per stage (2 k-blocks, 128 B)
+constexpr int kTStages = 4;
+constexpr int kTConsumers = 4;
+
+template <int NACC>
+struct TmaGemvCfg {
+    static constexpr int kSetBytes = kTRows * kTStageWords * 4;   // 8 KB per weight set
+    static constexpr int kStageBytes = NACC * kSetBytes;
+    static constexpr int kRedFloats = kTConsumers * NACC * 4 * 4 * 32;  // NT <= 4
+    static constexpr int kSmemBytes =
+        kTStages * kStageBytes + 1024 /*align*/ + 128 /*barriers*/ + kRedFloats * 4;
+};
+
+__device__ __forceinline__ bool tma_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                         unsigned int *err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_timer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            *abort = 1;
+            atomicOr(err, kErrWaitTimeout);
+            return false;
+        }
+    }
+}
+
+template <int BITS, int NT, bool DUAL>
+__global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ CUtensorMap tm_w,
+                                                        const __grid_constant__ CUtensorMap tm_w2,
+                                                        const GemvParams prm) {
+    constexpr int NACC = DUAL ? 2 : 1;
+    using Cfg = TmaGemvCfg<NACC>;
+    constexpr int kCodesPerKb = 16 * 32 / BITS;
+    constexpr int kCodesPerLane = 4 * 32 / BITS;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kTStages * Cfg::kStageBytes);
+    uint64_t *empty = full + kTStages;
+    volatile int *abort = reinterpret_cast<volatile int *>(empty + kTStages);
+    float *red = reinterpret_cast<float *>(smem + kTStages * Cfg::kStageBytes + 128);
+
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int g = lane >> 2, c = lane & 3;
+    const int p = blockIdx.z;
+
+    pdl_launch_dependents();
+    const bool indexed = prm.expert || prm.m_count || prm.x_rows || prm.lhs || prm.y_rows;
+    if (indexed) pdl_wait();
+
+    int e = prm.expert_is_p ? p : (prm.expert ? prm.expert[p] : 0);
+    bool bad = false;
+    if (e < 0 || e >= prm.E) {
+        bad = true;
+        e = 0;
+    }
+    const int Mp = prm.m_count ? prm.m_count[p] : prm.M;
+    const int off = prm.m_offset ? prm.m_offset[p] : p * prm.M;
+    int xi = prm.lhs ? prm.lhs[p] : (prm.x_batch == prm.P ? p : 0);
+    if (xi < 0 || xi >= prm.x_batch) {
+        bad = true;
+        xi = 0;
+    }
+    if (bad && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0)
+        atomicOr(prm.err, kErrBadIndex);
+    if (Mp <= 0) return;  // uniform over the CTA and the cluster (same problem)
+
+    const int n_stg_total = (prm.kb_total + 1) / 2;
+    const int ksplit = gridDim.y;
+    const int st_lo = (int)(((int64_t)blockIdx.y * n_stg_total) / ksplit);
+    const int st_hi = (int)(((int64_t)(blockIdx.y + 1) * n_stg_total) / ksplit);
+    const int nst = bad ? 0 : st_hi - st_lo;
+    const int passes = (Mp + 8 * NT - 1) / (8 * NT);
+    const int64_t n_base = (int64_t)blockIdx.x * kTRows;
+    if (gridDim.y > 1 && passes > 1) {
+        // never launched this way (the host splits K only for single-pass
+        // problems); refuse rather than risk the cluster barriers
+        if (threadIdx.x == 0) atomicOr(prm.err, kErrBadIndex);
+        return;
+    }
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kTConsumers);
+        }
+        *abort = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == kTConsumers) {
+        // ------------------------------------------------------ producer
+        if (lane == 0 && nst > 0) {
+            prefetch_tmap(&tm_w);
+            if (DUAL) prefetch_tmap(&tm_w2);
+            const int32_t row0 = (int32_t)((int64_t)e * prm.N + n_base);
+            const int total = nst * passes;
+            int t = 0;
+            for (; t < total; ++t) {
+                const int s = t % kTStages;
+                const uint32_t ph = (uint32_t)(t / kTStages) & 1u;
+                if (!tma_wait(&empty[s], ph ^ 1u, abort, prm.err)) break;
+                mbar_expect_tx(&full[s], Cfg::kStageBytes);
+                const int32_t col = (st_lo + t % nst) * kTStageWords;
+                uint8_t *dst = smem + s * Cfg::kStageBytes;
+                tma_load_2d(dst, &tm_w, &full[s], col, row0);
+                if (DUAL) tma_load_2d(dst + Cfg::kSetBytes, &tm_w2, &full[s], col, row0);
+            }
+            // every issued copy must land before the CTA may exit
+            for (int u = (t > kTStages ? t - kTStages : 0); u < t; ++u)
+                tma_wait(&full[u % kTStages], (uint32_t)(u / kTStages) & 1u, abort, prm.err);
+        }
+        __syncwarp();
+        // Cluster K split (only ever launched with a single token pass): the
+        // consumers meet twice per pass; the producer has issued every stage of
+        // the pass by then, so it can join without blocking them.
+        if (gridDim.y > 1) {
+            cg::cluster_group cl = cg::this_cluster();
+            for (int pass = 0; pass < passes; ++pass) {
+                cl.sync();
+                cl.sync();
+            }
+        }
+    } else {
+        // ------------------------------------------------------ consumers
+        const int rl0 = warp * 16 + g;           // local rows rl0, rl0 + 8
+        int64_t nrow[2];
+        const uint16_t *srow[2][NACC];
+        const uint16_t *brow[2][NACC];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            nrow[h] = n_base + rl0 + 8 * h;
+            const int64_t rc = min(nrow[h], prm.N - 1) + (int64_t)e * prm.N;
+#pragma unroll
+            for (int a = 0; a < NACC; ++a) {
+                srow[h][a] = (a ? prm.s2 : prm.s) + rc * prm.G;
+                brow[h][a] = (a ? prm.b2 : prm.b) + rc * prm.G;
+            }
+        }
+        if (!indexed) pdl_wait();
+        int t = 0;  // stage counter across passes
+        for (int pass = 0; pass < passes; ++pass) {
+            const int m0 = pass * 8 * NT;
+            const uint16_t *xrow[NT];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const int m = min(m0 + 8 * nt + g, Mp - 1);
+                const int64_t row = prm.x_rows ? (int64_t)prm.x_rows[off + m]
+                                    : (prm.x_from_offset ? (int64_t)off + m
+                                                         : (int64_t)xi * prm.M + m);
+                xrow[nt] = prm.x + row * prm.x_ld;
+            }
+            float acc[1][NACC][NT][4];
+#pragma unroll
+            for (int a = 0; a < NACC; ++a)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[0][a][nt][j] = 0.0f;
+
+            for (int i = 0; i < nst; ++i, ++t) {
+                const int s = t % kTStages;
+                const uint32_t ph = (uint32_t)(t / kTStages) & 1u;
+                const int kb0 = (st_lo + i) * 2;
+                // scales of this stage (issued before the wait: they are in flight meanwhile)
+                uint32_t sv[2][2][NACC], bv[2][2][NACC];  // [k-block][row][set]
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk) {
+                    const int code0 = (kb0 + kk) * kCodesPerKb + c * kCodesPerLane;
+                    const bool ok = code0 < prm.K;
+                    const int grp = ok ? (code0 >> prm.gs_shift) : 0;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int a = 0; a < NACC; ++a) {
+                            sv[kk][h][a] = ok ? ldg_u16z(srow[h][a] + grp) : 0u;
+                            bv[kk][h][a] = ok ? ldg_u16z(brow[h][a] + grp) : 0u;
+                        }
+                }
+                if (!tma_wait(&full[s], ph, abort, prm.err)) break;
+                KBlock<1, NACC> blk[2];
+                const uint8_t *st = smem + s * Cfg::kStageBytes;
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int rl = rl0 + 8 * h;
+                        const int chunk = (4 * kk + c) ^ (rl & 7);   // 128-byte swizzle
+#pragma unroll
+                        for (int a = 0; a < NACC; ++a) {
+                            blk[kk].w[0][h][a] = *reinterpret_cast<const uint4 *>(
+                                st + a * Cfg::kSetBytes + rl * 128 + chunk * 16);
+                            blk[kk].s[0][h][a] = sv[kk][h][a];
+                            blk[kk].b[0][h][a] = bv[kk][h][a];
+                        }
+                    }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk) {
+                    const int kb = kb0 + kk;
+                    if (kb >= prm.kb_total) break;
+                    const int code0 = kb * kCodesPerKb + c * kCodesPerLane;
+                    compute_kblock<BITS, NT, 1, NACC>(acc, blk[kk], xrow,
+                                                      code0 < prm.K ? code0 : 0);
+                }
+            }
+            // ---- reduce the K slices of the cluster (distributed shared memory)
+            constexpr int kVals = NACC * NT * 4;
+            float *mine = red + (size_t)warp * kVals * 32;
+            if (gridDim.y > 1) {
+                cg::cluster_group cl = cg::this_cluster();
+#pragma unroll
+                for (int a = 0; a < NACC; ++a)
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            mine[((a * NT + nt) * 4 + j) * 32 + lane] = acc[0][a][nt][j];
+                cl.sync();  // the producer warp joins both cluster barriers of a pass
+                if (blockIdx.y == 0) {
+                    for (unsigned r = 1; r < gridDim.y; ++r) {
+                        const float *o = cl.map_shared_rank(mine, r);
+#pragma unroll
+                        for (int a = 0; a < NACC; ++a)
+#pragma unroll
+                            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                                for (int j = 0; j < 4; ++j)
+                                    acc[0][a][nt][j] += o[((a * NT + nt) * 4 + j) * 32 + lane];
+                    }
+                }
+                cl.sync();
+            }
+            if (blockIdx.y == 0) {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int m = m0 + 8 * nt + 2 * c + (j & 1);
+                        const int64_t n = nrow[j >> 1];
+                        if (m >= Mp || n >= prm.N) continue;
+                        float v = acc[0][0][nt][j];
+                        if (DUAL && prm.swiglu) v = silu_f32(v) * acc[0][NACC - 1][nt][j];
+                        const int64_t row =
+                            prm.y_rows ? (int64_t)prm.y_rows[off + m] : (int64_t)off + m;
+                        if (prm.out_f32)
+                            static_cast<float *>(prm.y)[row * prm.y_ld + n] = v;
+                        else
+                            static_cast<uint16_t *>(prm.y)[row * prm.y_ld + n] = f32_to_bf16(v);
+                    }
+            }
+        }
+    }
+}
+
+template <int BITS, int NT, bool DUAL>
+cudaError_t launch_tma_variant(const CUtensorMap &m1, const CUtensorMap &m2,
+                               const GemvParams &prm, dim3 grid, int cluster,
+                               cudaStream_t stream) {
+    constexpr int NACC = DUAL ? 2 : 1;
+    const int smem = TmaGemvCfg<NACC>::kSmemBytes;
+    auto kern = qgemv_tma_kernel<BITS, NT, DUAL>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(32 * (kTConsumers + 1), 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attrs[2];
+    int na = 0;
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+    if (cluster > 1) {
+        attrs[na].id = cudaLaunchAttributeClusterDimension;
+        attrs[na].val.clusterDim.x = 1;
+        attrs[na].val.clusterDim.y = cluster;
+        attrs[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, kern, m1, m2, prm);
+}
+
+template <int BITS, bool DUAL>
+cudaError_t dispatch_tma(const CUtensorMap &m1, const CUtensorMap &m2, const GemvParams &prm,
+                         int nt, dim3 grid, int cluster, cudaStream_t stream) {
+    if (nt == 1) return launch_tma_variant<BITS, 1, DUAL>(m1, m2, prm, grid, cluster, stream);
+    if (nt == 2) return launch_tma_variant<BITS, 2, DUAL>(m1, m2, prm, grid, cluster, stream);
+    return launch_tma_variant<BITS, 4, DUAL>(m1, m2, prm, grid, cluster, stream);
+}
+
 }  // namespace
 
 cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
@@ -527,6 +834,40 @@ cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
     const bool dual = q.w2 != nullptr;
     const int max_m = std::max(1, q.max_m);
     const int nt = max_m <= 8 ? 1 : (max_m <= 16 ? 2 : 4);
+
+    // ---- TMA-fed kernel (the default)
+    {
+        CUtensorMap m1, m2;
+        const uint64_t rows = (uint64_t)q.E * (uint64_t)q.N;
+        bool ok = make_map_2d(&m1, CU_TENSOR_MAP_DATA_TYPE_UINT32, q.w, (uint64_t)prm.Kw, rows,
+                              (uint64_t)prm.Kw * 4, kTStageWords, kTRows,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+        if (ok)
+            ok = make_map_2d(&m2, CU_TENSOR_MAP_DATA_TYPE_UINT32, dual ? q.w2 : q.w,
+                             (uint64_t)prm.Kw, rows, (uint64_t)prm.Kw * 4, kTStageWords, kTRows,
+                             CU_TENSOR_MAP_SWIZZLE_128B);
+        if (ok) {
+            const int64_t row_blocks = (q.N + kTRows - 1) / kTRows;
+            const int64_t tasks = row_blocks * (int64_t)q.P;
+            const int n_stg = (prm.kb_total + 1) / 2;
+            // Split K over a cluster until there are ~4 CTAs of work per SM,
+            // keeping >= 2 stages per CTA.  Only single-pass problems (every
+            // problem's tokens fit one pass) may split: see the kernel.
+            const int64_t target = (int64_t)sm_count() * 4;
+            int ksplit = 1;
+            if (max_m <= 8 * nt)
+                while (ksplit < 8 && tasks * ksplit < target && n_stg >= 4 * ksplit) ksplit <<= 1;
+            prm.s_cta = 1;
+            dim3 grid((unsigned)row_blocks, (unsigned)ksplit, (unsigned)q.P);
+            if (q.bits == 4)
+                return dual ? dispatch_tma<4, true>(m1, m2, prm, nt, grid, ksplit, stream)
+                            : dispatch_tma<4, false>(m1, m2, prm, nt, grid, ksplit, stream);
+            return dual ? dispatch_tma<8, true>(m1, m2, prm, nt, grid, ksplit, stream)
+                        : dispatch_tma<8, false>(m1, m2, prm, nt, grid, ksplit, stream);
+        }
+    }
+
+    // ---- register-fed kernel (when no tensor map can be encoded)
     const int rt = (!dual && nt == 1 && q.N >= 64) ? 2 : 1;
     const int64_t row_groups = (q.N + 16 * rt - 1) / (16 * rt);
     const int64_t tasks = row_groups * (int64_t)q.P;

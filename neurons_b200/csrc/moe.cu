@@ -240,7 +240,7 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
         up.m_count = ws.counts;
         up.m_offset = ws.offsets;
         up.x_rows = ws.pos_token;
-        up.max_m = (int)std::min<int64_t>(P, 32);
+        up.max_m = (int)T;  // an expert sees each token at most once
         // down: problem = expert, rows of h in grouped order, d rows by pair id
         dn.P = (int)E;
         dn.expert_is_p = true;

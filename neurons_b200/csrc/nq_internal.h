@@ -2,6 +2,7 @@
 // kernel launchers.  Not part of the public ABI.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -71,6 +72,13 @@ struct TcGemmArgs {
 };
 
 bool tc_gemm_supported(const TcGemmArgs &a);
+
+// cuTensorMapEncodeTiled for a 2-D row-major tensor (resolved through
+// cudaGetDriverEntryPoint; false when the driver entry point is missing or the
+// encoding is rejected).
+bool make_map_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t inner,
+                 uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle sw);
 cudaError_t launch_tc_gemm(const TcGemmArgs &a, cudaStream_t stream);
 
 cudaError_t launch_quantize(const void *w, int w_dtype, int64_t rows, int64_t K, int bits,
