@@ -173,12 +173,17 @@ __device__ __forceinline__ void compute_kblock(float (&acc)[RT][NACC][NT][4],
                     d.b2 = prmt(blk.b[t][h][a], 0u, 0x1010u);
                     d.n2 = bf2_fma(d.s2, 0xC300C300u, 0x80008000u);  // exact -128*s
                 }
+        uint4 xr[4][NT];  // all activation loads of the k-block first
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) xr[i][nt] = ldg16(xrow[nt] + xoff + 8 * i);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             uint32_t bx[NT][4];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                const uint4 xv = ldg16(xrow[nt] + xoff + 8 * i);
+                const uint4 xv = xr[i][nt];
                 bx[nt][0] = prmt(xv.x, xv.z, 0x5410u);  // (x0, x4)
                 bx[nt][1] = prmt(xv.x, xv.z, 0x7632u);  // (x1, x5)
                 bx[nt][2] = prmt(xv.y, xv.w, 0x5410u);  // (x2, x6)
@@ -215,11 +220,14 @@ __device__ __forceinline__ void compute_kblock(float (&acc)[RT][NACC][NT][4],
 #pragma unroll
                 for (int a = 0; a < NACC; ++a)
                     dq[t][h][a] = make_dq8((uint16_t)blk.s[t][h][a], (uint16_t)blk.b[t][h][a]);
+        uint2 xr[4][NT];  // all activation loads of the k-block first
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) xr[i][nt] = ldg8(xrow[nt] + xoff + 4 * i);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            uint2 bx[NT];
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) bx[nt] = ldg8(xrow[nt] + xoff + 4 * i);
+            const uint2 *bx = xr[i];
 #pragma unroll
             for (int t = 0; t < RT; ++t)
 #pragma unroll
@@ -659,25 +667,39 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
 #pragma unroll
                     for (int j = 0; j < 4; ++j) acc[0][a][nt][j] = 0.0f;
 
-            for (int i = 0; i < nst; ++i, ++t) {
-                const int s = t % kTStages;
-                const uint32_t ph = (uint32_t)(t / kTStages) & 1u;
-                const int kb0 = (st_lo + i) * 2;
-                // scales of this stage (issued before the wait: they are in flight meanwhile)
-                uint32_t sv[2][2][NACC], bv[2][2][NACC];  // [k-block][row][set]
+            // scales and biases of a stage: [k-block][row][set], loaded one stage ahead
+            uint32_t sv[2][2][NACC], bv[2][2][NACC], sn[2][2][NACC], bn[2][2][NACC];
+            auto load_scales = [&](int stage, uint32_t(&so)[2][2][NACC],
+                                   uint32_t(&bo)[2][2][NACC]) {
 #pragma unroll
                 for (int kk = 0; kk < 2; ++kk) {
-                    const int code0 = (kb0 + kk) * kCodesPerKb + c * kCodesPerLane;
-                    const bool ok = code0 < prm.K;
+                    const int code0 = ((st_lo + stage) * 2 + kk) * kCodesPerKb + c * kCodesPerLane;
+                    const bool ok = stage < nst && code0 < prm.K;
                     const int grp = ok ? (code0 >> prm.gs_shift) : 0;
 #pragma unroll
                     for (int h = 0; h < 2; ++h)
 #pragma unroll
                         for (int a = 0; a < NACC; ++a) {
-                            sv[kk][h][a] = ok ? ldg_u16z(srow[h][a] + grp) : 0u;
-                            bv[kk][h][a] = ok ? ldg_u16z(brow[h][a] + grp) : 0u;
+                            so[kk][h][a] = ok ? ldg_u16z(srow[h][a] + grp) : 0u;
+                            bo[kk][h][a] = ok ? ldg_u16z(brow[h][a] + grp) : 0u;
                         }
                 }
+            };
+            load_scales(0, sn, bn);
+            for (int i = 0; i < nst; ++i, ++t) {
+                const int s = t % kTStages;
+                const uint32_t ph = (uint32_t)(t / kTStages) & 1u;
+                const int kb0 = (st_lo + i) * 2;
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int a = 0; a < NACC; ++a) {
+                            sv[kk][h][a] = sn[kk][h][a];
+                            bv[kk][h][a] = bn[kk][h][a];
+                        }
+                load_scales(i + 1, sn, bn);
                 if (!tma_wait(&full[s], ph, abort, prm.err)) break;
                 KBlock<1, NACC> blk[2];
                 const uint8_t *st = smem + s * Cfg::kStageBytes;
