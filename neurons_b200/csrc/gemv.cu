@@ -55,6 +55,7 @@ struct GemvParams {
     int kb_total;   // k-blocks per row (16 words each), the last one possibly partial
     int kb_full;    // complete k-blocks per row
     int s_cta;      // K slices handled by the warps of one CTA (1, 2 or 4)
+    int mx;         // tokens staged per pass (async path)
     unsigned int *err;
 };
 
@@ -493,28 +494,45 @@ cudaError_t dispatch(const GemvParams &prm, int nt, int rt, dim3 grid, int clust
 }
 
 // ----------------------------------------------------------------------------
-// TMA-fed variant (the default path).  A CTA owns 64 weight rows (4 consumer
-// warps x 16 rows) of one problem and one K slice.  Warp 4 streams the rows'
-// packed words into a 4-stage shared-memory ring with cp.async.bulk.tensor
-// (boxes of 32 words x 64 rows, 128-byte swizzle), so the bytes in flight no
-// longer depend on registers: 32 KB per CTA (64 KB for the gate/up pair).
-// Consumer warps read their rows with 128-bit shared loads (the swizzle keeps
-// them at most 2-way bank conflicted), dequantize and multiply exactly as the
-// register path does, and release each stage right after reading it.
+// Asynchronously fed variant (the default path).  A CTA owns 64 weight rows
+// (4 consumer warps x 16 rows) of one problem and one K slice.  Warp 4 fills a
+// 4-stage shared-memory ring; one stage covers 32 packed words per row (256
+// codes at 4 bits, 128 at 8 bits) and holds everything the consumers need for
+// it, so they never wait on a global load:
+//   * the packed words: one cp.async.bulk.tensor box [32 words x 64 rows] per
+//     weight set, 128-byte swizzle (consumer reads are <= 2-way conflicted);
+//   * the activation slice [mx tokens x stage codes] (cp.async, 16-byte
+//     chunks, chunk index XOR token so the 8 token rows of a fragment hit
+//     different banks; tokens past the problem's count are zero-filled);
+//   * the scale and bias spans of the stage's groups for all 64 rows (cp.async).
+// Completion: the bulk copies count bytes on the stage's mbarrier, and every
+// producer lane's cp.asyncs arrive on it (cp.async.mbarrier.arrive.noinc).
+// Consumers dequantize exactly (as the register path does), multiply with
+// mma.sync into two independent accumulator chains, and release the stage.
+// Requires K % 256 == 0 and (8-bit) group size <= 64; else the register path.
 // ----------------------------------------------------------------------------
 constexpr int kTRows = 64;         // weight rows per CTA
-constexpr int kTStageWords = 32;   // packed words per row per stage (2 k-blocks, 128 B)
+constexpr int kTStageWords = 32;   // packed words per row per stage
 constexpr int kTStages = 4;
 constexpr int kTConsumers = 4;
+constexpr int kTSetBytes = kTRows * kTStageWords * 4;  // 8 KB: one weight set of a stage
 
-template <int NACC>
-struct TmaGemvCfg {
-    static constexpr int kSetBytes = kTRows * kTStageWords * 4;   // 8 KB per weight set
-    static constexpr int kStageBytes = NACC * kSetBytes;
-    static constexpr int kRedFloats = kTConsumers * NACC * 4 * 4 * 32;  // NT <= 4
-    static constexpr int kSmemBytes =
-        kTStages * kStageBytes + 1024 /*align*/ + 128 /*barriers*/ + kRedFloats * 4;
+// Byte layout of one stage (offsets from the stage base; base 1024-aligned).
+struct TStageLayout {
+    int x_off, x_row_bytes, s_off, s_row_bytes, bytes;
 };
+
+__host__ __device__ inline TStageLayout tstage_layout(int bits, int nacc, int mx, int gs) {
+    TStageLayout L;
+    const int codes = kTStageWords * 32 / bits;
+    L.x_off = nacc * kTSetBytes;
+    L.x_row_bytes = codes * 2;
+    L.s_off = L.x_off + mx * L.x_row_bytes;
+    L.s_row_bytes = (codes / gs) * 2;                      // one row's group span, one array
+    const int s_bytes = nacc * 2 * kTRows * L.s_row_bytes;  // [set][scale|bias][row][span]
+    L.bytes = (L.s_off + s_bytes + 1023) & ~1023;
+    return L;
+}
 
 __device__ __forceinline__ bool tma_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
                                          unsigned int *err) {
@@ -531,21 +549,133 @@ __device__ __forceinline__ bool tma_wait(uint64_t *bar, uint32_t parity, volatil
     }
 }
 
+// cp.async of `bytes` (4, 8 or 16) from global to shared; src_bytes 0 zero-fills.
+__device__ __forceinline__ void cp_async(void *dst, const void *src, int bytes, int src_bytes) {
+    if (bytes == 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)),
+                     "l"(src), "r"(src_bytes)
+                     : "memory");
+    else if (bytes == 8)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32(dst)),
+                     "l"(src), "r"(src_bytes)
+                     : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)),
+                     "l"(src), "r"(src_bytes)
+                     : "memory");
+}
+
+// The mbarrier receives one arrival once all prior cp.asyncs of this thread land.
+__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// One k-block from shared memory.  ws[h][a]: this lane's 16 bytes of row h of
+// weight set a; sv/bv: its rows' scale and bias bits; xs: activation slice of
+// the stage; xe0: element offset of this lane's first code in the slice;
+// tk[nt]: the token row this lane supplies to n-tile nt.
+template <int BITS, int NT, int NACC>
+__device__ __forceinline__ void compute_kb_smem(float (&acc)[2][NACC][NT][4],
+                                                const uint4 (&w)[2][NACC],
+                                                const uint32_t (&sv)[2][NACC],
+                                                const uint32_t (&bv)[2][NACC],
+                                                const uint8_t *xs, int x_row_bytes, int xe0,
+                                                const int (&tk)[NT]) {
+    if constexpr (BITS == 4) {
+        Dq4 dq[2][NACC];
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int a = 0; a < NACC; ++a) {
+                dq[h][a].s2 = prmt(sv[h][a], 0u, 0x1010u);
+                dq[h][a].b2 = prmt(bv[h][a], 0u, 0x1010u);
+                dq[h][a].n2 = bf2_fma(dq[h][a].s2, 0xC300C300u, 0x80008000u);
+            }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            uint32_t bx[NT][4];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const int chunk = ((xe0 >> 3) + i) ^ (tk[nt] & 7);
+                const uint4 xv =
+                    *reinterpret_cast<const uint4 *>(xs + tk[nt] * x_row_bytes + (chunk << 4));
+                bx[nt][0] = prmt(xv.x, xv.z, 0x5410u);  // (x0, x4)
+                bx[nt][1] = prmt(xv.x, xv.z, 0x7632u);  // (x1, x5)
+                bx[nt][2] = prmt(xv.y, xv.w, 0x5410u);  // (x2, x6)
+                bx[nt][3] = prmt(xv.y, xv.w, 0x7632u);  // (x3, x7)
+            }
+#pragma unroll
+            for (int a = 0; a < NACC; ++a) {
+                const uint32_t wa = (&w[0][a].x)[i];
+                const uint32_t wb = (&w[1][a].x)[i];
+                const uint32_t wa4 = wa >> 4, wb4 = wb >> 4;
+                const uint32_t a0 = dq4_pair(lop3_and_or(wa, 0x000F000Fu, 0x43004300u), dq[0][a]);
+                const uint32_t a1 = dq4_pair(lop3_and_or(wb, 0x000F000Fu, 0x43004300u), dq[1][a]);
+                const uint32_t a2 = dq4_pair(lop3_and_or(wa4, 0x000F000Fu, 0x43004300u), dq[0][a]);
+                const uint32_t a3 = dq4_pair(lop3_and_or(wb4, 0x000F000Fu, 0x43004300u), dq[1][a]);
+                const uint32_t c0 = dq4_pair(lop3_and_or(wa >> 8, 0x000F000Fu, 0x43004300u), dq[0][a]);
+                const uint32_t c1 = dq4_pair(lop3_and_or(wb >> 8, 0x000F000Fu, 0x43004300u), dq[1][a]);
+                const uint32_t c2 = dq4_pair(lop3_and_or(wa4 >> 8, 0x000F000Fu, 0x43004300u), dq[0][a]);
+                const uint32_t c3 = dq4_pair(lop3_and_or(wb4 >> 8, 0x000F000Fu, 0x43004300u), dq[1][a]);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    mma16816(acc[0][a][nt], a0, a1, a2, a3, bx[nt][0], bx[nt][1]);
+                    mma16816(acc[1][a][nt], c0, c1, c2, c3, bx[nt][2], bx[nt][3]);
+                }
+            }
+        }
+    } else {
+        Dq8 dq[2][NACC];
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int a = 0; a < NACC; ++a)
+                dq[h][a] = make_dq8((uint16_t)sv[h][a], (uint16_t)bv[h][a]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            uint2 bx[NT];
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const int e = xe0 + 4 * i;
+                const int chunk = (e >> 3) ^ (tk[nt] & 7);
+                bx[nt] = *reinterpret_cast<const uint2 *>(xs + tk[nt] * x_row_bytes + (chunk << 4) +
+                                                          ((e & 7) << 1));
+            }
+#pragma unroll
+            for (int a = 0; a < NACC; ++a) {
+                const uint32_t wa = (&w[0][a].x)[i];
+                const uint32_t wb = (&w[1][a].x)[i];
+                const uint32_t a0 = dq8_pair(wa, 0, 1, dq[0][a]);
+                const uint32_t a1 = dq8_pair(wb, 0, 1, dq[1][a]);
+                const uint32_t a2 = dq8_pair(wa, 2, 3, dq[0][a]);
+                const uint32_t a3 = dq8_pair(wb, 2, 3, dq[1][a]);
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                    mma16816(acc[i & 1][a][nt], a0, a1, a2, a3, bx[nt].x, bx[nt].y);
+            }
+        }
+    }
+}
+
 template <int BITS, int NT, bool DUAL>
 __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ CUtensorMap tm_w,
                                                         const __grid_constant__ CUtensorMap tm_w2,
                                                         const GemvParams prm) {
     constexpr int NACC = DUAL ? 2 : 1;
-    using Cfg = TmaGemvCfg<NACC>;
+    constexpr int kCodesPerStage = kTStageWords * 32 / BITS;
     constexpr int kCodesPerKb = 16 * 32 / BITS;
     constexpr int kCodesPerLane = 4 * 32 / BITS;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kTStages * Cfg::kStageBytes);
+    const int mx = prm.mx;
+    const int gs = 1 << prm.gs_shift;
+    const TStageLayout L = tstage_layout(BITS, NACC, mx, gs);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kTStages * L.bytes);
     uint64_t *empty = full + kTStages;
     volatile int *abort = reinterpret_cast<volatile int *>(empty + kTStages);
-    float *red = reinterpret_cast<float *>(smem + kTStages * Cfg::kStageBytes + 128);
+    float *red = reinterpret_cast<float *>(smem + kTStages * L.bytes + 128);
 
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -573,23 +703,23 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
         atomicOr(prm.err, kErrBadIndex);
     if (Mp <= 0) return;  // uniform over the CTA and the cluster (same problem)
 
-    const int n_stg_total = (prm.kb_total + 1) / 2;
+    const int n_stg_total = (int)(prm.K / kCodesPerStage);
     const int ksplit = gridDim.y;
     const int st_lo = (int)(((int64_t)blockIdx.y * n_stg_total) / ksplit);
     const int st_hi = (int)(((int64_t)(blockIdx.y + 1) * n_stg_total) / ksplit);
     const int nst = bad ? 0 : st_hi - st_lo;
-    const int passes = (Mp + 8 * NT - 1) / (8 * NT);
+    const int passes = (Mp + mx - 1) / mx;
     const int64_t n_base = (int64_t)blockIdx.x * kTRows;
     if (gridDim.y > 1 && passes > 1) {
-        // never launched this way (the host splits K only for single-pass
-        // problems); refuse rather than risk the cluster barriers
+        // never launched this way (the host splits K only when every problem
+        // fits one pass); refuse rather than risk the cluster barriers
         if (threadIdx.x == 0) atomicOr(prm.err, kErrBadIndex);
         return;
     }
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTStages; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], 1 + 32);  // producer expect_tx + 32 cp.async lanes
             mbar_init(&empty[s], kTConsumers);
         }
         *abort = 0;
@@ -598,22 +728,57 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
     __syncthreads();
 
     if (warp == kTConsumers) {
-        // ------------------------------------------------------ producer
-        if (lane == 0 && nst > 0) {
-            prefetch_tmap(&tm_w);
-            if (DUAL) prefetch_tmap(&tm_w2);
+        // ------------------------------------------------------ producer warp
+        if (!indexed) pdl_wait();  // the activations may come from the previous kernel
+        if (nst > 0) {
+            if (lane == 0) {
+                prefetch_tmap(&tm_w);
+                if (DUAL) prefetch_tmap(&tm_w2);
+            }
             const int32_t row0 = (int32_t)((int64_t)e * prm.N + n_base);
+            // scale/bias rows of this CTA (rows past N clamped: valid memory)
             const int total = nst * passes;
             int t = 0;
             for (; t < total; ++t) {
                 const int s = t % kTStages;
                 const uint32_t ph = (uint32_t)(t / kTStages) & 1u;
                 if (!tma_wait(&empty[s], ph ^ 1u, abort, prm.err)) break;
-                mbar_expect_tx(&full[s], Cfg::kStageBytes);
-                const int32_t col = (st_lo + t % nst) * kTStageWords;
-                uint8_t *dst = smem + s * Cfg::kStageBytes;
-                tma_load_2d(dst, &tm_w, &full[s], col, row0);
-                if (DUAL) tma_load_2d(dst + Cfg::kSetBytes, &tm_w2, &full[s], col, row0);
+                uint8_t *st = smem + s * L.bytes;
+                const int stage = st_lo + t % nst;
+                const int m0 = (t / nst) * mx;
+                if (lane == 0) {
+                    mbar_expect_tx(&full[s], NACC * kTSetBytes);
+                    tma_load_2d(st, &tm_w, &full[s], stage * kTStageWords, row0);
+                    if (DUAL) tma_load_2d(st + kTSetBytes, &tm_w2, &full[s], stage * kTStageWords, row0);
+                }
+                // activation slice: mx tokens x (codes*2/16) chunks of 16 bytes
+                const int code0 = stage * kCodesPerStage;
+                const int chunks = L.x_row_bytes / 16;
+                for (int q = lane; q < mx * chunks; q += 32) {
+                    const int tk = q / chunks, ch = q % chunks;
+                    const int m = m0 + tk;
+                    const uint16_t *src = prm.x;
+                    int nbytes = 0;
+                    if (m < Mp) {
+                        const int64_t row = prm.x_rows ? (int64_t)prm.x_rows[off + m]
+                                            : (prm.x_from_offset ? (int64_t)off + m
+                                                                 : (int64_t)xi * prm.M + m);
+                        src = prm.x + row * prm.x_ld + code0 + ch * 8;
+                        nbytes = 16;
+                    }
+                    cp_async(st + L.x_off + tk * L.x_row_bytes + ((ch ^ (tk & 7)) << 4), src, 16,
+                             nbytes);
+                }
+                // scale / bias spans: [set][scale|bias][row] of L.s_row_bytes each
+                const int grp0 = code0 >> prm.gs_shift;
+                for (int q = lane; q < NACC * 2 * kTRows; q += 32) {
+                    const int a = q / (2 * kTRows), sb = (q / kTRows) & 1, r = q % kTRows;
+                    const int64_t rc = min(n_base + r, prm.N - 1) + (int64_t)e * prm.N;
+                    const uint16_t *base = sb ? (a ? prm.b2 : prm.b) : (a ? prm.s2 : prm.s);
+                    cp_async(st + L.s_off + q * L.s_row_bytes, base + rc * prm.G + grp0,
+                             L.s_row_bytes, L.s_row_bytes);
+                }
+                cp_async_arrive(&full[s]);
             }
             // every issued copy must land before the CTA may exit
             for (int u = (t > kTStages ? t - kTStages : 0); u < t; ++u)
@@ -621,8 +786,8 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
         }
         __syncwarp();
         // Cluster K split (only ever launched with a single token pass): the
-        // consumers meet twice per pass; the producer has issued every stage of
-        // the pass by then, so it can join without blocking them.
+        // consumers meet twice per pass; the producer has issued every stage by
+        // then, so it can join without blocking them.
         if (gridDim.y > 1) {
             cg::cluster_group cl = cg::this_cluster();
             for (int pass = 0; pass < passes; ++pass) {
@@ -631,103 +796,64 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
             }
         }
     } else {
-        // ------------------------------------------------------ consumers
-        const int rl0 = warp * 16 + g;           // local rows rl0, rl0 + 8
-        int64_t nrow[2];
-        const uint16_t *srow[2][NACC];
-        const uint16_t *brow[2][NACC];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            nrow[h] = n_base + rl0 + 8 * h;
-            const int64_t rc = min(nrow[h], prm.N - 1) + (int64_t)e * prm.N;
-#pragma unroll
-            for (int a = 0; a < NACC; ++a) {
-                srow[h][a] = (a ? prm.s2 : prm.s) + rc * prm.G;
-                brow[h][a] = (a ? prm.b2 : prm.b) + rc * prm.G;
-            }
-        }
-        if (!indexed) pdl_wait();
-        int t = 0;  // stage counter across passes
+        // ------------------------------------------------------ consumer warps
+        const int rl0 = warp * 16 + g;  // local rows rl0, rl0 + 8
+        int t = 0;
         for (int pass = 0; pass < passes; ++pass) {
-            const int m0 = pass * 8 * NT;
-            const uint16_t *xrow[NT];
+            const int m0 = pass * mx;
+            int tk[NT];
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const int m = min(m0 + 8 * nt + g, Mp - 1);
-                const int64_t row = prm.x_rows ? (int64_t)prm.x_rows[off + m]
-                                    : (prm.x_from_offset ? (int64_t)off + m
-                                                         : (int64_t)xi * prm.M + m);
-                xrow[nt] = prm.x + row * prm.x_ld;
+            for (int nt = 0; nt < NT; ++nt) tk[nt] = min(8 * nt + g, mx - 1);
+            float acc[2][NACC][NT][4];
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int a = 0; a < NACC; ++a)
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) acc[u][a][nt][j] = 0.0f;
+
+            for (int i = 0; i < nst; ++i, ++t) {
+                const int s = t % kTStages;
+                const uint32_t ph = (uint32_t)(t / kTStages) & 1u;
+                if (!tma_wait(&full[s], ph, abort, prm.err)) break;
+                const uint8_t *st = smem + s * L.bytes;
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk) {
+                    uint4 w[2][NACC];
+                    uint32_t sv[2][NACC], bv[2][NACC];
+                    const int lane_code = kk * kCodesPerKb + c * kCodesPerLane;  // in the stage
+                    const int gl = lane_code >> prm.gs_shift;                    // local group
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int rl = rl0 + 8 * h;
+                        const int chunk = (4 * kk + c) ^ (rl & 7);  // 128-byte swizzle
+#pragma unroll
+                        for (int a = 0; a < NACC; ++a) {
+                            w[h][a] = *reinterpret_cast<const uint4 *>(st + a * kTSetBytes + rl * 128 +
+                                                                       chunk * 16);
+                            const uint16_t *sp = reinterpret_cast<const uint16_t *>(
+                                st + L.s_off + ((a * 2 + 0) * kTRows + rl) * L.s_row_bytes);
+                            const uint16_t *bp = reinterpret_cast<const uint16_t *>(
+                                st + L.s_off + ((a * 2 + 1) * kTRows + rl) * L.s_row_bytes);
+                            sv[h][a] = sp[gl];
+                            bv[h][a] = bp[gl];
+                        }
+                    }
+                    compute_kb_smem<BITS, NT, NACC>(acc, w, sv, bv, st + L.x_off, L.x_row_bytes,
+                                                   lane_code, tk);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
             }
-            float acc[1][NACC][NT][4];
+            // fold the two accumulator chains
 #pragma unroll
             for (int a = 0; a < NACC; ++a)
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) acc[0][a][nt][j] = 0.0f;
-
-            // scales and biases of a stage: [k-block][row][set], loaded one stage ahead
-            uint32_t sv[2][2][NACC], bv[2][2][NACC], sn[2][2][NACC], bn[2][2][NACC];
-            auto load_scales = [&](int stage, uint32_t(&so)[2][2][NACC],
-                                   uint32_t(&bo)[2][2][NACC]) {
-#pragma unroll
-                for (int kk = 0; kk < 2; ++kk) {
-                    const int code0 = ((st_lo + stage) * 2 + kk) * kCodesPerKb + c * kCodesPerLane;
-                    const bool ok = stage < nst && code0 < prm.K;
-                    const int grp = ok ? (code0 >> prm.gs_shift) : 0;
-#pragma unroll
-                    for (int h = 0; h < 2; ++h)
-#pragma unroll
-                        for (int a = 0; a < NACC; ++a) {
-                            so[kk][h][a] = ok ? ldg_u16z(srow[h][a] + grp) : 0u;
-                            bo[kk][h][a] = ok ? ldg_u16z(brow[h][a] + grp) : 0u;
-                        }
-                }
-            };
-            load_scales(0, sn, bn);
-            for (int i = 0; i < nst; ++i, ++t) {
-                const int s = t % kTStages;
-                const uint32_t ph = (uint32_t)(t / kTStages) & 1u;
-                const int kb0 = (st_lo + i) * 2;
-#pragma unroll
-                for (int kk = 0; kk < 2; ++kk)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h)
-#pragma unroll
-                        for (int a = 0; a < NACC; ++a) {
-                            sv[kk][h][a] = sn[kk][h][a];
-                            bv[kk][h][a] = bn[kk][h][a];
-                        }
-                load_scales(i + 1, sn, bn);
-                if (!tma_wait(&full[s], ph, abort, prm.err)) break;
-                KBlock<1, NACC> blk[2];
-                const uint8_t *st = smem + s * Cfg::kStageBytes;
-#pragma unroll
-                for (int kk = 0; kk < 2; ++kk)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int rl = rl0 + 8 * h;
-                        const int chunk = (4 * kk + c) ^ (rl & 7);   // 128-byte swizzle
-#pragma unroll
-                        for (int a = 0; a < NACC; ++a) {
-                            blk[kk].w[0][h][a] = *reinterpret_cast<const uint4 *>(
-                                st + a * Cfg::kSetBytes + rl * 128 + chunk * 16);
-                            blk[kk].s[0][h][a] = sv[kk][h][a];
-                            blk[kk].b[0][h][a] = bv[kk][h][a];
-                        }
-                    }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
-#pragma unroll
-                for (int kk = 0; kk < 2; ++kk) {
-                    const int kb = kb0 + kk;
-                    if (kb >= prm.kb_total) break;
-                    const int code0 = kb * kCodesPerKb + c * kCodesPerLane;
-                    compute_kblock<BITS, NT, 1, NACC>(acc, blk[kk], xrow,
-                                                      code0 < prm.K ? code0 : 0);
-                }
-            }
+                    for (int j = 0; j < 4; ++j) acc[0][a][nt][j] += acc[1][a][nt][j];
             // ---- reduce the K slices of the cluster (distributed shared memory)
             constexpr int kVals = NACC * NT * 4;
             float *mine = red + (size_t)warp * kVals * 32;
@@ -761,8 +887,8 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const int m = m0 + 8 * nt + 2 * c + (j & 1);
-                        const int64_t n = nrow[j >> 1];
-                        if (m >= Mp || n >= prm.N) continue;
+                        const int64_t n = n_base + rl0 + 8 * (j >> 1);
+                        if (m >= Mp || m >= m0 + mx || n >= prm.N) continue;
                         float v = acc[0][0][nt][j];
                         if (DUAL && prm.swiglu) v = silu_f32(v) * acc[0][NACC - 1][nt][j];
                         const int64_t row =
@@ -782,7 +908,8 @@ cudaError_t launch_tma_variant(const CUtensorMap &m1, const CUtensorMap &m2,
                                const GemvParams &prm, dim3 grid, int cluster,
                                cudaStream_t stream) {
     constexpr int NACC = DUAL ? 2 : 1;
-    const int smem = TmaGemvCfg<NACC>::kSmemBytes;
+    const TStageLayout L = tstage_layout(BITS, NACC, prm.mx, 1 << prm.gs_shift);
+    const int smem = kTStages * L.bytes + 1024 + 128 + kTConsumers * NACC * NT * 4 * 32 * 4;
     auto kern = qgemv_tma_kernel<BITS, NT, DUAL>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -857,8 +984,9 @@ cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
     const int max_m = std::max(1, q.max_m);
     const int nt = max_m <= 8 ? 1 : (max_m <= 16 ? 2 : 4);
 
-    // ---- TMA-fed kernel (the default)
-    {
+    // ---- asynchronously fed kernel (the default)
+    if (q.K % 256 == 0 && !(q.bits == 8 && q.gs == 128) &&
+        (reinterpret_cast<uintptr_t>(q.x) & 15) == 0 && q.x_ld % 8 == 0) {
         CUtensorMap m1, m2;
         const uint64_t rows = (uint64_t)q.E * (uint64_t)q.N;
         bool ok = make_map_2d(&m1, CU_TENSOR_MAP_DATA_TYPE_UINT32, q.w, (uint64_t)prm.Kw, rows,
@@ -871,7 +999,8 @@ cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
         if (ok) {
             const int64_t row_blocks = (q.N + kTRows - 1) / kTRows;
             const int64_t tasks = row_blocks * (int64_t)q.P;
-            const int n_stg = (prm.kb_total + 1) / 2;
+            const int n_stg = (int)(q.K / (kTStageWords * 32 / q.bits));
+            prm.mx = std::min(max_m, 8 * nt);
             // Split K over a cluster until there are ~4 CTAs of work per SM,
             // keeping >= 2 stages per CTA.  Only single-pass problems (every
             // problem's tokens fit one pass) may split: see the kernel.
