@@ -511,28 +511,28 @@ cudaError_t dispatch(const GemvParams &prm, int nt, int rt, dim3 grid, int clust
 // mma.sync into two independent accumulator chains, and release the stage.
 // Requires K % 256 == 0 and (8-bit) group size <= 64; else the register path.
 // ----------------------------------------------------------------------------
-constexpr int kTRows = 64;         // weight rows per CTA
 constexpr int kTStageWords = 32;   // packed words per row per stage
-constexpr int kTStages = 4;
-constexpr int kTConsumers = 4;
-constexpr int kTSetBytes = kTRows * kTStageWords * 4;  // 8 KB: one weight set of a stage
+constexpr int kTConsumers = 4;     // consumer warps; each owns 16 * RT rows
 
 // Byte layout of one stage (offsets from the stage base; base 1024-aligned).
 struct TStageLayout {
-    int x_off, x_row_bytes, s_off, s_row_bytes, bytes;
+    int set_bytes, x_off, x_row_bytes, s_off, s_row_bytes, bytes;
 };
 
-__host__ __device__ inline TStageLayout tstage_layout(int bits, int nacc, int mx, int gs) {
+__host__ __device__ inline TStageLayout tstage_layout(int bits, int nacc, int rows, int mx, int gs) {
     TStageLayout L;
     const int codes = kTStageWords * 32 / bits;
-    L.x_off = nacc * kTSetBytes;
+    L.set_bytes = rows * kTStageWords * 4;
+    L.x_off = nacc * L.set_bytes;
     L.x_row_bytes = codes * 2;
     L.s_off = L.x_off + mx * L.x_row_bytes;
-    L.s_row_bytes = (codes / gs) * 2;                      // one row's group span, one array
-    const int s_bytes = nacc * 2 * kTRows * L.s_row_bytes;  // [set][scale|bias][row][span]
+    L.s_row_bytes = (codes / gs) * 2;                    // one row's group span, one array
+    const int s_bytes = nacc * 2 * rows * L.s_row_bytes;  // [set][scale|bias][row][span]
     L.bytes = (L.s_off + s_bytes + 1023) & ~1023;
     return L;
 }
+
+__host__ __device__ constexpr int tstages(int rt) { return rt == 2 ? 3 : 4; }
 
 __device__ __forceinline__ bool tma_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
                                          unsigned int *err) {
@@ -571,98 +571,101 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
                  : "memory");
 }
 
-// One k-block from shared memory.  ws[h][a]: this lane's 16 bytes of row h of
-// weight set a; sv/bv: its rows' scale and bias bits; xs: activation slice of
-// the stage; xe0: element offset of this lane's first code in the slice;
-// tk[nt]: the token row this lane supplies to n-tile nt.
-template <int BITS, int NT, int NACC>
-__device__ __forceinline__ void compute_kb_smem(float (&acc)[2][NACC][NT][4],
-                                                const uint4 (&w)[2][NACC],
-                                                const uint32_t (&sv)[2][NACC],
-                                                const uint32_t (&bv)[2][NACC],
-                                                const uint8_t *xs, int x_row_bytes, int xe0,
-                                                const int (&tk)[NT]) {
+// One k-block from shared memory.  w[t][h][a]: this lane's 16 bytes of row h
+// of tile t of weight set a; sv/bv: its rows' scale and bias bits; xo[nt][i]:
+// byte offsets (in the stage's activation slice xs) of the 16-byte (4-bit) /
+// 8-byte (8-bit) activation chunks this lane feeds to n-tile nt.
+template <int BITS, int NT, int RT, int NACC>
+__device__ __forceinline__ void compute_kb_smem(float (&acc)[2][RT][NACC][NT][4],
+                                                const uint4 (&w)[RT][2][NACC],
+                                                const uint32_t (&sv)[RT][2][NACC],
+                                                const uint32_t (&bv)[RT][2][NACC],
+                                                const uint8_t *xs, const int (&xo)[NT][4]) {
     if constexpr (BITS == 4) {
-        Dq4 dq[2][NACC];
+        Dq4 dq[RT][2][NACC];
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+        for (int t = 0; t < RT; ++t)
 #pragma unroll
-            for (int a = 0; a < NACC; ++a) {
-                dq[h][a].s2 = prmt(sv[h][a], 0u, 0x1010u);
-                dq[h][a].b2 = prmt(bv[h][a], 0u, 0x1010u);
-                dq[h][a].n2 = bf2_fma(dq[h][a].s2, 0xC300C300u, 0x80008000u);
-            }
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int a = 0; a < NACC; ++a) {
+                    dq[t][h][a].s2 = prmt(sv[t][h][a], 0u, 0x1010u);
+                    dq[t][h][a].b2 = prmt(bv[t][h][a], 0u, 0x1010u);
+                    dq[t][h][a].n2 = bf2_fma(dq[t][h][a].s2, 0xC300C300u, 0x80008000u);
+                }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             uint32_t bx[NT][4];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                const int chunk = ((xe0 >> 3) + i) ^ (tk[nt] & 7);
-                const uint4 xv =
-                    *reinterpret_cast<const uint4 *>(xs + tk[nt] * x_row_bytes + (chunk << 4));
+                const uint4 xv = *reinterpret_cast<const uint4 *>(xs + xo[nt][i]);
                 bx[nt][0] = prmt(xv.x, xv.z, 0x5410u);  // (x0, x4)
                 bx[nt][1] = prmt(xv.x, xv.z, 0x7632u);  // (x1, x5)
                 bx[nt][2] = prmt(xv.y, xv.w, 0x5410u);  // (x2, x6)
                 bx[nt][3] = prmt(xv.y, xv.w, 0x7632u);  // (x3, x7)
             }
 #pragma unroll
-            for (int a = 0; a < NACC; ++a) {
-                const uint32_t wa = (&w[0][a].x)[i];
-                const uint32_t wb = (&w[1][a].x)[i];
-                const uint32_t wa4 = wa >> 4, wb4 = wb >> 4;
-                const uint32_t a0 = dq4_pair(lop3_and_or(wa, 0x000F000Fu, 0x43004300u), dq[0][a]);
-                const uint32_t a1 = dq4_pair(lop3_and_or(wb, 0x000F000Fu, 0x43004300u), dq[1][a]);
-                const uint32_t a2 = dq4_pair(lop3_and_or(wa4, 0x000F000Fu, 0x43004300u), dq[0][a]);
-                const uint32_t a3 = dq4_pair(lop3_and_or(wb4, 0x000F000Fu, 0x43004300u), dq[1][a]);
-                const uint32_t c0 = dq4_pair(lop3_and_or(wa >> 8, 0x000F000Fu, 0x43004300u), dq[0][a]);
-                const uint32_t c1 = dq4_pair(lop3_and_or(wb >> 8, 0x000F000Fu, 0x43004300u), dq[1][a]);
-                const uint32_t c2 = dq4_pair(lop3_and_or(wa4 >> 8, 0x000F000Fu, 0x43004300u), dq[0][a]);
-                const uint32_t c3 = dq4_pair(lop3_and_or(wb4 >> 8, 0x000F000Fu, 0x43004300u), dq[1][a]);
+            for (int t = 0; t < RT; ++t)
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    mma16816(acc[0][a][nt], a0, a1, a2, a3, bx[nt][0], bx[nt][1]);
-                    mma16816(acc[1][a][nt], c0, c1, c2, c3, bx[nt][2], bx[nt][3]);
+                for (int a = 0; a < NACC; ++a) {
+                    const uint32_t wa = (&w[t][0][a].x)[i];
+                    const uint32_t wb = (&w[t][1][a].x)[i];
+                    const uint32_t wa4 = wa >> 4, wb4 = wb >> 4;
+                    const uint32_t a0 = dq4_pair(lop3_and_or(wa, 0x000F000Fu, 0x43004300u), dq[t][0][a]);
+                    const uint32_t a1 = dq4_pair(lop3_and_or(wb, 0x000F000Fu, 0x43004300u), dq[t][1][a]);
+                    const uint32_t a2 = dq4_pair(lop3_and_or(wa4, 0x000F000Fu, 0x43004300u), dq[t][0][a]);
+                    const uint32_t a3 = dq4_pair(lop3_and_or(wb4, 0x000F000Fu, 0x43004300u), dq[t][1][a]);
+                    const uint32_t c0 = dq4_pair(lop3_and_or(wa >> 8, 0x000F000Fu, 0x43004300u), dq[t][0][a]);
+                    const uint32_t c1 = dq4_pair(lop3_and_or(wb >> 8, 0x000F000Fu, 0x43004300u), dq[t][1][a]);
+                    const uint32_t c2 = dq4_pair(lop3_and_or(wa4 >> 8, 0x000F000Fu, 0x43004300u), dq[t][0][a]);
+                    const uint32_t c3 = dq4_pair(lop3_and_or(wb4 >> 8, 0x000F000Fu, 0x43004300u), dq[t][1][a]);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        mma16816(acc[0][t][a][nt], a0, a1, a2, a3, bx[nt][0], bx[nt][1]);
+                        mma16816(acc[1][t][a][nt], c0, c1, c2, c3, bx[nt][2], bx[nt][3]);
+                    }
                 }
-            }
         }
     } else {
-        Dq8 dq[2][NACC];
+        Dq8 dq[RT][2][NACC];
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+        for (int t = 0; t < RT; ++t)
 #pragma unroll
-            for (int a = 0; a < NACC; ++a)
-                dq[h][a] = make_dq8((uint16_t)sv[h][a], (uint16_t)bv[h][a]);
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int a = 0; a < NACC; ++a)
+                    dq[t][h][a] = make_dq8((uint16_t)sv[t][h][a], (uint16_t)bv[t][h][a]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             uint2 bx[NT];
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const int e = xe0 + 4 * i;
-                const int chunk = (e >> 3) ^ (tk[nt] & 7);
-                bx[nt] = *reinterpret_cast<const uint2 *>(xs + tk[nt] * x_row_bytes + (chunk << 4) +
-                                                          ((e & 7) << 1));
-            }
+            for (int nt = 0; nt < NT; ++nt)
+                bx[nt] = *reinterpret_cast<const uint2 *>(xs + xo[nt][i]);
 #pragma unroll
-            for (int a = 0; a < NACC; ++a) {
-                const uint32_t wa = (&w[0][a].x)[i];
-                const uint32_t wb = (&w[1][a].x)[i];
-                const uint32_t a0 = dq8_pair(wa, 0, 1, dq[0][a]);
-                const uint32_t a1 = dq8_pair(wb, 0, 1, dq[1][a]);
-                const uint32_t a2 = dq8_pair(wa, 2, 3, dq[0][a]);
-                const uint32_t a3 = dq8_pair(wb, 2, 3, dq[1][a]);
+            for (int t = 0; t < RT; ++t)
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
-                    mma16816(acc[i & 1][a][nt], a0, a1, a2, a3, bx[nt].x, bx[nt].y);
-            }
+                for (int a = 0; a < NACC; ++a) {
+                    const uint32_t wa = (&w[t][0][a].x)[i];
+                    const uint32_t wb = (&w[t][1][a].x)[i];
+                    const uint32_t a0 = dq8_pair(wa, 0, 1, dq[t][0][a]);
+                    const uint32_t a1 = dq8_pair(wb, 0, 1, dq[t][1][a]);
+                    const uint32_t a2 = dq8_pair(wa, 2, 3, dq[t][0][a]);
+                    const uint32_t a3 = dq8_pair(wb, 2, 3, dq[t][1][a]);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+                        mma16816(acc[i & 1][t][a][nt], a0, a1, a2, a3, bx[nt].x, bx[nt].y);
+                }
         }
     }
 }
 
-template <int BITS, int NT, bool DUAL>
+template <int BITS, int NT, int RT, bool DUAL>
 __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ CUtensorMap tm_w,
                                                         const __grid_constant__ CUtensorMap tm_w2,
                                                         const GemvParams prm) {
     constexpr int NACC = DUAL ? 2 : 1;
+    constexpr int kRows = kTConsumers * 16 * RT;  // weight rows per CTA
+    constexpr int kStages = tstages(RT);
     constexpr int kCodesPerStage = kTStageWords * 32 / BITS;
     constexpr int kCodesPerKb = 16 * 32 / BITS;
     constexpr int kCodesPerLane = 4 * 32 / BITS;
@@ -670,12 +673,11 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~uintptr_t(1023));
     const int mx = prm.mx;
-    const int gs = 1 << prm.gs_shift;
-    const TStageLayout L = tstage_layout(BITS, NACC, mx, gs);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kTStages * L.bytes);
-    uint64_t *empty = full + kTStages;
-    volatile int *abort = reinterpret_cast<volatile int *>(empty + kTStages);
-    float *red = reinterpret_cast<float *>(smem + kTStages * L.bytes + 128);
+    const TStageLayout L = tstage_layout(BITS, NACC, kRows, mx, 1 << prm.gs_shift);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * L.bytes);
+    uint64_t *empty = full + kStages;
+    volatile int *abort = reinterpret_cast<volatile int *>(empty + kStages);
+    float *red = reinterpret_cast<float *>(smem + kStages * L.bytes + 128);
 
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -709,7 +711,7 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
     const int st_hi = (int)(((int64_t)(blockIdx.y + 1) * n_stg_total) / ksplit);
     const int nst = bad ? 0 : st_hi - st_lo;
     const int passes = (Mp + mx - 1) / mx;
-    const int64_t n_base = (int64_t)blockIdx.x * kTRows;
+    const int64_t n_base = (int64_t)blockIdx.x * kRows;
     if (gridDim.y > 1 && passes > 1) {
         // never launched this way (the host splits K only when every problem
         // fits one pass); refuse rather than risk the cluster barriers
@@ -718,7 +720,7 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
     }
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kTStages; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1 + 32);  // producer expect_tx + 32 cp.async lanes
             mbar_init(&empty[s], kTConsumers);
         }
@@ -736,26 +738,26 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
                 if (DUAL) prefetch_tmap(&tm_w2);
             }
             const int32_t row0 = (int32_t)((int64_t)e * prm.N + n_base);
-            // scale/bias rows of this CTA (rows past N clamped: valid memory)
+            const int chunks = L.x_row_bytes / 16;  // 16-byte chunks per token row
             const int total = nst * passes;
             int t = 0;
             for (; t < total; ++t) {
-                const int s = t % kTStages;
-                const uint32_t ph = (uint32_t)(t / kTStages) & 1u;
+                const int s = t % kStages;
+                const uint32_t ph = (uint32_t)(t / kStages) & 1u;
                 if (!tma_wait(&empty[s], ph ^ 1u, abort, prm.err)) break;
                 uint8_t *st = smem + s * L.bytes;
-                const int stage = st_lo + t % nst;
-                const int m0 = (t / nst) * mx;
+                const int pass = t / nst;
+                const int stage = st_lo + (t - pass * nst);
+                const int m0 = pass * mx;
                 if (lane == 0) {
-                    mbar_expect_tx(&full[s], NACC * kTSetBytes);
+                    mbar_expect_tx(&full[s], NACC * L.set_bytes);
                     tma_load_2d(st, &tm_w, &full[s], stage * kTStageWords, row0);
-                    if (DUAL) tma_load_2d(st + kTSetBytes, &tm_w2, &full[s], stage * kTStageWords, row0);
+                    if (DUAL)
+                        tma_load_2d(st + L.set_bytes, &tm_w2, &full[s], stage * kTStageWords, row0);
                 }
-                // activation slice: mx tokens x (codes*2/16) chunks of 16 bytes
+                // activation slice: mx token rows of `chunks` 16-byte chunks, chunk ^ (token & 7)
                 const int code0 = stage * kCodesPerStage;
-                const int chunks = L.x_row_bytes / 16;
-                for (int q = lane; q < mx * chunks; q += 32) {
-                    const int tk = q / chunks, ch = q % chunks;
+                for (int tk = 0; tk < mx; ++tk) {
                     const int m = m0 + tk;
                     const uint16_t *src = prm.x;
                     int nbytes = 0;
@@ -763,16 +765,18 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
                         const int64_t row = prm.x_rows ? (int64_t)prm.x_rows[off + m]
                                             : (prm.x_from_offset ? (int64_t)off + m
                                                                  : (int64_t)xi * prm.M + m);
-                        src = prm.x + row * prm.x_ld + code0 + ch * 8;
+                        src = prm.x + row * prm.x_ld + code0;
                         nbytes = 16;
                     }
-                    cp_async(st + L.x_off + tk * L.x_row_bytes + ((ch ^ (tk & 7)) << 4), src, 16,
-                             nbytes);
+                    uint8_t *xdst = st + L.x_off + tk * L.x_row_bytes;
+                    for (int ch = lane; ch < chunks; ch += 32)
+                        cp_async(xdst + ((ch ^ (tk & 7)) << 4), src + (nbytes ? ch * 8 : 0), 16,
+                                 nbytes);
                 }
-                // scale / bias spans: [set][scale|bias][row] of L.s_row_bytes each
+                // scale / bias spans: [set][scale|bias][row], L.s_row_bytes each
                 const int grp0 = code0 >> prm.gs_shift;
-                for (int q = lane; q < NACC * 2 * kTRows; q += 32) {
-                    const int a = q / (2 * kTRows), sb = (q / kTRows) & 1, r = q % kTRows;
+                for (int q = lane; q < NACC * 2 * kRows; q += 32) {
+                    const int a = q / (2 * kRows), sb = (q / kRows) & 1, r = q % kRows;
                     const int64_t rc = min(n_base + r, prm.N - 1) + (int64_t)e * prm.N;
                     const uint16_t *base = sb ? (a ? prm.b2 : prm.b) : (a ? prm.s2 : prm.s);
                     cp_async(st + L.s_off + q * L.s_row_bytes, base + rc * prm.G + grp0,
@@ -781,8 +785,8 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
                 cp_async_arrive(&full[s]);
             }
             // every issued copy must land before the CTA may exit
-            for (int u = (t > kTStages ? t - kTStages : 0); u < t; ++u)
-                tma_wait(&full[u % kTStages], (uint32_t)(u / kTStages) & 1u, abort, prm.err);
+            for (int u = (t > kStages ? t - kStages : 0); u < t; ++u)
+                tma_wait(&full[u % kStages], (uint32_t)(u / kStages) & 1u, abort, prm.err);
         }
         __syncwarp();
         // Cluster K split (only ever launched with a single token pass): the
@@ -797,120 +801,151 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
         }
     } else {
         // ------------------------------------------------------ consumer warps
-        const int rl0 = warp * 16 + g;  // local rows rl0, rl0 + 8
+        // Per-lane byte offsets inside a stage, fixed for the whole kernel.
+        int wo[2][RT][2];  // [k-block][tile][row]: this lane's 16 bytes of packed words
+        int so[2][RT][2];  // scale of [k-block][tile][row] (bias: + kRows * s_row_bytes)
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+            for (int t = 0; t < RT; ++t)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int rl = warp * 16 * RT + 16 * t + 8 * h + g;
+                    wo[kk][t][h] = rl * 128 + (((4 * kk + c) ^ (rl & 7)) << 4);
+                    const int gl = (kk * kCodesPerKb + c * kCodesPerLane) >> prm.gs_shift;
+                    so[kk][t][h] = L.s_off + rl * L.s_row_bytes + gl * 2;
+                }
+        const int bias_delta = kRows * L.s_row_bytes;
+        const int set_s_delta = 2 * kRows * L.s_row_bytes;
         int t = 0;
         for (int pass = 0; pass < passes; ++pass) {
             const int m0 = pass * mx;
-            int tk[NT];
+            int xo[2][NT][4];  // [k-block][n-tile][chunk]: activation chunk offsets
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) tk[nt] = min(8 * nt + g, mx - 1);
-            float acc[2][NACC][NT][4];
+            for (int nt = 0; nt < NT; ++nt) {
+                const int tk = min(8 * nt + g, mx - 1);
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int el = kk * kCodesPerKb + c * kCodesPerLane + i * (32 / BITS);
+                        xo[kk][nt][i] = L.x_off + tk * L.x_row_bytes +
+                                        (((el >> 3) ^ (tk & 7)) << 4) + ((el & 7) << 1);
+                    }
+            }
+            float acc[2][RT][NACC][NT][4];
 #pragma unroll
             for (int u = 0; u < 2; ++u)
 #pragma unroll
-                for (int a = 0; a < NACC; ++a)
+                for (int r = 0; r < RT; ++r)
 #pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
+                    for (int a = 0; a < NACC; ++a)
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) acc[u][a][nt][j] = 0.0f;
+                        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) acc[u][r][a][nt][j] = 0.0f;
 
             for (int i = 0; i < nst; ++i, ++t) {
-                const int s = t % kTStages;
-                const uint32_t ph = (uint32_t)(t / kTStages) & 1u;
+                const int s = t % kStages;
+                const uint32_t ph = (uint32_t)(t / kStages) & 1u;
                 if (!tma_wait(&full[s], ph, abort, prm.err)) break;
                 const uint8_t *st = smem + s * L.bytes;
 #pragma unroll
                 for (int kk = 0; kk < 2; ++kk) {
-                    uint4 w[2][NACC];
-                    uint32_t sv[2][NACC], bv[2][NACC];
-                    const int lane_code = kk * kCodesPerKb + c * kCodesPerLane;  // in the stage
-                    const int gl = lane_code >> prm.gs_shift;                    // local group
+                    uint4 w[RT][2][NACC];
+                    uint32_t sv[RT][2][NACC], bv[RT][2][NACC];
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int rl = rl0 + 8 * h;
-                        const int chunk = (4 * kk + c) ^ (rl & 7);  // 128-byte swizzle
+                    for (int r = 0; r < RT; ++r)
 #pragma unroll
-                        for (int a = 0; a < NACC; ++a) {
-                            w[h][a] = *reinterpret_cast<const uint4 *>(st + a * kTSetBytes + rl * 128 +
-                                                                       chunk * 16);
-                            const uint16_t *sp = reinterpret_cast<const uint16_t *>(
-                                st + L.s_off + ((a * 2 + 0) * kTRows + rl) * L.s_row_bytes);
-                            const uint16_t *bp = reinterpret_cast<const uint16_t *>(
-                                st + L.s_off + ((a * 2 + 1) * kTRows + rl) * L.s_row_bytes);
-                            sv[h][a] = sp[gl];
-                            bv[h][a] = bp[gl];
-                        }
-                    }
-                    compute_kb_smem<BITS, NT, NACC>(acc, w, sv, bv, st + L.x_off, L.x_row_bytes,
-                                                   lane_code, tk);
+                        for (int h = 0; h < 2; ++h)
+#pragma unroll
+                            for (int a = 0; a < NACC; ++a) {
+                                w[r][h][a] = *reinterpret_cast<const uint4 *>(
+                                    st + a * L.set_bytes + wo[kk][r][h]);
+                                const uint8_t *sp = st + so[kk][r][h] + a * set_s_delta;
+                                sv[r][h][a] = *reinterpret_cast<const uint16_t *>(sp);
+                                bv[r][h][a] = *reinterpret_cast<const uint16_t *>(sp + bias_delta);
+                            }
+                    compute_kb_smem<BITS, NT, RT, NACC>(acc, w, sv, bv, st, xo[kk]);
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
             // fold the two accumulator chains
 #pragma unroll
-            for (int a = 0; a < NACC; ++a)
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) acc[0][a][nt][j] += acc[1][a][nt][j];
-            // ---- reduce the K slices of the cluster (distributed shared memory)
-            constexpr int kVals = NACC * NT * 4;
-            float *mine = red + (size_t)warp * kVals * 32;
-            if (gridDim.y > 1) {
-                cg::cluster_group cl = cg::this_cluster();
+            for (int r = 0; r < RT; ++r)
 #pragma unroll
                 for (int a = 0; a < NACC; ++a)
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            mine[((a * NT + nt) * 4 + j) * 32 + lane] = acc[0][a][nt][j];
+                        for (int j = 0; j < 4; ++j) acc[0][r][a][nt][j] += acc[1][r][a][nt][j];
+            // ---- reduce the K slices of the cluster (distributed shared memory)
+            constexpr int kVals = RT * NACC * NT * 4;
+            float *mine = red + (size_t)warp * kVals * 32;
+            if (gridDim.y > 1) {
+                cg::cluster_group cl = cg::this_cluster();
+#pragma unroll
+                for (int r = 0; r < RT; ++r)
+#pragma unroll
+                    for (int a = 0; a < NACC; ++a)
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                mine[(((r * NACC + a) * NT + nt) * 4 + j) * 32 + lane] =
+                                    acc[0][r][a][nt][j];
                 cl.sync();  // the producer warp joins both cluster barriers of a pass
                 if (blockIdx.y == 0) {
-                    for (unsigned r = 1; r < gridDim.y; ++r) {
-                        const float *o = cl.map_shared_rank(mine, r);
+                    for (unsigned q = 1; q < gridDim.y; ++q) {
+                        const float *o = cl.map_shared_rank(mine, q);
 #pragma unroll
-                        for (int a = 0; a < NACC; ++a)
+                        for (int r = 0; r < RT; ++r)
 #pragma unroll
-                            for (int nt = 0; nt < NT; ++nt)
+                            for (int a = 0; a < NACC; ++a)
 #pragma unroll
-                                for (int j = 0; j < 4; ++j)
-                                    acc[0][a][nt][j] += o[((a * NT + nt) * 4 + j) * 32 + lane];
+                                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                                    for (int j = 0; j < 4; ++j)
+                                        acc[0][r][a][nt][j] +=
+                                            o[(((r * NACC + a) * NT + nt) * 4 + j) * 32 + lane];
                     }
                 }
                 cl.sync();
             }
             if (blockIdx.y == 0) {
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
+                for (int r = 0; r < RT; ++r)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int m = m0 + 8 * nt + 2 * c + (j & 1);
-                        const int64_t n = n_base + rl0 + 8 * (j >> 1);
-                        if (m >= Mp || m >= m0 + mx || n >= prm.N) continue;
-                        float v = acc[0][0][nt][j];
-                        if (DUAL && prm.swiglu) v = silu_f32(v) * acc[0][NACC - 1][nt][j];
-                        const int64_t row =
-                            prm.y_rows ? (int64_t)prm.y_rows[off + m] : (int64_t)off + m;
-                        if (prm.out_f32)
-                            static_cast<float *>(prm.y)[row * prm.y_ld + n] = v;
-                        else
-                            static_cast<uint16_t *>(prm.y)[row * prm.y_ld + n] = f32_to_bf16(v);
-                    }
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const int m = m0 + 8 * nt + 2 * c + (j & 1);
+                            const int64_t n = n_base + warp * 16 * RT + 16 * r + g + 8 * (j >> 1);
+                            if (m >= Mp || m >= m0 + mx || n >= prm.N) continue;
+                            float v = acc[0][r][0][nt][j];
+                            if (DUAL && prm.swiglu) v = silu_f32(v) * acc[0][r][NACC - 1][nt][j];
+                            const int64_t row =
+                                prm.y_rows ? (int64_t)prm.y_rows[off + m] : (int64_t)off + m;
+                            if (prm.out_f32)
+                                static_cast<float *>(prm.y)[row * prm.y_ld + n] = v;
+                            else
+                                static_cast<uint16_t *>(prm.y)[row * prm.y_ld + n] = f32_to_bf16(v);
+                        }
             }
         }
     }
 }
 
-template <int BITS, int NT, bool DUAL>
+template <int BITS, int NT, int RT, bool DUAL>
 cudaError_t launch_tma_variant(const CUtensorMap &m1, const CUtensorMap &m2,
                                const GemvParams &prm, dim3 grid, int cluster,
                                cudaStream_t stream) {
     constexpr int NACC = DUAL ? 2 : 1;
-    const TStageLayout L = tstage_layout(BITS, NACC, prm.mx, 1 << prm.gs_shift);
-    const int smem = kTStages * L.bytes + 1024 + 128 + kTConsumers * NACC * NT * 4 * 32 * 4;
-    auto kern = qgemv_tma_kernel<BITS, NT, DUAL>;
+    constexpr int kRows = kTConsumers * 16 * RT;
+    const TStageLayout L = tstage_layout(BITS, NACC, kRows, prm.mx, 1 << prm.gs_shift);
+    const int smem = tstages(RT) * L.bytes + 1024 + 128 + kTConsumers * RT * NACC * NT * 4 * 32 * 4;
+    auto kern = qgemv_tma_kernel<BITS, NT, RT, DUAL>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
@@ -937,10 +972,12 @@ cudaError_t launch_tma_variant(const CUtensorMap &m1, const CUtensorMap &m2,
 
 template <int BITS, bool DUAL>
 cudaError_t dispatch_tma(const CUtensorMap &m1, const CUtensorMap &m2, const GemvParams &prm,
-                         int nt, dim3 grid, int cluster, cudaStream_t stream) {
-    if (nt == 1) return launch_tma_variant<BITS, 1, DUAL>(m1, m2, prm, grid, cluster, stream);
-    if (nt == 2) return launch_tma_variant<BITS, 2, DUAL>(m1, m2, prm, grid, cluster, stream);
-    return launch_tma_variant<BITS, 4, DUAL>(m1, m2, prm, grid, cluster, stream);
+                         int nt, int rt, dim3 grid, int cluster, cudaStream_t stream) {
+    if (nt == 1)
+        return rt == 2 ? launch_tma_variant<BITS, 1, 2, DUAL>(m1, m2, prm, grid, cluster, stream)
+                       : launch_tma_variant<BITS, 1, 1, DUAL>(m1, m2, prm, grid, cluster, stream);
+    if (nt == 2) return launch_tma_variant<BITS, 2, 1, DUAL>(m1, m2, prm, grid, cluster, stream);
+    return launch_tma_variant<BITS, 4, 1, DUAL>(m1, m2, prm, grid, cluster, stream);
 }
 
 }  // namespace
@@ -987,17 +1024,19 @@ cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
     // ---- asynchronously fed kernel (the default)
     if (q.K % 256 == 0 && !(q.bits == 8 && q.gs == 128) &&
         (reinterpret_cast<uintptr_t>(q.x) & 15) == 0 && q.x_ld % 8 == 0) {
+        const int rt_t = (!dual && nt == 1) ? 2 : 1;
+        const int rows_cta = kTConsumers * 16 * rt_t;
         CUtensorMap m1, m2;
         const uint64_t rows = (uint64_t)q.E * (uint64_t)q.N;
         bool ok = make_map_2d(&m1, CU_TENSOR_MAP_DATA_TYPE_UINT32, q.w, (uint64_t)prm.Kw, rows,
-                              (uint64_t)prm.Kw * 4, kTStageWords, kTRows,
+                              (uint64_t)prm.Kw * 4, kTStageWords, rows_cta,
                               CU_TENSOR_MAP_SWIZZLE_128B);
         if (ok)
             ok = make_map_2d(&m2, CU_TENSOR_MAP_DATA_TYPE_UINT32, dual ? q.w2 : q.w,
-                             (uint64_t)prm.Kw, rows, (uint64_t)prm.Kw * 4, kTStageWords, kTRows,
-                             CU_TENSOR_MAP_SWIZZLE_128B);
+                             (uint64_t)prm.Kw, rows, (uint64_t)prm.Kw * 4, kTStageWords,
+                             rows_cta, CU_TENSOR_MAP_SWIZZLE_128B);
         if (ok) {
-            const int64_t row_blocks = (q.N + kTRows - 1) / kTRows;
+            const int64_t row_blocks = (q.N + rows_cta - 1) / rows_cta;
             const int64_t tasks = row_blocks * (int64_t)q.P;
             const int n_stg = (int)(q.K / (kTStageWords * 32 / q.bits));
             prm.mx = std::min(max_m, 8 * nt);
@@ -1006,15 +1045,15 @@ cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
             // problem's tokens fit one pass) may split: see the kernel.
             const int64_t target = (int64_t)sm_count() * 4;
             int ksplit = 1;
-            if (max_m <= 8 * nt)
+            if (max_m <= prm.mx)
                 while (ksplit < 8 && tasks * ksplit < target && n_stg >= 4 * ksplit) ksplit <<= 1;
             prm.s_cta = 1;
             dim3 grid((unsigned)row_blocks, (unsigned)ksplit, (unsigned)q.P);
             if (q.bits == 4)
-                return dual ? dispatch_tma<4, true>(m1, m2, prm, nt, grid, ksplit, stream)
-                            : dispatch_tma<4, false>(m1, m2, prm, nt, grid, ksplit, stream);
-            return dual ? dispatch_tma<8, true>(m1, m2, prm, nt, grid, ksplit, stream)
-                        : dispatch_tma<8, false>(m1, m2, prm, nt, grid, ksplit, stream);
+                return dual ? dispatch_tma<4, true>(m1, m2, prm, nt, rt_t, grid, ksplit, stream)
+                            : dispatch_tma<4, false>(m1, m2, prm, nt, rt_t, grid, ksplit, stream);
+            return dual ? dispatch_tma<8, true>(m1, m2, prm, nt, rt_t, grid, ksplit, stream)
+                        : dispatch_tma<8, false>(m1, m2, prm, nt, rt_t, grid, ksplit, stream);
         }
     }
 
