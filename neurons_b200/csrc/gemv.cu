@@ -526,8 +526,8 @@ __host__ __device__ inline TStageLayout tstage_layout(int bits, int nacc, int ro
     L.x_off = nacc * L.set_bytes;
     L.x_row_bytes = codes * 2;
     L.s_off = L.x_off + mx * L.x_row_bytes;
-    L.s_row_bytes = (codes / gs) * 2;                    // one row's group span, one array
-    const int s_bytes = nacc * 2 * rows * L.s_row_bytes;  // [set][scale|bias][row][span]
+    L.s_row_bytes = (codes / gs) * 2;       // one row's group span (4, 8 or 16 bytes) ...
+    const int s_bytes = nacc * 2 * rows * 16;  // ... in a 16-byte slot: [set][scale|bias][row]
     L.bytes = (L.s_off + s_bytes + 1023) & ~1023;
     return L;
 }
@@ -779,8 +779,8 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
                     const int a = q / (2 * kRows), sb = (q / kRows) & 1, r = q % kRows;
                     const int64_t rc = min(n_base + r, prm.N - 1) + (int64_t)e * prm.N;
                     const uint16_t *base = sb ? (a ? prm.b2 : prm.b) : (a ? prm.s2 : prm.s);
-                    cp_async(st + L.s_off + q * L.s_row_bytes, base + rc * prm.G + grp0,
-                             L.s_row_bytes, L.s_row_bytes);
+                    cp_async(st + L.s_off + q * 16, base + rc * prm.G + grp0, L.s_row_bytes,
+                             L.s_row_bytes);
                 }
                 cp_async_arrive(&full[s]);
             }
@@ -801,37 +801,30 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
         }
     } else {
         // ------------------------------------------------------ consumer warps
-        // Per-lane byte offsets inside a stage, fixed for the whole kernel.
-        int wo[2][RT][2];  // [k-block][tile][row]: this lane's 16 bytes of packed words
-        int so[2][RT][2];  // scale of [k-block][tile][row] (bias: + kRows * s_row_bytes)
-#pragma unroll
-        for (int kk = 0; kk < 2; ++kk)
-#pragma unroll
-            for (int t = 0; t < RT; ++t)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int rl = warp * 16 * RT + 16 * t + 8 * h + g;
-                    wo[kk][t][h] = rl * 128 + (((4 * kk + c) ^ (rl & 7)) << 4);
-                    const int gl = (kk * kCodesPerKb + c * kCodesPerLane) >> prm.gs_shift;
-                    so[kk][t][h] = L.s_off + rl * L.s_row_bytes + gl * 2;
-                }
-        const int bias_delta = kRows * L.s_row_bytes;
-        const int set_s_delta = 2 * kRows * L.s_row_bytes;
+        // Every shared-memory read is (per-lane base) + (compile-time constant):
+        //   packed words of row warp*16*RT + 16r + 8h + g: the 128-byte swizzle
+        //   XORs the chunk with (row & 7) == g, so only the k-block term is
+        //   lane-dependent; scales/biases sit in 16-byte row slots.
+        const int row_l = warp * 16 * RT + g;
+        const int wbase0 = row_l * 128 + (((0 + c) ^ g) << 4);
+        const int wbase1 = row_l * 128 + (((4 + c) ^ g) << 4);
+        const int gl0 = (c * kCodesPerLane) >> prm.gs_shift;
+        const int gl1 = (kCodesPerKb + c * kCodesPerLane) >> prm.gs_shift;
+        const int sbase0 = L.s_off + row_l * 16 + gl0 * 2;
+        const int sbase1 = L.s_off + row_l * 16 + gl1 * 2;
         int t = 0;
         for (int pass = 0; pass < passes; ++pass) {
             const int m0 = pass * mx;
-            int xo[2][NT][4];  // [k-block][n-tile][chunk]: activation chunk offsets
+            int xo[NT][4];  // activation chunk offsets of k-block 0 (k-block 1: + kb bytes)
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const int tk = min(8 * nt + g, mx - 1);
 #pragma unroll
-                for (int kk = 0; kk < 2; ++kk)
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int el = kk * kCodesPerKb + c * kCodesPerLane + i * (32 / BITS);
-                        xo[kk][nt][i] = L.x_off + tk * L.x_row_bytes +
-                                        (((el >> 3) ^ (tk & 7)) << 4) + ((el & 7) << 1);
-                    }
+                for (int i = 0; i < 4; ++i) {
+                    const int el = c * kCodesPerLane + i * (32 / BITS);
+                    xo[nt][i] = L.x_off + tk * L.x_row_bytes + (((el >> 3) ^ (tk & 7)) << 4) +
+                                ((el & 7) << 1);
+                }
             }
             float acc[2][RT][NACC][NT][4];
 #pragma unroll
@@ -852,6 +845,8 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
                 const uint8_t *st = smem + s * L.bytes;
 #pragma unroll
                 for (int kk = 0; kk < 2; ++kk) {
+                    const uint8_t *wb = st + (kk ? wbase1 : wbase0);
+                    const uint8_t *sb = st + (kk ? sbase1 : sbase0);
                     uint4 w[RT][2][NACC];
                     uint32_t sv[RT][2][NACC], bv[RT][2][NACC];
 #pragma unroll
@@ -860,13 +855,16 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
                         for (int h = 0; h < 2; ++h)
 #pragma unroll
                             for (int a = 0; a < NACC; ++a) {
-                                w[r][h][a] = *reinterpret_cast<const uint4 *>(
-                                    st + a * L.set_bytes + wo[kk][r][h]);
-                                const uint8_t *sp = st + so[kk][r][h] + a * set_s_delta;
-                                sv[r][h][a] = *reinterpret_cast<const uint16_t *>(sp);
-                                bv[r][h][a] = *reinterpret_cast<const uint16_t *>(sp + bias_delta);
+                                constexpr int kSet = kRows * kTStageWords * 4;
+                                const int ro = (16 * r + 8 * h);
+                                w[r][h][a] = *reinterpret_cast<const uint4 *>(wb + a * kSet + ro * 128);
+                                sv[r][h][a] = *reinterpret_cast<const uint16_t *>(
+                                    sb + (a * 2 + 0) * kRows * 16 + ro * 16);
+                                bv[r][h][a] = *reinterpret_cast<const uint16_t *>(
+                                    sb + (a * 2 + 1) * kRows * 16 + ro * 16);
                             }
-                    compute_kb_smem<BITS, NT, RT, NACC>(acc, w, sv, bv, st, xo[kk]);
+                    compute_kb_smem<BITS, NT, RT, NACC>(acc, w, sv, bv, st + kk * kCodesPerKb * 2,
+                                                       xo);
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
