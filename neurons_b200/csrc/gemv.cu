@@ -731,58 +731,72 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
 
     if (warp == kTConsumers) {
         // ------------------------------------------------------ producer warp
-        if (!indexed) pdl_wait();  // the activations may come from the previous kernel
+        // Weights and scales never depend on the previous kernel on the stream,
+        // activations may: the first ring of weight boxes and scale spans is
+        // issued before griddepcontrol.wait, so with programmatic dependent
+        // launch this projection's weight stream overlaps the previous kernel.
+        const int total = nst * passes;
+        const int32_t row0 = (int32_t)((int64_t)e * prm.N + n_base);
+        const int chunks = L.x_row_bytes / 16;  // 16-byte chunks per token row
+        auto issue_weights = [&](int t) {
+            const int s = t % kStages;
+            uint8_t *st = smem + s * L.bytes;
+            const int pass = t / nst;
+            const int stage = st_lo + (t - pass * nst);
+            if (lane == 0) {
+                mbar_expect_tx(&full[s], NACC * L.set_bytes);
+                tma_load_2d(st, &tm_w, &full[s], stage * kTStageWords, row0);
+                if (DUAL) tma_load_2d(st + L.set_bytes, &tm_w2, &full[s], stage * kTStageWords, row0);
+            }
+            const int grp0 = (stage * kCodesPerStage) >> prm.gs_shift;
+            for (int q = lane; q < NACC * 2 * kRows; q += 32) {
+                const int a = q / (2 * kRows), sb = (q / kRows) & 1, r = q % kRows;
+                const int64_t rc = min(n_base + r, prm.N - 1) + (int64_t)e * prm.N;
+                const uint16_t *base = sb ? (a ? prm.b2 : prm.b) : (a ? prm.s2 : prm.s);
+                cp_async(st + L.s_off + q * 16, base + rc * prm.G + grp0, L.s_row_bytes,
+                         L.s_row_bytes);
+            }
+        };
+        auto issue_acts = [&](int t) {
+            const int s = t % kStages;
+            uint8_t *st = smem + s * L.bytes;
+            const int pass = t / nst;
+            const int stage = st_lo + (t - pass * nst);
+            const int m0 = pass * mx;
+            const int code0 = stage * kCodesPerStage;
+            for (int tk = 0; tk < mx; ++tk) {
+                const int m = m0 + tk;
+                const uint16_t *src = prm.x;
+                int nbytes = 0;
+                if (m < Mp) {
+                    const int64_t row = prm.x_rows ? (int64_t)prm.x_rows[off + m]
+                                        : (prm.x_from_offset ? (int64_t)off + m
+                                                             : (int64_t)xi * prm.M + m);
+                    src = prm.x + row * prm.x_ld + code0;
+                    nbytes = 16;
+                }
+                uint8_t *xdst = st + L.x_off + tk * L.x_row_bytes;
+                for (int ch = lane; ch < chunks; ch += 32)
+                    cp_async(xdst + ((ch ^ (tk & 7)) << 4), src + (nbytes ? ch * 8 : 0), 16, nbytes);
+            }
+            cp_async_arrive(&full[s]);  // this lane's copies of the stage, weights included
+        };
+        int t = 0;
         if (nst > 0) {
             if (lane == 0) {
                 prefetch_tmap(&tm_w);
                 if (DUAL) prefetch_tmap(&tm_w2);
             }
-            const int32_t row0 = (int32_t)((int64_t)e * prm.N + n_base);
-            const int chunks = L.x_row_bytes / 16;  // 16-byte chunks per token row
-            const int total = nst * passes;
-            int t = 0;
-            for (; t < total; ++t) {
+            const int pre = min(total, kStages);  // ring slots free at start: no wait
+            for (int u = 0; u < pre; ++u) issue_weights(u);
+            if (!indexed) pdl_wait();
+            for (int u = 0; u < pre; ++u) issue_acts(u);
+            for (t = pre; t < total; ++t) {
                 const int s = t % kStages;
                 const uint32_t ph = (uint32_t)(t / kStages) & 1u;
                 if (!tma_wait(&empty[s], ph ^ 1u, abort, prm.err)) break;
-                uint8_t *st = smem + s * L.bytes;
-                const int pass = t / nst;
-                const int stage = st_lo + (t - pass * nst);
-                const int m0 = pass * mx;
-                if (lane == 0) {
-                    mbar_expect_tx(&full[s], NACC * L.set_bytes);
-                    tma_load_2d(st, &tm_w, &full[s], stage * kTStageWords, row0);
-                    if (DUAL)
-                        tma_load_2d(st + L.set_bytes, &tm_w2, &full[s], stage * kTStageWords, row0);
-                }
-                // activation slice: mx token rows of `chunks` 16-byte chunks, chunk ^ (token & 7)
-                const int code0 = stage * kCodesPerStage;
-                for (int tk = 0; tk < mx; ++tk) {
-                    const int m = m0 + tk;
-                    const uint16_t *src = prm.x;
-                    int nbytes = 0;
-                    if (m < Mp) {
-                        const int64_t row = prm.x_rows ? (int64_t)prm.x_rows[off + m]
-                                            : (prm.x_from_offset ? (int64_t)off + m
-                                                                 : (int64_t)xi * prm.M + m);
-                        src = prm.x + row * prm.x_ld + code0;
-                        nbytes = 16;
-                    }
-                    uint8_t *xdst = st + L.x_off + tk * L.x_row_bytes;
-                    for (int ch = lane; ch < chunks; ch += 32)
-                        cp_async(xdst + ((ch ^ (tk & 7)) << 4), src + (nbytes ? ch * 8 : 0), 16,
-                                 nbytes);
-                }
-                // scale / bias spans: [set][scale|bias][row], L.s_row_bytes each
-                const int grp0 = code0 >> prm.gs_shift;
-                for (int q = lane; q < NACC * 2 * kRows; q += 32) {
-                    const int a = q / (2 * kRows), sb = (q / kRows) & 1, r = q % kRows;
-                    const int64_t rc = min(n_base + r, prm.N - 1) + (int64_t)e * prm.N;
-                    const uint16_t *base = sb ? (a ? prm.b2 : prm.b) : (a ? prm.s2 : prm.s);
-                    cp_async(st + L.s_off + q * 16, base + rc * prm.G + grp0, L.s_row_bytes,
-                             L.s_row_bytes);
-                }
-                cp_async_arrive(&full[s]);
+                issue_weights(t);
+                issue_acts(t);
             }
             // every issued copy must land before the CTA may exit
             for (int u = (t > kStages ? t - kStages : 0); u < t; ++u)
@@ -911,6 +925,7 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
                 }
                 cl.sync();
             }
+            if (!indexed) pdl_wait();  // (no-op once the producer's copies landed)
             if (blockIdx.y == 0) {
 #pragma unroll
                 for (int r = 0; r < RT; ++r)
@@ -1022,7 +1037,11 @@ cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
     // ---- asynchronously fed kernel (the default)
     if (q.K % 256 == 0 && !(q.bits == 8 && q.gs == 128) &&
         (reinterpret_cast<uintptr_t>(q.x) & 15) == 0 && q.x_ld % 8 == 0) {
-        const int rt_t = (!dual && nt == 1) ? 2 : 1;
+        // 32 rows per consumer warp (shares the activation work between two
+        // row tiles) unless that leaves fewer than ~2 CTAs per SM
+        const int rt_t = (!dual && nt == 1 && ((q.N + 127) / 128) * (int64_t)q.P >= 2 * sm_count())
+                             ? 2
+                             : 1;
         const int rows_cta = kTConsumers * 16 * rt_t;
         CUtensorMap m1, m2;
         const uint64_t rows = (uint64_t)q.E * (uint64_t)q.N;
