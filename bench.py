@@ -8,6 +8,7 @@ quantized with the min/max scheme, activations N(0, 1) in bf16, seeded):
   prefill  x [2048, 4096] . W[14336, 4096]^T   (the headline, TFLOP/s)
   square   x [2048, 4096] . W[4096, 4096]^T    (TFLOP/s)
   decode   x [1, 4096]    . W[4096, 4096]^T    (GB/s of algorithmic bytes)
+  lmhead   x [1, 3072]    . W[128256, 3072]^T  (GB/s; a 4-bit tied LM head)
 A step is one quantized_matmul call through the C ABI.  Each rank runs its
 own full step on its own GPU (token batches are independent: no collective on
 the data path, weak scaling); the timed region is bracketed by a barrier and a
@@ -43,6 +44,7 @@ WORKLOADS = {
     "prefill": dict(M=2048, N=14336, K=4096),
     "square": dict(M=2048, N=4096, K=4096),
     "decode": dict(M=1, N=4096, K=4096),
+    "lmhead": dict(M=1, N=128256, K=3072),
 }
 BITS, GS = 4, 64
 L2_BYTES = 126 * 1024 * 1024
@@ -322,6 +324,11 @@ def ours(args):
                 "frac": achieved / pk["hbm_gbs"], "peak_source": pk["source"],
                 "algorithmic_bytes_per_launch": byts}
     roof["traffic"] = ncu_traffic(args.workload)
+    if args.kernel_only:
+        if rank == 0:
+            print(json.dumps({"workload": args.workload, "value": value, "unit": unit,
+                              "roofline": roof, "clocks": clk}), flush=True)
+        return
     line = {"metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": t_dev / args.steps * 1e3, "higher_is_better": True,
@@ -401,6 +408,8 @@ def main():
     ap.add_argument("--workload", default="prefill", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-line")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="only the device-resident timed loop (a small target for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

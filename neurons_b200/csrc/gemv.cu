@@ -1062,8 +1062,9 @@ cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
             // problem's tokens fit one pass) may split: see the kernel.
             const int64_t target = (int64_t)sm_count() * 4;
             int ksplit = 1;
+            const int kmax = max_m > 1 ? 4 : 8;  // measured: deeper splits only pay at M = 1
             if (max_m <= prm.mx)
-                while (ksplit < 8 && tasks * ksplit < target && n_stg >= 4 * ksplit) ksplit <<= 1;
+                while (ksplit < kmax && tasks * ksplit < target && n_stg >= 4 * ksplit) ksplit <<= 1;
             prm.s_cta = 1;
             dim3 grid((unsigned)row_blocks, (unsigned)ksplit, (unsigned)q.P);
             if (q.bits == 4)
