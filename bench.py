@@ -270,30 +270,57 @@ def time_e2e(M, N, K, steps, warmup, world, seed):
     return total, M * K * 2, M * N * 2
 
 
-def cpu_baseline(M, N, K, target_s=12.0):
-    """The oracle's qmm on every host thread, on a bounded sample of the workload:
-    all M tokens against a slice of the weight rows, sized for ~target_s seconds."""
-    import numpy as np
-    from oracle import oracle as O
-    rng = np.random.default_rng(0)
-    threads = O.max_threads()
-    x = O.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+class CpuSample:
+    """The oracle's qmm on every host thread over all M tokens and a slice of the
+    weight rows.  `calibrate` grows the slice until one call takes about
+    target_s seconds (never more than the N rows of the workload); `time` then
+    re-times that same call."""
 
-    def run(rows):
-        wq, s, b = O.quantize((rng.standard_normal((rows, K)) * 0.02).astype(np.float32),
-                              BITS, GS, O.SCHEME_MINMAX)
+    def __init__(self, M, N, K):
+        import numpy as np
+        from oracle import oracle as O
+        self.O, self.np = O, np
+        self.M, self.N, self.K = M, N, K
+        self.rng = np.random.default_rng(0)
+        self.threads = O.max_threads()
+        self.x = O.f32_to_bf16(self.rng.standard_normal((M, K)).astype(np.float32))
+        self.rows = 0
+        self.w = None
+
+    def _prepare(self, rows):
+        np, O = self.np, self.O
+        self.w = O.quantize((self.rng.standard_normal((rows, self.K)) * 0.02).astype(np.float32),
+                            BITS, GS, O.SCHEME_MINMAX)
+        self.rows = rows
+
+    def time(self):
+        wq, s, b = self.w
         t = time.perf_counter()
-        O.qmm(x, wq, s, b, BITS, GS, nthreads=threads)
+        self.O.qmm(self.x, wq, s, b, BITS, GS, nthreads=self.threads)
         return time.perf_counter() - t
 
-    probe_rows = 8 if M > 1 else 512
-    dt = run(probe_rows)
-    rows = int(min(N, max(probe_rows, probe_rows * target_s / max(dt, 1e-6))))
-    dt = run(rows)
-    flops = algo_flops(M, rows, K)
-    byts = algo_bytes(M, rows, K)
-    return {"rows": rows, "seconds": dt, "threads": threads, "tflops": flops / dt / 1e12,
-            "gbs": byts / dt / 1e9}
+    def calibrate(self, target_s):
+        rows = 8 if self.M > 1 else 512
+        while True:
+            self._prepare(rows)
+            dt = self.time()
+            if dt >= min(0.5, target_s / 4) or rows >= self.N:
+                break
+            rows = min(self.N, rows * 4)
+        if dt < target_s and rows < self.N:
+            self._prepare(int(min(self.N, rows * target_s / dt)))
+        return self
+
+    def result(self, dt):
+        return {"rows": self.rows, "seconds": dt, "threads": self.threads,
+                "tflops": algo_flops(self.M, self.rows, self.K) / dt / 1e12,
+                "gbs": algo_bytes(self.M, self.rows, self.K) / dt / 1e9}
+
+
+def cpu_baseline(M, N, K, target_s=12.0):
+    """One bounded sample of the workload on the host cores, ~target_s seconds."""
+    smp = CpuSample(M, N, K).calibrate(target_s)
+    return smp.result(smp.time())
 
 
 def ours(args):
@@ -377,12 +404,16 @@ def reference(args):
         return
     wl = WORKLOADS[args.workload]
     M, N, K = wl["M"], wl["N"], wl["K"]
+    # Each step re-times one bounded sample; the sample is sized so that the
+    # whole run (warm-up included) takes about two and a half minutes.
+    per_step = min(4.0, max(0.1, 150.0 / (args.steps + args.warmup)))
+    smp = CpuSample(M, N, K).calibrate(per_step)
     samples = []
-    cb = None
     for i in range(args.warmup + args.steps):
-        cb = cpu_baseline(M, N, K, target_s=4.0 if i >= args.warmup else 1.0)
+        dt = smp.time()
         if i >= args.warmup:
-            samples.append(cb)
+            samples.append(smp.result(dt))
+    cb = samples[-1]
     unit = "TFLOP/s" if M > 1 else "GB/s"
     v = statistics.mean(c["tflops"] if M > 1 else c["gbs"] for c in samples)
     sec = statistics.mean(c["seconds"] for c in samples)
