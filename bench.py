@@ -270,6 +270,60 @@ def time_e2e(M, N, K, steps, warmup, world, seed):
     return total, M * K * 2, M * N * 2
 
 
+LLAMA3B = dict(hidden=3072, n_heads=24, n_kv=8, head_dim=128, inter=8192, layers=28,
+               vocab=128256)
+
+
+def time_replay(tokens, warmup, world, seed, clocks=None):
+    """Llama-3.2-3B decode replay (28 layers x 7 projections + the 4-bit LM head,
+    M=1): one CUDA graph holds one token's 197 quantized_matmul launches and is
+    replayed `tokens` times.  The 1.8 GB of weights dwarf the L2, so every token
+    reads them from HBM.  Returns (seconds, max over ranks; replay object)."""
+    import torch
+    import neurons_b200 as nb
+    from neurons_b200.replay import LlamaDecodeReplay
+    rp = LlamaDecodeReplay(**LLAMA3B, bits=BITS, group_size=GS, seed=seed)
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    rp.x.copy_(torch.randn(rp.x.shape, device="cuda", generator=g).to(torch.bfloat16))
+    rp.step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        rp.step()
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    barrier(world)
+    torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(tokens):
+        graph.replay()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop() if clocks is not None else None
+    barrier(world)
+    assert nb.take_device_error() == 0
+    total = t0.elapsed_time(t1) / 1e3
+    del graph
+    return max_over_ranks(total, world), rp, clk
+
+
+def replay_summary(t, tokens, rp, world, pk):
+    byts = rp.algorithmic_bytes()
+    gbs = world * byts * tokens / t / 1e9
+    return {"workload": "Llama-3.2-3B decode replay: 28 layers x (q,k,v,o,gate,up,down) + "
+                        "4-bit LM head, M=1, one CUDA graph per token",
+            "unit": "GB/s", "value": gbs, "tokens_per_s": world * tokens / t,
+            "us_per_token": t / tokens * 1e6, "frac": gbs / world / pk["hbm_gbs"],
+            "algorithmic_bytes_per_token": byts, "launches_per_token": rp.launches_per_token(),
+            "tokens": tokens}
+
+
 class CpuSample:
     """The oracle's qmm on every host thread over all M tokens and a slice of the
     weight rows.  `calibrate` grows the slice until one call takes about
@@ -328,9 +382,11 @@ def ours(args):
     world, rank, local = dist_setup(args.gpus)
     import neurons_b200 as nb
     nb.lib()
+    pk = peaks()
+    if args.workload == "llama3b-decode":
+        return ours_replay(args, world, rank, local, pk)
     wl = WORKLOADS[args.workload]
     M, N, K = wl["M"], wl["N"], wl["K"]
-    pk = peaks()
     t_dev, per_launch, sets, clk = time_device(M, N, K, args.steps, args.warmup, world,
                                                seed=rank, clocks=ClockSampler(local))
     flops, byts = algo_flops(M, N, K), algo_bytes(M, N, K)
@@ -377,6 +433,11 @@ def ours(args):
                           "kernel_gbs": db / pl_d / 1e9, "frac": db / pl_d / 1e9 / pk["hbm_gbs"],
                           "us_per_launch": pl_d * 1e6, "algorithmic_bytes_per_launch": db}
         line["gpu_launches"] += dsteps
+    if args.workload == "prefill" and not args.no_decode:
+        t_r, rp, _ = time_replay(50, 3, world, seed=rank + 200)
+        line["llama3b_decode"] = replay_summary(t_r, 50, rp, world, pk)
+        line["gpu_launches"] += 50 * rp.launches_per_token()
+        del rp
     t_e, h2d, d2h = time_e2e(M, N, K, min(args.steps, 50), args.warmup, world, seed=rank)
     e2e_val = world * (flops if M > 1 else byts) * min(args.steps, 50) / t_e / (
         1e12 if M > 1 else 1e9)
@@ -397,12 +458,69 @@ def ours(args):
         print(json.dumps(line), flush=True)
 
 
+def ours_replay(args, world, rank, local, pk):
+    """--workload llama3b-decode: the replay alone, value in GB/s of algorithmic
+    bytes (weights + activations) per token."""
+    import torch
+    t, rp, clk = time_replay(args.steps, args.warmup, world, seed=rank,
+                             clocks=ClockSampler(local))
+    s = replay_summary(t, args.steps, rp, world, pk)
+    byts = rp.algorithmic_bytes()
+    roof = {"bound": "hbm", "achieved": byts * args.steps / t / 1e9, "peak": pk["hbm_gbs"],
+            "unit": "GB/s", "frac": s["frac"], "peak_source": pk["source"],
+            "algorithmic_bytes_per_launch": byts / rp.launches_per_token(),
+            "note": "whole-token average over the 197 launches of one graph",
+            "traffic": ncu_traffic("llama3b-decode")}
+    # End to end: the token's input row from pinned host memory, the logits back.
+    xh = torch.randn(rp.x.shape).to(torch.bfloat16).pin_memory()
+    lh = torch.empty(rp.logits.shape, dtype=torch.bfloat16).pin_memory()
+    stream = torch.cuda.current_stream()
+    n_e = min(args.steps, 50)
+    for _ in range(args.warmup):
+        rp.x.copy_(xh, non_blocking=True)
+        rp.step()
+        lh.copy_(rp.logits, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(n_e):
+        rp.x.copy_(xh, non_blocking=True)
+        rp.step()
+        lh.copy_(rp.logits, non_blocking=True)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    t_e = max_over_ranks(t0.elapsed_time(t1) / 1e3, world)
+    line = {"metric": METRIC, "value": s["value"], "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) weights quantized 4-bit g64, N(0,1) bf16 x)",
+            "config": {"workload": "llama3b-decode", **LLAMA3B, "bits": BITS, "group_size": GS,
+                       "tokens_per_s": s["tokens_per_s"], "us_per_token": s["us_per_token"],
+                       "parallelism": f"replicas x{world}",
+                       "l2": "1.8 GB of weights per token (> L2)"},
+            "roofline": roof, "gpu_launches": args.steps * rp.launches_per_token()
+            + n_e * rp.launches_per_token(), "clocks": clk,
+            "e2e": {"value": world * byts * n_e / t_e / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": rp.x.numel() * 2,
+                    "d2h_bytes_per_step": rp.logits.numel() * 2,
+                    "note": "eager launches (no graph), host copies inside the timed region"}}
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    wl = WORKLOADS[args.workload]
+    # The replay's CPU sample is its largest projection shape (gate/up, 3072 -> 8192).
+    wl = WORKLOADS.get(args.workload, dict(M=1, N=8192, K=3072))
     M, N, K = wl["M"], wl["N"], wl["K"]
     # Each step re-times one bounded sample; the sample is sized so that the
     # whole run (warm-up included) takes about two and a half minutes.
@@ -436,7 +554,7 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="prefill", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="prefill", choices=sorted(WORKLOADS) + ["llama3b-decode"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-line")
     ap.add_argument("--kernel-only", action="store_true",
