@@ -324,6 +324,101 @@ def replay_summary(t, tokens, rp, world, pk):
             "tokens": tokens}
 
 
+QWEN3_MOE = dict(E=128, top_k=8, H=2048, I=768)
+
+
+def moe_weights(E, H, I, gen):
+    import torch
+    import neurons_b200 as nb
+    out = []
+    for n, k in ((I, H), (I, H), (H, I)):
+        w = torch.randn(E, n, k, device="cuda", generator=gen) * 0.02
+        out.append(nb.quantize(w, GS, BITS, nb.SCHEME_MINMAX))
+        del w
+    return out
+
+
+def time_moe(T, steps, warmup, world, seed, clocks=None):
+    """Qwen3-30B-A3B MoE switch step (router + gate/up/down gather_qmm + SwiGLU +
+    weighted sum) for T tokens.  Three weight sets (1 GB) rotate so experts are
+    read from HBM; T <= 64 steps are captured in one CUDA graph.
+    Returns (seconds for `steps` steps, max over ranks; algorithmic bytes and
+    flops per step, averaged over the steps)."""
+    import torch
+    import neurons_b200 as nb
+    E, k, H, I = (QWEN3_MOE[x] for x in ("E", "top_k", "H", "I"))
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    sets = []
+    for _ in range(3):
+        gate, up, down = moe_weights(E, H, I, g)
+        x = torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16)
+        logits = torch.randn(T, E, device="cuda", generator=g).to(torch.bfloat16)
+        ws = torch.empty(max(nb.moe_workspace_size(T, E, k, H, I), 1), dtype=torch.uint8,
+                         device="cuda")
+        idx = torch.empty(T, k, dtype=torch.int32, device="cuda")
+        sc = torch.empty(T, k, dtype=torch.float32, device="cuda")
+        y = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+        sets.append((x, logits, gate, up, down, ws, idx, sc, y))
+    lib = nb.lib()
+
+    def step(i):
+        x, logits, gate, up, down, ws, idx, sc, y = sets[i % 3]
+        nb.ops.check(lib.nq_moe_route(nb.ops._ptr(logits), T, E, k, nb.ops._ptr(idx),
+                                      nb.ops._ptr(sc), nb.ops._stream()))
+        nb.moe_switch(x, idx, sc, gate, up, down, GS, BITS, workspace=ws, out=y)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    graph = None
+    if T <= 64:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(steps):
+                step(i)
+        graph.replay()
+        torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    barrier(world)
+    torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    if graph is not None:
+        graph.replay()
+    else:
+        for i in range(steps):
+            step(i)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop() if clocks is not None else None
+    barrier(world)
+    assert nb.take_device_error() == 0
+    per_expert = sum(t.numel() * t.element_size() for t in sets[0][2] + sets[0][3] + sets[0][4]) // E
+    byts = 0
+    for i in range(steps):
+        x, logits, gate, up, down, ws, idx, sc, y = sets[i % 3]
+        touched = int(torch.unique(idx).numel())
+        byts += touched * per_expert + T * H * 2 * 2 + T * E * 2
+    byts /= steps
+    flops = 2 * T * k * 3 * I * H
+    total = t0.elapsed_time(t1) / 1e3
+    del graph
+    return max_over_ranks(total, world), byts, flops, clk
+
+
+def moe_summary(T, t, steps, byts, flops, world, pk):
+    sec = t / steps
+    d = {"T": T, "us_per_step": sec * 1e6, "gbs": world * byts / sec / 1e9,
+         "tflops": world * flops / sec / 1e12, "algorithmic_bytes_per_step": byts,
+         "flops_per_step": flops}
+    d["frac_hbm"] = byts / sec / 1e9 / pk["hbm_gbs"]
+    d["frac_tensor"] = flops / sec / 1e12 / pk["bf16_tflops"]
+    return d
+
+
 class CpuSample:
     """The oracle's qmm on every host thread over all M tokens and a slice of the
     weight rows.  `calibrate` grows the slice until one call takes about
@@ -433,6 +528,14 @@ def ours(args):
                           "kernel_gbs": db / pl_d / 1e9, "frac": db / pl_d / 1e9 / pk["hbm_gbs"],
                           "us_per_launch": pl_d * 1e6, "algorithmic_bytes_per_launch": db}
         line["gpu_launches"] += dsteps
+    if args.workload == "prefill" and not args.no_moe:
+        moe = {"workload": "Qwen3-30B-A3B MoE switch step (E=128, top-8, H=2048, I=768), "
+                           "router + gate/up/down + SwiGLU + weighted sum"}
+        for T, n in ((1, 500), (64, 200), (2048, 20)):
+            t_m, b_m, f_m, _ = time_moe(T, n, 3, world, seed=rank + 300 + T)
+            moe[f"T{T}"] = moe_summary(T, t_m, n, b_m, f_m, world, pk)
+            line["gpu_launches"] += n * (7 if T * 8 > 128 else 5)
+        line["moe"] = moe
     if args.workload == "prefill" and not args.no_decode:
         t_r, rp, _ = time_replay(50, 3, world, seed=rank + 200)
         line["llama3b_decode"] = replay_summary(t_r, 50, rp, world, pk)
@@ -556,7 +659,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="prefill", choices=sorted(WORKLOADS) + ["llama3b-decode"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-line")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-lines")
+    ap.add_argument("--no-moe", action="store_true", help="skip the MoE sub-line")
     ap.add_argument("--kernel-only", action="store_true",
                     help="only the device-resident timed loop (a small target for ncu)")
     args = ap.parse_args()

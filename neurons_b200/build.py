@@ -20,7 +20,7 @@ LIB = os.path.join(HERE, "libnq.so")
 ROOT = os.path.dirname(HERE)
 INCLUDE = os.path.join(ROOT, "include")
 
-CU_SOURCES = ["abi.cu", "quant.cu", "gemv.cu", "gemm_tc.cu", "moe.cu"]
+CU_SOURCES = ["abi.cu", "quant.cu", "gemv.cu", "gemm_tc.cu", "gemm_tc_moe.cu", "moe.cu"]
 CPP_SOURCES = ["cuda_backend.cpp"]
 HEADERS = ["nq_common.cuh", "nq_internal.h", "cuda_backend.h", "compute_types.h"]
 

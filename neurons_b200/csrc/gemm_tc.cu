@@ -345,6 +345,8 @@ bool make_map_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint6
 }
 
 
+bool tensor_maps_available() { return encode_fn() != nullptr; }
+
 bool tc_gemm_supported(const TcGemmArgs &a) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0) return false;
     if (a.bits != 4 && a.bits != 8) return false;

@@ -1032,7 +1032,8 @@ cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
 
     const bool dual = q.w2 != nullptr;
     const int max_m = std::max(1, q.max_m);
-    const int nt = max_m <= 8 ? 1 : (max_m <= 16 ? 2 : 4);
+    const int size_m = q.tile_m > 0 ? std::min(q.tile_m, max_m) : max_m;
+    const int nt = size_m <= 8 ? 1 : (size_m <= 16 ? 2 : 4);
 
     // ---- asynchronously fed kernel (the default)
     if (q.K % 256 == 0 && !(q.bits == 8 && q.gs == 128) &&

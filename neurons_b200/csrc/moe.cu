@@ -83,12 +83,17 @@ __global__ void count_kernel(const int32_t *__restrict__ idx, int64_t pairs, int
     atomicAdd(&counts[e], 1);
 }
 
-// exclusive prefix sum over experts (single block, E <= 1024); clears cursors
+// exclusive prefix sum over experts (single block, E <= 1024); clears cursors.
+// With `tiles`, also lists the tensor-core tiles: expert e's run of grouped
+// rows [offsets[e], offsets[e] + counts[e]) cut into pieces of at most
+// kMoeTileTokens, as {e, first row, count, 0}; *n_tiles = their number.
 __global__ void scan_kernel(const int32_t *__restrict__ counts, int E, int32_t *__restrict__ offsets,
-                            int32_t *__restrict__ cursor) {
+                            int32_t *__restrict__ cursor, int4 *__restrict__ tiles,
+                            int32_t *__restrict__ n_tiles) {
     __shared__ int32_t buf[1024];
     const int t = threadIdx.x;
-    buf[t] = t < E ? counts[t] : 0;
+    const int32_t c = t < E ? counts[t] : 0;
+    buf[t] = c;
     __syncthreads();
     for (int o = 1; o < 1024; o <<= 1) {
         const int32_t v = t >= o ? buf[t - o] : 0;
@@ -96,10 +101,27 @@ __global__ void scan_kernel(const int32_t *__restrict__ counts, int E, int32_t *
         buf[t] += v;
         __syncthreads();
     }
+    const int32_t off = buf[t] - c;
     if (t < E) {
-        offsets[t] = buf[t] - counts[t];
+        offsets[t] = off;
         cursor[t] = 0;
     }
+    if (tiles == nullptr) return;
+    const int32_t nt = (c + kMoeTileTokens - 1) / kMoeTileTokens;
+    __syncthreads();
+    buf[t] = nt;
+    __syncthreads();
+    for (int o = 1; o < 1024; o <<= 1) {
+        const int32_t v = t >= o ? buf[t - o] : 0;
+        __syncthreads();
+        buf[t] += v;
+        __syncthreads();
+    }
+    const int32_t first = buf[t] - nt;
+    for (int i = 0; i < nt; ++i)
+        tiles[first + i] = make_int4(t, off + i * kMoeTileTokens,
+                                     min(kMoeTileTokens, c - i * kMoeTileTokens), 0);
+    if (t == 1023) *n_tiles = buf[1023];
 }
 
 // place every pair at offsets[e] + rank; the rank order inside an expert does
@@ -147,10 +169,17 @@ inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 // Workspace layout (each region 256-byte aligned), P = T * top_k pairs:
 //   counts[E], offsets[E], cursor[E], pos_token[P], pos_pair[P]   int32
+//   tiles[max_tiles] int4, n_tiles int32   (tensor-core tile list)
 //   h[P, I]  bf16      (SwiGLU activations, grouped or pair order)
 //   d[P, H]  fp32      (down-projection sums, pair order)
+int64_t max_moe_tiles(int64_t P, int64_t E) {
+    return (P + kMoeTileTokens - 1) / kMoeTileTokens + std::min<int64_t>(E, P);
+}
+
 struct MoeWorkspace {
     int32_t *counts, *offsets, *cursor, *pos_token, *pos_pair;
+    int4 *tiles;
+    int32_t *n_tiles;
     uint16_t *h;
     float *d;
     size_t bytes;
@@ -170,6 +199,8 @@ MoeWorkspace carve(void *base, int64_t T, int64_t E, int64_t top_k, int64_t H, i
     w.cursor = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * E));
     w.pos_token = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * P));
     w.pos_pair = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * P));
+    w.tiles = reinterpret_cast<int4 *>(take(sizeof(int4) * max_moe_tiles(P, E)));
+    w.n_tiles = reinterpret_cast<int32_t *>(take(sizeof(int32_t)));
     w.h = reinterpret_cast<uint16_t *>(take(sizeof(uint16_t) * P * I));
     w.d = reinterpret_cast<float *>(take(sizeof(float) * P * H));
     w.bytes = off;
@@ -207,6 +238,9 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
     const int thr = 256;
     const unsigned pblocks = (unsigned)((P + thr - 1) / thr);
     const bool grouped = P > E;
+    // Tensor-core path once experts average >= 16 tokens (a 16-column MMA);
+    // below that the grouped GEMV streams each expert's weights once.
+    const bool use_tc = grouped && P >= 16 * E && tc_moe_supported(bits, gsz, H, I, E, x, H);
     cudaError_t e;
 
     GemvProblems up;
@@ -230,10 +264,49 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
         if ((e = cudaMemsetAsync(ws.counts, 0, sizeof(int32_t) * E, stream)) != cudaSuccess)
             return e;
         count_kernel<<<pblocks, thr, 0, stream>>>(idx, P, (int)E, ws.counts, err);
-        scan_kernel<<<1, 1024, 0, stream>>>(ws.counts, (int)E, ws.offsets, ws.cursor);
+        scan_kernel<<<1, 1024, 0, stream>>>(ws.counts, (int)E, ws.offsets, ws.cursor,
+                                            use_tc ? ws.tiles : nullptr, ws.n_tiles);
         fill_kernel<<<pblocks, thr, 0, stream>>>(idx, P, (int)top_k, (int)E, ws.offsets, ws.cursor,
                                                   ws.pos_token, ws.pos_pair);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if (use_tc) {
+            TcMoeArgs a;
+            a.up = true;
+            a.bits = bits;
+            a.gs = gsz;
+            a.E = E;
+            a.N = I;
+            a.K = H;
+            a.w1 = gw; a.s1 = gs_; a.b1 = gb;
+            a.w2 = uw; a.s2 = us; a.b2 = ub;
+            a.x = x;
+            a.x_ld = H;
+            a.x_rows_total = T;
+            a.rows = ws.pos_token;
+            a.tiles = ws.tiles;
+            a.n_tiles = ws.n_tiles;
+            a.max_tiles = max_moe_tiles(P, E);
+            a.y = ws.h;
+            a.y_ld = I;
+            if ((e = launch_tc_moe(a, stream)) != cudaSuccess) return e;
+            TcMoeArgs d = a;
+            d.up = false;
+            d.N = H;
+            d.K = I;
+            d.w1 = dw; d.s1 = ds; d.b1 = db;
+            d.w2 = nullptr; d.s2 = nullptr; d.b2 = nullptr;
+            d.x = ws.h;
+            d.x_ld = I;
+            d.x_rows_total = P;
+            d.rows = ws.pos_pair;
+            d.y = ws.d;
+            d.y_ld = H;
+            if ((e = launch_tc_moe(d, stream)) != cudaSuccess) return e;
+            const int64_t n4 = T * (H / 4);
+            combine_kernel<<<(unsigned)((n4 + thr - 1) / thr), thr, 0, stream>>>(ws.d, scores, T, H,
+                                                                                  (int)top_k, y);
+            return cudaGetLastError();
+        }
         // gate/up: problem = expert, its tokens gathered from x, h rows in grouped order
         up.P = (int)E;
         up.expert_is_p = true;
@@ -241,6 +314,9 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
         up.m_offset = ws.offsets;
         up.x_rows = ws.pos_token;
         up.max_m = (int)T;  // an expert sees each token at most once
+        // token tile sized for the average expert (P / E); busier experts take
+        // more passes over their (then L2-resident) weights
+        up.tile_m = (int)std::min<int64_t>(32, std::max<int64_t>(8, 2 * ((P + E - 1) / E)));
         // down: problem = expert, rows of h in grouped order, d rows by pair id
         dn.P = (int)E;
         dn.expert_is_p = true;
@@ -249,6 +325,7 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
         dn.x_from_offset = true;
         dn.y_rows = ws.pos_pair;
         dn.max_m = up.max_m;
+        dn.tile_m = up.tile_m;
     } else {
         pair_token_kernel<<<pblocks, thr, 0, stream>>>(P, (int)top_k, ws.pos_token);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;

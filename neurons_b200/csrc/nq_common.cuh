@@ -284,6 +284,47 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int mma_m, int mma_n) {
            | ((uint32_t)(mma_m >> 4) << 24);      // M >> 4
 }
 
+// Bounded wait on an mbarrier phase shared by the roles of one CTA.  Gives up
+// when another role raised *abort, or after kWaitLimitNs: then it raises
+// *abort and the timeout bit of the device error word.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t *bar, uint32_t parity,
+                                                   volatile int *abort, unsigned int *err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_timer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            *abort = 1;
+            atomicOr(err, kErrWaitTimeout);
+            return false;
+        }
+    }
+}
+
+// 16-byte cp.async global -> shared (L2 only); src_bytes 0 writes zeros.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy reads (tcgen05.mma operands, TMA stores).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Named barrier over `count` threads (a multiple of 32).
+__device__ __forceinline__ void bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // Programmatic dependent launch: wait for the producing grid / let the next
 // grid start its prologue.  Both are no-ops without the launch attribute.
 __device__ __forceinline__ void pdl_wait() {

@@ -53,6 +53,7 @@ struct GemvProblems {
     int out_f32 = 0;                   // 1: fp32 output, 0: bf16 output
     int swiglu = 0;                    // 1: y = bf16(silu(x.w^T) * (x.w2^T))
     int max_m = 1;                     // upper bound of tokens per problem
+    int tile_m = 0;                    // tokens per pass to size for (0: from max_m)
 };
 
 cudaError_t launch_gemv(const GemvProblems &p, cudaStream_t stream);
@@ -80,6 +81,34 @@ bool make_map_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint6
                  uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
                  CUtensorMapSwizzle sw);
 cudaError_t launch_tc_gemm(const TcGemmArgs &a, cudaStream_t stream);
+
+// True when cuTensorMapEncodeTiled could be resolved from the driver.
+bool tensor_maps_available();
+
+// Expert-grouped tcgen05 GEMMs of the MoE switch step (gemm_tc_moe.cu).
+// A tile is {expert, first grouped row, token count <= kMoeTileTokens, 0}.
+constexpr int kMoeTileTokens = 256;
+struct TcMoeArgs {
+    bool up = true;                  // true: gate/up + SwiGLU -> h; false: down -> d (fp32)
+    int bits = 4, gs = 64;
+    int64_t E = 0, N = 0, K = 0;     // experts, weight rows per expert, reduction length
+    const uint32_t *w1 = nullptr;    // [E, N, K*bits/32] (gate, or down)
+    const uint16_t *s1 = nullptr, *b1 = nullptr;
+    const uint32_t *w2 = nullptr;    // up (up kernel)
+    const uint16_t *s2 = nullptr, *b2 = nullptr;
+    const uint16_t *x = nullptr;     // up: x [T, K]; down: h [P, K] in grouped order
+    int64_t x_ld = 0;
+    int64_t x_rows_total = 0;        // rows of x (down: P)
+    const int32_t *rows = nullptr;   // up: token of grouped row; down: pair of grouped row
+    const int4 *tiles = nullptr;
+    const int32_t *n_tiles = nullptr;
+    int64_t max_tiles = 0;           // grid bound; CTAs past *n_tiles exit at once
+    void *y = nullptr;               // up: h [P, N] bf16; down: d [P, N] fp32 (rows by pair)
+    int64_t y_ld = 0;
+};
+bool tc_moe_supported(int bits, int gs, int64_t H, int64_t I, int64_t E, const void *x,
+                      int64_t x_ld);
+cudaError_t launch_tc_moe(const TcMoeArgs &a, cudaStream_t stream);
 
 cudaError_t launch_quantize(const void *w, int w_dtype, int64_t rows, int64_t K, int bits,
                             int gs, int scheme, uint32_t *wq, uint16_t *s, uint16_t *b,

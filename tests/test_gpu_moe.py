@@ -102,15 +102,17 @@ def workspace_hidden(ws, T, E, k, H, I):
     """The SwiGLU activations h the GPU wrote into the caller-owned workspace,
     returned in pair order (t*k + j).  Follows the workspace layout of
     neurons_b200/csrc/moe.cu: counts[E], offsets[E], cursor[E], pos_token[P],
-    pos_pair[P] (int32), h[P, I] (bf16), d[P, H] (fp32), each region aligned to
-    256 bytes; h is in pair order when P <= E, else grouped by expert with
-    pos_pair giving each row's pair."""
+    pos_pair[P] (int32), tiles[ceil(P/256) + min(E, P)] (int4), n_tiles (int32),
+    h[P, I] (bf16), d[P, H] (fp32), each region aligned to 256 bytes; h is in
+    pair order when P <= E, else grouped by expert with pos_pair giving each
+    row's pair."""
     P = T * k
     a = lambda n: (n + 255) // 256 * 256
     raw = ws.cpu().numpy()
     off = 3 * a(4 * E)
     pos_pair = raw[off + a(4 * P): off + a(4 * P) + 4 * P].view(np.int32)
-    hoff = off + 2 * a(4 * P)
+    max_tiles = (P + 255) // 256 + min(E, P)
+    hoff = off + 2 * a(4 * P) + a(16 * max_tiles) + a(4)
     h = raw[hoff: hoff + 2 * P * I].view(np.uint16).reshape(P, I)
     if P <= E:
         return h.copy()
@@ -154,10 +156,13 @@ def test_golden_switch(oracle, nqlib):
 
 
 @pytest.mark.parametrize("T,E,k,H,I", [(1, 128, 8, 2048, 768), (20, 128, 8, 2048, 768),
+                                       (64, 128, 8, 2048, 768), (512, 128, 8, 2048, 768),
                                        (3, 16, 4, 256, 128), (64, 16, 4, 256, 128),
-                                       (100, 8, 2, 128, 64)])
+                                       (100, 8, 2, 128, 64), (600, 4, 2, 256, 128)])
 def test_switch_matches_oracle(oracle, nqlib, T, E, k, H, I):
-    """pair mode (T*k <= E) and grouped mode (T*k > E)."""
+    """pair mode (T*k <= E), grouped GEMV mode (E < T*k < 16 E) and the grouped
+    tensor-core mode (T*k >= 16 E; (600, 4, 2) puts ~300 tokens on every expert,
+    more than one 256-token tile)."""
     rng = np.random.default_rng(T * 31 + E)
     gate = experts(oracle, rng, E, I, H)
     up = experts(oracle, rng, E, I, H)
@@ -165,3 +170,17 @@ def test_switch_matches_oracle(oracle, nqlib, T, E, k, H, I):
     x = acts(rng, T, H)
     idx, sc = oracle.moe_route(acts(rng, T, E), k)
     staged_switch_check(oracle, x, idx, sc, gate, up, down, 4, 64, f"switch T={T} E={E}")
+
+
+@pytest.mark.parametrize("bits,gs", [(8, 32), (4, 128), (8, 64), (4, 32)])
+def test_switch_tensor_core_bits_groups(oracle, nqlib, bits, gs):
+    """The grouped tensor-core mode at every code width and group size."""
+    T, E, k, H, I = 256, 16, 4, 256, 256
+    rng = np.random.default_rng(bits * 100 + gs)
+    gate = experts(oracle, rng, E, I, H, bits, gs)
+    up = experts(oracle, rng, E, I, H, bits, gs)
+    down = experts(oracle, rng, E, H, I, bits, gs)
+    x = acts(rng, T, H)
+    idx, sc = oracle.moe_route(acts(rng, T, E), k)
+    staged_switch_check(oracle, x, idx, sc, gate, up, down, bits, gs,
+                        f"switch {bits}-bit g{gs}")
