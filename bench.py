@@ -480,6 +480,8 @@ def ours(args):
     pk = peaks()
     if args.workload == "llama3b-decode":
         return ours_replay(args, world, rank, local, pk)
+    if args.workload.startswith("moe-"):
+        return ours_moe(args, world, rank, local, pk)
     wl = WORKLOADS[args.workload]
     M, N, K = wl["M"], wl["N"], wl["K"]
     t_dev, per_launch, sets, clk = time_device(M, N, K, args.steps, args.warmup, world,
@@ -617,6 +619,27 @@ def ours_replay(args, world, rank, local, pk):
         print(json.dumps(line), flush=True)
 
 
+def ours_moe(args, world, rank, local, pk):
+    """--workload moe-<T>: the Qwen3-30B-A3B switch step alone for T tokens."""
+    T = int(args.workload.split("-")[1])
+    t, byts, flops, clk = time_moe(T, args.steps, args.warmup, world, seed=rank,
+                                   clocks=ClockSampler(local))
+    s = moe_summary(T, t, args.steps, byts, flops, world, pk)
+    tensor = T * QWEN3_MOE["top_k"] >= 16 * QWEN3_MOE["E"]
+    line = {"metric": METRIC, "value": s["tflops"] if tensor else s["gbs"],
+            "unit": "TFLOP/s" if tensor else "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": args.workload, **QWEN3_MOE, "T": T, "bits": BITS,
+                       "group_size": GS, "l2": "3 rotating weight sets of 340 MB (> L2)"},
+            "moe": s, "clocks": clk}
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -657,7 +680,8 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="prefill", choices=sorted(WORKLOADS) + ["llama3b-decode"])
+    ap.add_argument("--workload", default="prefill", choices=sorted(WORKLOADS) + ["llama3b-decode", "moe-1", "moe-64",
+                                                             "moe-2048"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-lines")
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE sub-line")

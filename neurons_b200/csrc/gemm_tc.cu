@@ -38,6 +38,7 @@ namespace {
 
 constexpr int kBlockW = 128;     // weight rows per CTA (UMMA M)
 constexpr int kBlockK = 64;      // codes per stage
+constexpr int kSbAhead = 2;       // scale/bias prefetch depth, in this warp's iterations
 constexpr int kStageArrivals = 8;   // of the 16 dequant warps, those working on one stage
 constexpr int kProducerWarp = 16;
 constexpr int kMmaWarp = 17;
@@ -182,9 +183,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bv = brow[k >> prm.gs_shift];
             }
         };
-        uint16_t s_cur, b_cur, s_nxt, b_nxt;
-        load_sb(par, s_cur, b_cur);
-        load_sb(par + 2, s_nxt, b_nxt);
+        // Scale and bias of this thread's row for its next kSbAhead stages, in
+        // a shift register: the load for a stage is issued kSbAhead of this
+        // warp's iterations before its use, which covers an HBM round trip.
+        uint16_t sq[kSbAhead], bq[kSbAhead];
+#pragma unroll
+        for (int i = 0; i < kSbAhead; ++i) load_sb(par + 2 * i, sq[i], bq[i]);
         const uint32_t t_lane = (uint32_t)(q * 32) << 16;
         for (int kb = par; kb < num_kb; kb += 2) {
             const int s = kb % S;
@@ -199,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     wst + r * 32 + 16 * (h ^ ((r >> 2) & 1)));
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
-                const Dq4 d = make_dq4(s_cur, b_cur);
+                const Dq4 d = make_dq4(sq[0], bq[0]);
                 const uint32_t words[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -220,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *reinterpret_cast<const uint4 *>(wst + r * 64 + 16 * ((2 * h + 1) ^ x));
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
-                const Dq8 d = make_dq8(s_cur, b_cur);
+                const Dq8 d = make_dq8(sq[0], bq[0]);
                 const uint32_t words[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
@@ -233,9 +237,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&afull[s]);
-            s_cur = s_nxt;
-            b_cur = b_nxt;
-            load_sb(kb + 4, s_nxt, b_nxt);
+#pragma unroll
+            for (int i = 0; i + 1 < kSbAhead; ++i) {
+                sq[i] = sq[i + 1];
+                bq[i] = bq[i + 1];
+            }
+            load_sb(kb + 2 * kSbAhead, sq[kSbAhead - 1], bq[kSbAhead - 1]);
         }
         // ------------------------------------------------ epilogue
         if (wait_or_abort(accfull, 0, abort, prm.err) && !*abort) {

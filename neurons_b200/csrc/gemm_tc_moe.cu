@@ -11,11 +11,11 @@
 //   up kernel:    h[g, n] = bf16( silu(x[tok(g)] . Wg[e, n]) * (x[tok(g)] . Wu[e, n]) )
 //                 The 128-row weight tile holds 64 gate rows (TMEM lanes
 //                 0-63) and the same 64 rows of up (lanes 64-127), so one
-//                 accumulator holds both factors of every h element.  The
-//                 tile's token rows are gathered from x with cp.async into the
-//                 128-byte-swizzled K-major layout the MMA reads.
+//                 accumulator holds both factors of every h element.  Token
+//                 rows come from xg, x copied into grouped order (moe.cu).
 //   down kernel:  d[pair(g), n] = h[g] . Wd[e, n]   (fp32)
-//                 h rows are contiguous per expert: one TMA box of 256 rows.
+// Both kernels read their token rows (xg or h, contiguous per expert) with one
+// TMA box of 256 rows x 64 bf16 per stage, 128-byte swizzled.
 //
 // The MMA's N is the tile's count rounded up to 16 (a tile wastes at most 15
 // token columns).  Roles as in the dense kernel (gemm_tc.cu): warps 0-15 turn
@@ -34,11 +34,11 @@ namespace {
 constexpr int kBlockW = 128;       // weight rows per CTA (UMMA M)
 constexpr int kBlockK = 64;        // codes per stage
 constexpr int kMaxTok = kMoeTileTokens;
+constexpr int kSbAhead = 2;       // scale/bias prefetch depth, in this warp's iterations
 constexpr int kStageArrivals = 8;  // dequant warps working on one stage
 constexpr int kProducerWarp = 16;
 constexpr int kMmaWarp = 17;
 constexpr int kThreads = 576;
-constexpr int kLookahead = 2;      // gathered stages in flight before one is published
 
 template <int BITS>
 struct MoeCfg {
@@ -49,7 +49,6 @@ struct MoeCfg {
     static constexpr int kACol0 = kMaxTok;  // accumulator: columns [0, 256)
     static constexpr int kTmemCols = 512;
     static_assert(kACol0 + kStages * 32 <= kTmemCols, "TMEM budget");
-    static_assert(kStages > kLookahead, "gather lookahead");
     static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256 + kMaxTok * 4;
     static_assert(kSmemBytes <= 232448, "shared memory budget");
     // epilogue exchange of the up kernel: 8 warp pairs x 2 buffers x [16][32] fp32
@@ -63,9 +62,7 @@ struct MoeTcParams {
     const uint16_t *s2, *b2;          // up (up kernel only)
     const int4 *tiles;                // {expert, g0, count, 0}
     const int32_t *n_tiles;
-    const uint16_t *x;                // up kernel: token rows
-    int64_t x_ld;
-    const int32_t *rows;              // up: token of grouped row; down: pair of grouped row
+    const int32_t *rows;              // down: pair of grouped row
     void *y;                          // up: h [P, N] bf16 (grouped rows); down: d [P, N] fp32
     int64_t y_ld;
     unsigned int *err;
@@ -106,13 +103,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int32_t wrow0 = (int32_t)((int64_t)e * prm.N + nbase);
     const int num_kb = prm.num_kb;
 
-    if (threadIdx.x < kMaxTok) {
+    if (!UP && threadIdx.x < kMaxTok) {
         const int t = threadIdx.x;
         rows[t] = t < cnt ? prm.rows[g0 + t] : 0;
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], UP ? 2 : 1);  // expect_tx arrival (+ the gather's publish)
+            mbar_init(&full[s], 1);  // TMA bytes of the stage landed
             mbar_init(&empty[s], 1 + kStageArrivals);
             mbar_init(&afull[s], kStageArrivals);
         }
@@ -123,7 +120,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kProducerWarp && lane == 0) {
         prefetch_tmap(&tmap_w1);
         if (UP) prefetch_tmap(&tmap_w2);
-        else prefetch_tmap(&tmap_x);
+        prefetch_tmap(&tmap_x);
     }
     if (warp == kMmaWarp) {
         tmem_alloc(tmem_holder, Cfg::kTmemCols);
@@ -135,58 +132,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = *tmem_holder;
 
     if (warp == kProducerWarp) {
-        if constexpr (UP) {
-            // Weights by TMA (two 64-row boxes); token rows gathered by the
-            // whole warp with cp.async.  A gathered stage is published (proxy
-            // fence, then an mbarrier arrival) kLookahead stages later, once
-            // its copies have landed.
-            constexpr int kHalfW = Cfg::kWStageBytes / 2;
-            const int c = lane & 7;  // this lane's 16-byte chunk of every row it copies
-            bool ok = true;
-            for (int kb = 0; kb < num_kb + kLookahead; ++kb) {
-                if (kb < num_kb && ok) {
-                    const int s = kb % S;
-                    const uint32_t ph = (uint32_t)(kb / S) & 1u;
-                    int got = 0;
-                    if (lane == 0) got = mbar_wait_or_abort(&empty[s], ph ^ 1u, abort, prm.err);
-                    ok = __shfl_sync(0xffffffffu, got, 0) != 0;
-                    if (ok) {
-                        uint8_t *wst = ws + s * Cfg::kWStageBytes;
-                        if (lane == 0) {
-                            mbar_expect_tx(&full[s], Cfg::kWStageBytes);
-                            tma_load_2d(wst, &tmap_w1, &full[s], kb * (kBlockK * BITS / 32), wrow0);
-                            tma_load_2d(wst + kHalfW, &tmap_w2, &full[s],
-                                        kb * (kBlockK * BITS / 32), wrow0);
-                        }
-                        uint8_t *xst = xs + s * Cfg::kXStageBytes;
-                        const uint16_t *xk = prm.x + (int64_t)kb * kBlockK + c * 8;
-                        for (int j = lane >> 3; j < n_mma; j += 4) {
-                            const bool live = j < cnt;
-                            const uint16_t *src = live ? xk + (int64_t)rows[j] * prm.x_ld : prm.x;
-                            cp_async16(xst + j * 128 + ((c ^ (j & 7)) << 4), src, live ? 16 : 0);
-                        }
-                    }
-                }
-                cp_async_commit();
-                if (kb >= kLookahead) {
-                    cp_async_wait_group<kLookahead>();
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0 && ok) mbar_arrive(&full[(kb - kLookahead) % S]);
-                }
-            }
-            cp_async_wait_group<0>();
-        } else {
-            if (lane == 0) {
-                for (int kb = 0; kb < num_kb; ++kb) {
-                    const int s = kb % S;
-                    const uint32_t ph = (uint32_t)(kb / S) & 1u;
-                    if (!mbar_wait_or_abort(&empty[s], ph ^ 1u, abort, prm.err)) break;
-                    mbar_expect_tx(&full[s], Cfg::kXStageBytes + Cfg::kWStageBytes);
-                    tma_load_2d(xs + s * Cfg::kXStageBytes, &tmap_x, &full[s], kb * kBlockK, g0);
-                    tma_load_2d(ws + s * Cfg::kWStageBytes, &tmap_w1, &full[s],
-                                kb * (kBlockK * BITS / 32), wrow0);
-                }
+        if (lane == 0) {
+            constexpr int kWords = kBlockK * BITS / 32;
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % S;
+                const uint32_t ph = (uint32_t)(kb / S) & 1u;
+                if (!mbar_wait_or_abort(&empty[s], ph ^ 1u, abort, prm.err)) break;
+                mbar_expect_tx(&full[s], Cfg::kXStageBytes + Cfg::kWStageBytes);
+                tma_load_2d(xs + s * Cfg::kXStageBytes, &tmap_x, &full[s], kb * kBlockK, g0);
+                uint8_t *wst = ws + s * Cfg::kWStageBytes;
+                tma_load_2d(wst, &tmap_w1, &full[s], kb * kWords, wrow0);
+                if (UP)  // the up rows fill the second half of the weight tile
+                    tma_load_2d(wst + Cfg::kWStageBytes / 2, &tmap_w2, &full[s], kb * kWords, wrow0);
             }
         }
     } else if (warp == kMmaWarp) {
@@ -230,9 +187,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bv = brow[k >> prm.gs_shift];
             }
         };
-        uint16_t s_cur, b_cur, s_nxt, b_nxt;
-        load_sb(par, s_cur, b_cur);
-        load_sb(par + 2, s_nxt, b_nxt);
+        // Scale and bias of this thread's row for its next kSbAhead stages, in
+        // a shift register: the load for a stage is issued kSbAhead of this
+        // warp's iterations before its use, which covers an HBM round trip.
+        uint16_t sq[kSbAhead], bq[kSbAhead];
+#pragma unroll
+        for (int i = 0; i < kSbAhead; ++i) load_sb(par + 2 * i, sq[i], bq[i]);
         const uint32_t t_lane = (uint32_t)(q * 32) << 16;
         for (int kb = par; kb < num_kb; kb += 2) {
             const int s = kb % S;
@@ -246,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     wst + r * 32 + 16 * (h ^ ((r >> 2) & 1)));
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
-                const Dq4 d = make_dq4(s_cur, b_cur);
+                const Dq4 d = make_dq4(sq[0], bq[0]);
                 const uint32_t words[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -266,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *reinterpret_cast<const uint4 *>(wst + r * 64 + 16 * ((2 * h + 1) ^ x));
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
-                const Dq8 d = make_dq8(s_cur, b_cur);
+                const Dq8 d = make_dq8(sq[0], bq[0]);
                 const uint32_t words[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
@@ -279,9 +239,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&afull[s]);
-            s_cur = s_nxt;
-            b_cur = b_nxt;
-            load_sb(kb + 4, s_nxt, b_nxt);
+#pragma unroll
+            for (int i = 0; i + 1 < kSbAhead; ++i) {
+                sq[i] = sq[i + 1];
+                bq[i] = bq[i + 1];
+            }
+            load_sb(kb + 2 * kSbAhead, sq[kSbAhead - 1], bq[kSbAhead - 1]);
         }
         // ------------------------------------------------ epilogue
         const bool ok = mbar_wait_or_abort(accfull, 0, abort, prm.err) && !*abort;
@@ -364,18 +327,14 @@ cudaError_t launch_cfg(const TcMoeArgs &a, cudaStream_t stream) {
     if (!make_map_2d(&m1, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w1, Kw, wrows, Kw * 4,
                      kBlockK * BITS / 32, wbox_rows, wsw))
         return cudaErrorInvalidValue;
-    if (UP) {
-        if (!make_map_2d(&m2, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w2, Kw, wrows, Kw * 4,
-                         kBlockK * BITS / 32, wbox_rows, wsw))
-            return cudaErrorInvalidValue;
-        mx = m1;  // unused
-    } else {
-        if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, (uint64_t)a.K,
-                         (uint64_t)a.x_rows_total, (uint64_t)a.x_ld * 2, kBlockK, kMaxTok,
-                         CU_TENSOR_MAP_SWIZZLE_128B))
-            return cudaErrorInvalidValue;
-        m2 = m1;  // unused
-    }
+    m2 = m1;  // unused by the down kernel
+    if (UP && !make_map_2d(&m2, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w2, Kw, wrows, Kw * 4,
+                           kBlockK * BITS / 32, wbox_rows, wsw))
+        return cudaErrorInvalidValue;
+    if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, (uint64_t)a.K,
+                     (uint64_t)a.x_rows_total, (uint64_t)a.x_ld * 2, kBlockK, kMaxTok,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
     MoeTcParams prm;
     prm.N = a.N;
     prm.K = a.K;
@@ -388,8 +347,6 @@ cudaError_t launch_cfg(const TcMoeArgs &a, cudaStream_t stream) {
     prm.b2 = a.b2;
     prm.tiles = a.tiles;
     prm.n_tiles = a.n_tiles;
-    prm.x = a.x;
-    prm.x_ld = a.x_ld;
     prm.rows = a.rows;
     prm.y = a.y;
     prm.y_ld = a.y_ld;
@@ -410,7 +367,7 @@ bool tc_moe_supported(int bits, int gs, int64_t H, int64_t I, int64_t E, const v
     if (bits != 4 && bits != 8) return false;
     if (gs != 32 && gs != 64 && gs != 128) return false;
     if (H % kBlockK || I % kBlockK) return false;         // whole stages along both K
-    if ((reinterpret_cast<uintptr_t>(x) & 15) || x_ld % 8) return false;  // 16-byte gathers
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || x_ld % 8) return false;  // 16-byte row copies
     if (E * (H > I ? H : I) > ((int64_t)1 << 31) - 1) return false;      // TMA row coordinate
     return tensor_maps_available();
 }

@@ -138,6 +138,21 @@ __global__ void fill_kernel(const int32_t *__restrict__ idx, int64_t pairs, int 
     pos_pair[pos] = (int32_t)i;
 }
 
+// xg[g] = x[pos_token[g]] for the grouped rows g < sum(counts): one warp per
+// row, 16-byte copies (H % 8 == 0, 16-byte aligned rows)
+__global__ void group_rows_kernel(const uint16_t *__restrict__ x, int64_t H,
+                                  const int32_t *__restrict__ pos_token,
+                                  const int32_t *__restrict__ offsets,
+                                  const int32_t *__restrict__ counts, int E,
+                                  uint16_t *__restrict__ xg) {
+    const int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (g >= (int64_t)offsets[E - 1] + counts[E - 1]) return;
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + (int64_t)pos_token[g] * H);
+    uint4 *dst = reinterpret_cast<uint4 *>(xg + g * H);
+    for (int64_t i = lane; i < H / 8; i += 32) dst[i] = src[i];
+}
+
 __global__ void pair_token_kernel(int64_t pairs, int top_k, int32_t *__restrict__ tok) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < pairs) tok[i] = (int32_t)(i / top_k);
@@ -172,6 +187,8 @@ inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 //   tiles[max_tiles] int4, n_tiles int32   (tensor-core tile list)
 //   h[P, I]  bf16      (SwiGLU activations, grouped or pair order)
 //   d[P, H]  fp32      (down-projection sums, pair order)
+//   xg[P, H] bf16      (tokens in grouped order; only when P >= 16 E, the
+//                       tensor-core path)
 int64_t max_moe_tiles(int64_t P, int64_t E) {
     return (P + kMoeTileTokens - 1) / kMoeTileTokens + std::min<int64_t>(E, P);
 }
@@ -182,8 +199,12 @@ struct MoeWorkspace {
     int32_t *n_tiles;
     uint16_t *h;
     float *d;
+    uint16_t *xg;
     size_t bytes;
 };
+
+// The grouped tensor-core path is taken from this many pairs on.
+inline bool tc_pairs(int64_t P, int64_t E) { return P >= 16 * E; }
 
 MoeWorkspace carve(void *base, int64_t T, int64_t E, int64_t top_k, int64_t H, int64_t I) {
     MoeWorkspace w;
@@ -203,6 +224,7 @@ MoeWorkspace carve(void *base, int64_t T, int64_t E, int64_t top_k, int64_t H, i
     w.n_tiles = reinterpret_cast<int32_t *>(take(sizeof(int32_t)));
     w.h = reinterpret_cast<uint16_t *>(take(sizeof(uint16_t) * P * I));
     w.d = reinterpret_cast<float *>(take(sizeof(float) * P * H));
+    w.xg = tc_pairs(P, E) ? reinterpret_cast<uint16_t *>(take(sizeof(uint16_t) * P * H)) : nullptr;
     w.bytes = off;
     return w;
 }
@@ -240,7 +262,7 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
     const bool grouped = P > E;
     // Tensor-core path once experts average >= 16 tokens (a 16-column MMA);
     // below that the grouped GEMV streams each expert's weights once.
-    const bool use_tc = grouped && P >= 16 * E && tc_moe_supported(bits, gsz, H, I, E, x, H);
+    const bool use_tc = grouped && tc_pairs(P, E) && tc_moe_supported(bits, gsz, H, I, E, x, H);
     cudaError_t e;
 
     GemvProblems up;
@@ -270,6 +292,8 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
                                                   ws.pos_token, ws.pos_pair);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
         if (use_tc) {
+            group_rows_kernel<<<(unsigned)((P + 7) / 8), 256, 0, stream>>>(
+                x, H, ws.pos_token, ws.offsets, ws.counts, (int)E, ws.xg);
             TcMoeArgs a;
             a.up = true;
             a.bits = bits;
@@ -279,10 +303,9 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
             a.K = H;
             a.w1 = gw; a.s1 = gs_; a.b1 = gb;
             a.w2 = uw; a.s2 = us; a.b2 = ub;
-            a.x = x;
+            a.x = ws.xg;
             a.x_ld = H;
-            a.x_rows_total = T;
-            a.rows = ws.pos_token;
+            a.x_rows_total = P;
             a.tiles = ws.tiles;
             a.n_tiles = ws.n_tiles;
             a.max_tiles = max_moe_tiles(P, E);

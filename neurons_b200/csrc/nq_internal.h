@@ -96,10 +96,10 @@ struct TcMoeArgs {
     const uint16_t *s1 = nullptr, *b1 = nullptr;
     const uint32_t *w2 = nullptr;    // up (up kernel)
     const uint16_t *s2 = nullptr, *b2 = nullptr;
-    const uint16_t *x = nullptr;     // up: x [T, K]; down: h [P, K] in grouped order
+    const uint16_t *x = nullptr;     // token rows in grouped order: up: xg [P, K]; down: h [P, K]
     int64_t x_ld = 0;
-    int64_t x_rows_total = 0;        // rows of x (down: P)
-    const int32_t *rows = nullptr;   // up: token of grouped row; down: pair of grouped row
+    int64_t x_rows_total = 0;        // P
+    const int32_t *rows = nullptr;   // down: pair of grouped row
     const int4 *tiles = nullptr;
     const int32_t *n_tiles = nullptr;
     int64_t max_tiles = 0;           // grid bound; CTAs past *n_tiles exit at once
