@@ -142,6 +142,30 @@ int nq_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I,
                   int group_size, void *workspace, size_t workspace_bytes,
                   uint16_t *y, void *stream);
 
+/* The switch step restricted to one shard of the experts, for expert
+ * parallelism: the weights passed hold experts [e0, e0 + ne) of the E the
+ * router chose from (gate/up w [ne, I, H*bits/32], down w [ne, H, ...]), and
+ * the call writes, in fp32,
+ *   y_partial[t] = sum over the slots j with e0 <= topk_idx[t,j] < e0 + ne of
+ *                  bf16(score[t,j]) * down_e( bf16(silu(gate_e(x_t)) * up_e(x_t)) ).
+ * Summing y_partial over all shards and rounding to bf16 gives nq_moe_switch's
+ * result up to the order of the fp32 additions.  No counterpart in the
+ * reference (which runs one device); it shards the switch step
+ * compute/src/compute/model/qwen3_transformer_moe_model_mlx.cpp:29-79.
+ * workspace: nq_moe_partial_workspace_size(T, E, ne, top_k, H, I) bytes. */
+size_t nq_moe_partial_workspace_size(int64_t T, int64_t E, int64_t ne,
+                                     int64_t top_k, int64_t H, int64_t I);
+int nq_moe_switch_partial(const uint16_t *x, int64_t T, int64_t H, int64_t I,
+                          int64_t E, int64_t top_k, const int32_t *topk_idx,
+                          const float *topk_scores, int64_t e0, int64_t ne,
+                          const uint32_t *gate_w, const uint16_t *gate_s,
+                          const uint16_t *gate_b, const uint32_t *up_w,
+                          const uint16_t *up_s, const uint16_t *up_b,
+                          const uint32_t *down_w, const uint16_t *down_s,
+                          const uint16_t *down_b, int bits, int group_size,
+                          void *workspace, size_t workspace_bytes,
+                          float *y_partial, void *stream);
+
 /* nq_moe_switch without a workspace argument, for callers that cannot
  * allocate device memory themselves (an FFI host or a runtime that only
  * hands over the tensors it owns and exposes no allocator).  No counterpart

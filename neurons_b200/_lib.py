@@ -36,6 +36,9 @@ SIGNATURES = {
                           U64, P, P]),
     "nq_moe_switch_static": (I, [P, I64, I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, P, I,
                                  I, P, P]),
+    "nq_moe_partial_workspace_size": (U64, [I64, I64, I64, I64, I64, I64]),
+    "nq_moe_switch_partial": (I, [P, I64, I64, I64, I64, I64, P, P, I64, I64, P, P, P, P, P, P, P,
+                                  P, P, I, I, P, U64, P, P]),
 }
 
 

@@ -261,36 +261,79 @@ size_t nq_moe_workspace_size(int64_t T, int64_t E, int64_t top_k, int64_t H, int
     return nq::moe_workspace_bytes(T, E, top_k, H, I);
 }
 
+}  // extern "C"
+
+// Shared validation and launch of nq_moe_switch / nq_moe_switch_partial: the
+// weights passed hold experts [e0, e0 + ne) of E.
+static int moe_switch_checked(const char *what, const uint16_t *x, int64_t T, int64_t H, int64_t I,
+                              int64_t E, int64_t top_k, const int32_t *topk_idx,
+                              const float *topk_scores, int64_t e0, int64_t ne,
+                              const uint32_t *gate_w, const uint16_t *gate_s,
+                              const uint16_t *gate_b, const uint32_t *up_w, const uint16_t *up_s,
+                              const uint16_t *up_b, const uint32_t *down_w, const uint16_t *down_s,
+                              const uint16_t *down_b, int bits, int group_size, void *workspace,
+                              size_t workspace_bytes, uint16_t *y, float *y_partial,
+                              void *stream) {
+    const std::string w(what);
+    if (int rc = check_quant(I, H, bits, group_size, what)) return rc;
+    if (int rc = check_quant(H, I, bits, group_size, what)) return rc;
+    if (T < 0 || E <= 0 || E > 1024 || top_k <= 0 || top_k > 32 || top_k > E)
+        return fail(NQ_INVALID_INPUT, w + ": need 0 < top_k <= min(E, 32), E <= 1024");
+    if (e0 < 0 || ne <= 0 || e0 + ne > E)
+        return fail(NQ_INVALID_INPUT, w + ": expert range outside [0, E)");
+    if (H % 4) return fail(NQ_INVALID_INPUT, w + ": H must be a multiple of 4");
+    if (T == 0) return NQ_SUCCESS;
+    if (T * top_k > 65535 * 64) return fail(NQ_INVALID_INPUT, w + ": too many tokens for one call");
+    if (!x || !topk_idx || !topk_scores || !gate_w || !gate_s || !gate_b || !up_w || !up_s ||
+        !up_b || !down_w || !down_s || !down_b || !(y || y_partial) || !workspace)
+        return fail(NQ_INVALID_INPUT, w + ": NULL pointer");
+    const size_t need = nq::moe_partial_workspace_bytes(T, E, ne, top_k, H, I);
+    if (workspace_bytes < need)
+        return fail(NQ_INVALID_INPUT,
+                    w + ": workspace too small: need " + std::to_string(need) + " bytes");
+    if (!aligned16(x) || !aligned16(gate_w) || !aligned16(up_w) || !aligned16(down_w) ||
+        !aligned16(workspace) || !aligned16(y_partial))
+        return fail(NQ_INVALID_INPUT, w + ": tensors must be 16-byte aligned");
+    if (int rc = need_device(what)) return rc;
+    return from_cuda(nq::launch_moe_switch(x, T, H, I, E, top_k, topk_idx, topk_scores, e0, ne,
+                                           gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s,
+                                           down_b, bits, group_size, workspace, y, y_partial,
+                                           static_cast<cudaStream_t>(stream)),
+                     what);
+}
+
+extern "C" {
+
 int nq_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t top_k,
                   const int32_t *topk_idx, const float *topk_scores, const uint32_t *gate_w,
                   const uint16_t *gate_s, const uint16_t *gate_b, const uint32_t *up_w,
                   const uint16_t *up_s, const uint16_t *up_b, const uint32_t *down_w,
                   const uint16_t *down_s, const uint16_t *down_b, int bits, int group_size,
                   void *workspace, size_t workspace_bytes, uint16_t *y, void *stream) {
-    if (int rc = check_quant(I, H, bits, group_size, "nq_moe_switch")) return rc;
-    if (int rc = check_quant(H, I, bits, group_size, "nq_moe_switch")) return rc;
-    if (T < 0 || E <= 0 || E > 1024 || top_k <= 0 || top_k > 32 || top_k > E)
-        return fail(NQ_INVALID_INPUT, "nq_moe_switch: need 0 < top_k <= min(E, 32), E <= 1024");
-    if (H % 4) return fail(NQ_INVALID_INPUT, "nq_moe_switch: H must be a multiple of 4");
-    if (T == 0) return NQ_SUCCESS;
-    if (T * top_k > 65535 * 64)
-        return fail(NQ_INVALID_INPUT, "nq_moe_switch: too many tokens for one call");
-    if (!x || !topk_idx || !topk_scores || !gate_w || !gate_s || !gate_b || !up_w || !up_s ||
-        !up_b || !down_w || !down_s || !down_b || !y || !workspace)
-        return fail(NQ_INVALID_INPUT, "nq_moe_switch: NULL pointer");
-    const size_t need = nq::moe_workspace_bytes(T, E, top_k, H, I);
-    if (workspace_bytes < need)
-        return fail(NQ_INVALID_INPUT, "nq_moe_switch: workspace too small: need " +
-                                          std::to_string(need) + " bytes");
-    if (!aligned16(x) || !aligned16(gate_w) || !aligned16(up_w) || !aligned16(down_w) ||
-        !aligned16(workspace))
-        return fail(NQ_INVALID_INPUT, "nq_moe_switch: tensors must be 16-byte aligned");
-    if (int rc = need_device("nq_moe_switch")) return rc;
-    return from_cuda(nq::launch_moe_switch(x, T, H, I, E, top_k, topk_idx, topk_scores, gate_w,
-                                           gate_s, gate_b, up_w, up_s, up_b, down_w, down_s,
-                                           down_b, bits, group_size, workspace, y,
-                                           static_cast<cudaStream_t>(stream)),
-                     "nq_moe_switch");
+    if (!y && T > 0) return fail(NQ_INVALID_INPUT, "nq_moe_switch: NULL pointer");
+    return moe_switch_checked("nq_moe_switch", x, T, H, I, E, top_k, topk_idx, topk_scores, 0, E,
+                              gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s, down_b,
+                              bits, group_size, workspace, workspace_bytes, y, nullptr, stream);
+}
+
+size_t nq_moe_partial_workspace_size(int64_t T, int64_t E, int64_t ne, int64_t top_k, int64_t H,
+                                     int64_t I) {
+    if (T < 0 || E <= 0 || ne <= 0 || ne > E || top_k <= 0 || H <= 0 || I <= 0) return 0;
+    return nq::moe_partial_workspace_bytes(T, E, ne, top_k, H, I);
+}
+
+int nq_moe_switch_partial(const uint16_t *x, int64_t T, int64_t H, int64_t I, int64_t E,
+                          int64_t top_k, const int32_t *topk_idx, const float *topk_scores,
+                          int64_t e0, int64_t ne, const uint32_t *gate_w, const uint16_t *gate_s,
+                          const uint16_t *gate_b, const uint32_t *up_w, const uint16_t *up_s,
+                          const uint16_t *up_b, const uint32_t *down_w, const uint16_t *down_s,
+                          const uint16_t *down_b, int bits, int group_size, void *workspace,
+                          size_t workspace_bytes, float *y_partial, void *stream) {
+    if (!y_partial && T > 0) return fail(NQ_INVALID_INPUT, "nq_moe_switch_partial: NULL pointer");
+    return moe_switch_checked("nq_moe_switch_partial", x, T, H, I, E, top_k, topk_idx, topk_scores,
+                              e0, ne, gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s,
+                              down_b, bits, group_size, workspace, workspace_bytes, nullptr,
+                              y_partial, stream);
 }
 
 }  // extern "C"

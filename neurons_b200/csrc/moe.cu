@@ -70,8 +70,10 @@ __global__ void route_kernel(const uint16_t *__restrict__ logits, int64_t T, int
     }
 }
 
-// counts[e] = number of (token, slot) pairs routed to expert e
-__global__ void count_kernel(const int32_t *__restrict__ idx, int64_t pairs, int E,
+// counts[e - e0] = number of (token, slot) pairs routed to expert e, for the
+// experts [e0, e0 + ne) this call serves; indices outside [0, E) raise the
+// bad-index bit of the device error word
+__global__ void count_kernel(const int32_t *__restrict__ idx, int64_t pairs, int E, int e0, int ne,
                              int32_t *__restrict__ counts, unsigned int *err) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= pairs) return;
@@ -80,7 +82,8 @@ __global__ void count_kernel(const int32_t *__restrict__ idx, int64_t pairs, int
         atomicOr(err, kErrBadIndex);
         return;
     }
-    atomicAdd(&counts[e], 1);
+    const int l = e - e0;
+    if (l >= 0 && l < ne) atomicAdd(&counts[l], 1);
 }
 
 // exclusive prefix sum over experts (single block, E <= 1024); clears cursors.
@@ -126,14 +129,16 @@ __global__ void scan_kernel(const int32_t *__restrict__ counts, int E, int32_t *
 
 // place every pair at offsets[e] + rank; the rank order inside an expert does
 // not change any result (each output row depends on its own input row only)
-__global__ void fill_kernel(const int32_t *__restrict__ idx, int64_t pairs, int top_k, int E,
-                            const int32_t *__restrict__ offsets, int32_t *__restrict__ cursor,
+__global__ void fill_kernel(const int32_t *__restrict__ idx, int64_t pairs, int top_k, int E, int e0,
+                            int ne, const int32_t *__restrict__ offsets, int32_t *__restrict__ cursor,
                             int32_t *__restrict__ pos_token, int32_t *__restrict__ pos_pair) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= pairs) return;
     const int e = idx[i];
     if (e < 0 || e >= E) return;
-    const int32_t pos = offsets[e] + atomicAdd(&cursor[e], 1);
+    const int l = e - e0;
+    if (l < 0 || l >= ne) return;
+    const int32_t pos = offsets[l] + atomicAdd(&cursor[l], 1);
     pos_token[pos] = (int32_t)(i / top_k);
     pos_pair[pos] = (int32_t)i;
 }
@@ -158,21 +163,31 @@ __global__ void pair_token_kernel(int64_t pairs, int top_k, int32_t *__restrict_
     if (i < pairs) tok[i] = (int32_t)(i / top_k);
 }
 
-// y[t, n] = bf16( sum_j bf16(score[t, j]) * d[t*k + j, n] ), slot order 0..k-1
+// sum_j bf16(score[t, j]) * d[t*k + j, n] over the slots j routed to experts
+// [e0, e0 + ne), slot order 0..k-1; y gets it rounded to bf16, or y_partial
+// gets the fp32 sum (the share of one expert shard)
 __global__ void combine_kernel(const float *__restrict__ d, const float *__restrict__ scores,
-                               int64_t T, int64_t H, int top_k, uint16_t *__restrict__ y) {
+                               const int32_t *__restrict__ idx, int e0, int ne, int64_t T,
+                               int64_t H, int top_k, uint16_t *__restrict__ y,
+                               float *__restrict__ y_partial) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over T * H / 4
     if (i >= T * (H / 4)) return;
     const int64_t t = i / (H / 4);
     const int64_t n = (i % (H / 4)) * 4;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int j = 0; j < top_k; ++j) {
+        const int l = idx[t * top_k + j] - e0;
+        if (l < 0 || l >= ne) continue;
         const float sc = bf16_to_f32(f32_to_bf16(scores[t * top_k + j]));
         const float4 v = *reinterpret_cast<const float4 *>(d + (t * top_k + j) * H + n);
         acc.x = __fmaf_rn(sc, v.x, acc.x);
         acc.y = __fmaf_rn(sc, v.y, acc.y);
         acc.z = __fmaf_rn(sc, v.z, acc.z);
         acc.w = __fmaf_rn(sc, v.w, acc.w);
+    }
+    if (y_partial) {
+        *reinterpret_cast<float4 *>(y_partial + t * H + n) = acc;
+        return;
     }
     uint2 out;
     out.x = (uint32_t)f32_to_bf16(acc.x) | ((uint32_t)f32_to_bf16(acc.y) << 16);
@@ -206,7 +221,10 @@ struct MoeWorkspace {
 // The grouped tensor-core path is taken from this many pairs on.
 inline bool tc_pairs(int64_t P, int64_t E) { return P >= 16 * E; }
 
-MoeWorkspace carve(void *base, int64_t T, int64_t E, int64_t top_k, int64_t H, int64_t I) {
+// E: experts this call serves (sizes the per-expert arrays); E_total: experts
+// the router chose from (decides whether the tensor-core path, and xg, is used)
+MoeWorkspace carve(void *base, int64_t T, int64_t E, int64_t top_k, int64_t H, int64_t I,
+                   int64_t E_total) {
     MoeWorkspace w;
     const int64_t P = T * top_k;
     size_t off = 0;
@@ -224,7 +242,8 @@ MoeWorkspace carve(void *base, int64_t T, int64_t E, int64_t top_k, int64_t H, i
     w.n_tiles = reinterpret_cast<int32_t *>(take(sizeof(int32_t)));
     w.h = reinterpret_cast<uint16_t *>(take(sizeof(uint16_t) * P * I));
     w.d = reinterpret_cast<float *>(take(sizeof(float) * P * H));
-    w.xg = tc_pairs(P, E) ? reinterpret_cast<uint16_t *>(take(sizeof(uint16_t) * P * H)) : nullptr;
+    w.xg = tc_pairs(P, E_total) ? reinterpret_cast<uint16_t *>(take(sizeof(uint16_t) * P * H))
+                                : nullptr;
     w.bytes = off;
     return w;
 }
@@ -241,28 +260,41 @@ cudaError_t launch_moe_route(const uint16_t *logits, int64_t T, int64_t E, int64
 }
 
 size_t moe_workspace_bytes(int64_t T, int64_t E, int64_t top_k, int64_t H, int64_t I) {
-    return carve(nullptr, T, E, top_k, H, I).bytes;
+    return carve(nullptr, T, E, top_k, H, I, E).bytes;
+}
+
+size_t moe_partial_workspace_bytes(int64_t T, int64_t E, int64_t ne, int64_t top_k, int64_t H,
+                                   int64_t I) {
+    return carve(nullptr, T, ne, top_k, H, I, E).bytes;
 }
 
 // Pairs routed to one expert are processed together ("grouped" mode) once
 // there are more pairs than experts; below that every pair is its own
 // problem ("pair" mode: no grouping kernels, one weight stream per pair).
-cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I, int64_t E,
-                              int64_t top_k, const int32_t *idx, const float *scores,
-                              const uint32_t *gw, const uint16_t *gs_, const uint16_t *gb,
-                              const uint32_t *uw, const uint16_t *us, const uint16_t *ub,
-                              const uint32_t *dw, const uint16_t *ds, const uint16_t *db, int bits,
-                              int gsz, void *workspace, uint16_t *y, cudaStream_t stream) {
+// The switch step for the experts [e0, e0 + ne) of E: the weights passed are
+// those ne experts.  Serving all experts (e0 = 0, ne = E) writes the bf16
+// result to y; serving a shard writes the fp32 partial sum to y_partial.
+cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I, int64_t E_total,
+                              int64_t top_k, const int32_t *idx, const float *scores, int64_t e0,
+                              int64_t E, const uint32_t *gw, const uint16_t *gs_,
+                              const uint16_t *gb, const uint32_t *uw, const uint16_t *us,
+                              const uint16_t *ub, const uint32_t *dw, const uint16_t *ds,
+                              const uint16_t *db, int bits, int gsz, void *workspace, uint16_t *y,
+                              float *y_partial, cudaStream_t stream) {
     if (T == 0) return cudaSuccess;
     const int64_t P = T * top_k;
-    MoeWorkspace ws = carve(workspace, T, E, top_k, H, I);
+    MoeWorkspace ws = carve(workspace, T, E, top_k, H, I, E_total);
     unsigned int *err = device_error_word();
     const int thr = 256;
     const unsigned pblocks = (unsigned)((P + thr - 1) / thr);
-    const bool grouped = P > E;
+    // a shard always groups (pairs of other shards are skipped while grouping)
+    const bool grouped = P > E || y_partial != nullptr;
     // Tensor-core path once experts average >= 16 tokens (a 16-column MMA);
     // below that the grouped GEMV streams each expert's weights once.
-    const bool use_tc = grouped && tc_pairs(P, E) && tc_moe_supported(bits, gsz, H, I, E, x, H);
+    const bool use_tc =
+        grouped && tc_pairs(P, E_total) && tc_moe_supported(bits, gsz, H, I, E, x, H);
+    const int64_t n4 = T * (H / 4);
+    const unsigned cblocks = (unsigned)((n4 + thr - 1) / thr);
     cudaError_t e;
 
     GemvProblems up;
@@ -285,11 +317,12 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
     if (grouped) {
         if ((e = cudaMemsetAsync(ws.counts, 0, sizeof(int32_t) * E, stream)) != cudaSuccess)
             return e;
-        count_kernel<<<pblocks, thr, 0, stream>>>(idx, P, (int)E, ws.counts, err);
+        count_kernel<<<pblocks, thr, 0, stream>>>(idx, P, (int)E_total, (int)e0, (int)E, ws.counts,
+                                                   err);
         scan_kernel<<<1, 1024, 0, stream>>>(ws.counts, (int)E, ws.offsets, ws.cursor,
                                             use_tc ? ws.tiles : nullptr, ws.n_tiles);
-        fill_kernel<<<pblocks, thr, 0, stream>>>(idx, P, (int)top_k, (int)E, ws.offsets, ws.cursor,
-                                                  ws.pos_token, ws.pos_pair);
+        fill_kernel<<<pblocks, thr, 0, stream>>>(idx, P, (int)top_k, (int)E_total, (int)e0, (int)E,
+                                                  ws.offsets, ws.cursor, ws.pos_token, ws.pos_pair);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
         if (use_tc) {
             group_rows_kernel<<<(unsigned)((P + 7) / 8), 256, 0, stream>>>(
@@ -325,9 +358,8 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
             d.y = ws.d;
             d.y_ld = H;
             if ((e = launch_tc_moe(d, stream)) != cudaSuccess) return e;
-            const int64_t n4 = T * (H / 4);
-            combine_kernel<<<(unsigned)((n4 + thr - 1) / thr), thr, 0, stream>>>(ws.d, scores, T, H,
-                                                                                  (int)top_k, y);
+            combine_kernel<<<cblocks, thr, 0, stream>>>(ws.d, scores, idx, (int)e0, (int)E, T, H,
+                                                        (int)top_k, y, y_partial);
             return cudaGetLastError();
         }
         // gate/up: problem = expert, its tokens gathered from x, h rows in grouped order
@@ -366,9 +398,8 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
     }
     if ((e = launch_gemv(up, stream)) != cudaSuccess) return e;
     if ((e = launch_gemv(dn, stream)) != cudaSuccess) return e;
-    const int64_t n4 = T * (H / 4);
-    combine_kernel<<<(unsigned)((n4 + thr - 1) / thr), thr, 0, stream>>>(ws.d, scores, T, H,
-                                                                          (int)top_k, y);
+    combine_kernel<<<cblocks, thr, 0, stream>>>(ws.d, scores, idx, (int)e0, (int)E, T, H,
+                                                (int)top_k, y, y_partial);
     return cudaGetLastError();
 }
 

@@ -118,12 +118,17 @@ cudaError_t launch_dequantize(const uint32_t *wq, const uint16_t *s, const uint1
                               cudaStream_t stream);
 
 size_t moe_workspace_bytes(int64_t T, int64_t E, int64_t top_k, int64_t H, int64_t I);
-cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I, int64_t E,
-                              int64_t top_k, const int32_t *idx, const float *scores,
-                              const uint32_t *gw, const uint16_t *gs_, const uint16_t *gb,
-                              const uint32_t *uw, const uint16_t *us, const uint16_t *ub,
-                              const uint32_t *dw, const uint16_t *ds, const uint16_t *db, int bits,
-                              int gsz, void *workspace, uint16_t *y, cudaStream_t stream);
+size_t moe_partial_workspace_bytes(int64_t T, int64_t E, int64_t ne, int64_t top_k, int64_t H,
+                                   int64_t I);
+// The switch step for experts [e0, e0 + ne) of E_total (weights: those ne
+// experts).  y: bf16 result (all experts); y_partial: fp32 partial sums.
+cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I, int64_t E_total,
+                              int64_t top_k, const int32_t *idx, const float *scores, int64_t e0,
+                              int64_t ne, const uint32_t *gw, const uint16_t *gs_,
+                              const uint16_t *gb, const uint32_t *uw, const uint16_t *us,
+                              const uint16_t *ub, const uint32_t *dw, const uint16_t *ds,
+                              const uint16_t *db, int bits, int gsz, void *workspace, uint16_t *y,
+                              float *y_partial, cudaStream_t stream);
 
 cudaError_t launch_moe_route(const uint16_t *logits, int64_t T, int64_t E, int64_t top_k,
                              int32_t *idx, float *scores, cudaStream_t stream);

@@ -182,6 +182,33 @@ def moe_switch(x, idx, scores, gate, up, down, group_size=64, bits=4, workspace=
     return out
 
 
+def moe_partial_workspace_size(T, E, ne, top_k, H, I):
+    return int(lib().nq_moe_partial_workspace_size(T, E, ne, top_k, H, I))
+
+
+def moe_switch_partial(x, idx, scores, gate, up, down, E, e0, group_size=64, bits=4,
+                       workspace=None, out=None):
+    """fp32 share [T, H] of the switch step that the experts [e0, e0 + ne)
+    contribute; gate/up/down hold those ne experts.  Summed over all shards
+    and rounded to bf16 it is moe_switch's result."""
+    _need(x, "x", (torch.bfloat16,))
+    T, H = int(x.shape[0]), int(x.shape[1])
+    top_k = int(idx.shape[1])
+    ne, I = int(gate[0].shape[0]), int(gate[0].shape[1])
+    need = moe_partial_workspace_size(T, E, ne, top_k, H, I)
+    if workspace is None:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.float32, device=x.device)
+    check(lib().nq_moe_switch_partial(_ptr(x), T, H, I, E, top_k, _ptr(idx), _ptr(scores), e0, ne,
+                                      _ptr(gate[0]), _ptr(gate[1]), _ptr(gate[2]),
+                                      _ptr(up[0]), _ptr(up[1]), _ptr(up[2]),
+                                      _ptr(down[0]), _ptr(down[1]), _ptr(down[2]),
+                                      bits, group_size, _ptr(workspace), workspace.numel(),
+                                      _ptr(out), _stream()))
+    return out
+
+
 def take_device_error():
     v = ctypes.c_uint(0)
     check(lib().nq_take_device_error(ctypes.byref(v)))

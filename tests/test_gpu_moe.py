@@ -184,3 +184,25 @@ def test_switch_tensor_core_bits_groups(oracle, nqlib, bits, gs):
     idx, sc = oracle.moe_route(acts(rng, T, E), k)
     staged_switch_check(oracle, x, idx, sc, gate, up, down, bits, gs,
                         f"switch {bits}-bit g{gs}")
+
+
+@pytest.mark.parametrize("T", [20, 300])
+def test_switch_partials_sum_to_the_full_step(oracle, nqlib, T):
+    """Expert shards (the expert-parallel building block): the fp32 partials of
+    four shards of 4 experts sum to the full switch step."""
+    import neurons_b200 as nb
+    E, k, H, I = 16, 4, 256, 128
+    rng = np.random.default_rng(T)
+    W = [experts(oracle, rng, E, r, c) for r, c in ((I, H), (I, H), (H, I))]
+    x = acts(rng, T, H)
+    idx, sc = oracle.moe_route(acts(rng, T, E), k)
+    full = nb.moe_switch(dev_bf16(x), dev_i32(idx), dev_f32(sc), *(dev3(w) for w in W), 64, 4)
+    tot = torch.zeros(T, H, dtype=torch.float32, device="cuda")
+    for e0 in range(0, E, 4):
+        sh = [tuple(a[e0:e0 + 4] for a in w) for w in W]
+        tot += nb.moe_switch_partial(dev_bf16(x), dev_i32(idx), dev_f32(sc),
+                                     *(dev3(w) for w in sh), E, e0, 64, 4)
+    torch.cuda.synchronize()
+    assert nb.take_device_error() == 0
+    y = tot.to(torch.bfloat16)
+    assert_close(host_u16(y), host_u16(full), f"partials T={T}")
