@@ -419,6 +419,123 @@ def moe_summary(T, t, steps, byts, flops, world, pk):
     return d
 
 
+def _events_time(step, steps, warmup, world):
+    """Device time of `steps` calls of step(i), bracketed by a barrier and a
+    synchronize, CUDA events on the current stream, max over ranks."""
+    import torch
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(steps):
+        step(i)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(t0.elapsed_time(t1) / 1e3, world)
+
+
+def time_tp(comm, M, N, K, steps, warmup, world, rank):
+    """Tensor-parallel quantized matmul: this rank's N/world weight rows, the
+    output columns all-gathered so every rank holds y [M, N] (strong scaling:
+    the total work is fixed as ranks are added).  Three rotating input sets."""
+    import torch
+    import neurons_b200 as nb
+    from neurons_b200 import dist
+    _, rows = dist.tp_shard(N, world, rank)
+    g = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    sets = []
+    for _ in range(3):
+        w = torch.randn(rows, K, device="cuda", generator=g) * 0.02
+        wq, s, b = nb.quantize(w, GS, BITS, nb.SCHEME_MINMAX)
+        del w
+        x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+        y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        ws = torch.empty(max(dist.tp_workspace_size(M, N, world), 1), dtype=torch.uint8,
+                         device="cuda")
+        sets.append((x, wq, s, b, y, ws))
+
+    def step(i):
+        x, wq, s, b, y, ws = sets[i % 3]
+        dist.tp_quantized_matmul(comm, x, wq, s, b, N, GS, BITS, out=y, workspace=ws)
+
+    t = _events_time(step, steps, warmup, world)
+    assert nb.take_device_error() == 0
+    return t
+
+
+def time_ep(comm, T, steps, warmup, world, rank):
+    """Expert-parallel Qwen3-30B-A3B switch step for T tokens in total: this
+    rank routes its T/world tokens, holds E/world experts; dispatch (all-gather
+    of tokens and routing), the shard's switch step, combine (reduce-scatter
+    of fp32 partials).  Strong scaling.  Two rotating weight sets."""
+    import torch
+    import neurons_b200 as nb
+    from neurons_b200 import dist
+    E, k, H, I = (QWEN3_MOE[v] for v in ("E", "top_k", "H", "I"))
+    _, ne = dist.ep_shard(E, world, rank)
+    _, nt = dist.ep_token_shard(T, world, rank)
+    g = torch.Generator(device="cuda").manual_seed(2000 + rank)
+    sets = []
+    for _ in range(2):
+        W = []
+        for n, kk in ((I, H), (I, H), (H, I)):
+            w = torch.randn(ne, n, kk, device="cuda", generator=g) * 0.02
+            W.append(nb.quantize(w, GS, BITS, nb.SCHEME_MINMAX))
+            del w
+        x = torch.randn(nt, H, device="cuda", generator=g).to(torch.bfloat16)
+        logits = torch.randn(nt, E, device="cuda", generator=g).to(torch.bfloat16)
+        sets.append((x, logits, W))
+    ws = torch.empty(dist.ep_workspace_size(T, E, k, H, I, world), dtype=torch.uint8,
+                     device="cuda")
+    y = torch.empty(nt, H, dtype=torch.bfloat16, device="cuda")
+
+    def step(i):
+        x, logits, W = sets[i % 2]
+        idx, sc = nb.moe_route(logits, k)
+        dist.ep_moe_switch(comm, x, T, idx, sc, W[0], W[1], W[2], E, GS, BITS, workspace=ws,
+                           out=y)
+
+    t = _events_time(step, steps, warmup, world)
+    assert nb.take_device_error() == 0
+    return t
+
+
+def sharded_summary(world, rank, pk):
+    """The tensor- and expert-parallel configurations at this N (strong
+    scaling), for the JSON line."""
+    from neurons_b200 import dist
+    comm = dist.Comm()
+    out = {"note": "strong scaling: total work fixed, split over the ranks; NCCL all-gather "
+                   "(TP) and all-gather + reduce-scatter (EP); time = max over ranks"}
+    M, N, K = WORKLOADS["prefill"]["M"], WORKLOADS["prefill"]["N"], WORKLOADS["prefill"]["K"]
+    n = 30
+    t = time_tp(comm, M, N, K, n, 3, world, rank)
+    out["tp_prefill"] = {"workload": "x[2048,4096] . W[14336,4096]^T, rows split over ranks",
+                         "us_per_step": t / n * 1e6,
+                         "tflops": algo_flops(M, N, K) * n / t / 1e12}
+    d = WORKLOADS["decode"]
+    n = 200
+    t = time_tp(comm, d["M"], d["N"], d["K"], n, 5, world, rank)
+    out["tp_decode"] = {"workload": "x[1,4096] . W[4096,4096]^T, rows split over ranks",
+                        "us_per_step": t / n * 1e6,
+                        "gbs": algo_bytes(d["M"], d["N"], d["K"]) * n / t / 1e9}
+    n = 10
+    t = time_ep(comm, 2048, n, 3, world, rank)
+    E, k, H, I = (QWEN3_MOE[v] for v in ("E", "top_k", "H", "I"))
+    out["ep_moe_T2048"] = {"workload": "Qwen3-30B-A3B switch step, T=2048, experts and tokens "
+                                       "split over ranks",
+                           "us_per_step": t / n * 1e6,
+                           "tflops": 2 * 2048 * k * 3 * I * H * n / t / 1e12}
+    comm.close()
+    return out
+
+
 class CpuSample:
     """The oracle's qmm on every host thread over all M tokens and a slice of the
     weight rows.  `calibrate` grows the slice until one call takes about
@@ -538,6 +655,11 @@ def ours(args):
             moe[f"T{T}"] = moe_summary(T, t_m, n, b_m, f_m, world, pk)
             line["gpu_launches"] += n * (7 if T * 8 > 128 else 5)
         line["moe"] = moe
+    if args.workload == "prefill" and not args.no_sharded:
+        line["sharded"] = sharded_summary(world, rank, pk)
+        # qmm + layout kernel per prefill step, one GEMV per decode step, nine
+        # kernels per expert-parallel step (NCCL's own kernels not counted)
+        line["gpu_launches"] += 2 * 30 + 200 + 9 * 10
     if args.workload == "prefill" and not args.no_decode:
         t_r, rp, _ = time_replay(50, 3, world, seed=rank + 200)
         line["llama3b_decode"] = replay_summary(t_r, 50, rp, world, pk)
@@ -685,6 +807,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-lines")
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE sub-line")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the tensor/expert-parallel sub-line")
     ap.add_argument("--kernel-only", action="store_true",
                     help="only the device-resident timed loop (a small target for ncu)")
     args = ap.parse_args()

@@ -1,5 +1,5 @@
 // nq_common.cuh -- device-side helpers shared by the sm_100a kernels:
-// bf16 packing, bounded mbarrier waits, TMA (non-multicast) loads and the
+// bf16 packing, bounded mbarrier waits, single-CTA TMA loads and the
 // tcgen05 (TMEM / UMMA) instruction wrappers.  Inline PTX only; no library.
 #pragma once
 

@@ -112,15 +112,19 @@ class Comm:
 
     def __init__(self, group=None):
         import torch.distributed as tdist
-        self.rank = tdist.get_rank(group)
-        self.size = tdist.get_world_size(group)
         ident = ctypes.create_string_buffer(NQ_COMM_ID_BYTES)
-        if self.rank == 0:
+        if not tdist.is_initialized():  # a single process: a communicator of one rank
+            self.rank, self.size = 0, 1
             _check(dist_lib().nq_comm_unique_id(ident))
-        box = [bytes(ident.raw) if self.rank == 0 else None]
-        tdist.broadcast_object_list(box, src=tdist.get_global_rank(group, 0) if group else 0,
-                                    group=group)
-        ident = ctypes.create_string_buffer(box[0], NQ_COMM_ID_BYTES)
+        else:
+            self.rank = tdist.get_rank(group)
+            self.size = tdist.get_world_size(group)
+            if self.rank == 0:
+                _check(dist_lib().nq_comm_unique_id(ident))
+            box = [bytes(ident.raw) if self.rank == 0 else None]
+            tdist.broadcast_object_list(box, src=tdist.get_global_rank(group, 0) if group else 0,
+                                        group=group)
+            ident = ctypes.create_string_buffer(box[0], NQ_COMM_ID_BYTES)
         self.handle = P()
         _check(dist_lib().nq_comm_init(ctypes.byref(self.handle), self.size, self.rank, ident))
 
