@@ -419,21 +419,34 @@ def moe_summary(T, t, steps, byts, flops, world, pk):
     return d
 
 
-def _events_time(step, steps, warmup, world):
+def _events_time(step, steps, warmup, world, graph=False):
     """Device time of `steps` calls of step(i), bracketed by a barrier and a
-    synchronize, CUDA events on the current stream, max over ranks."""
+    synchronize, CUDA events on the current stream, max over ranks.  With
+    graph=True the steps are captured in one CUDA graph and replayed, as a
+    decode loop does, so host submission is not timed."""
     import torch
     for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
+    g = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(steps):
+                step(i)
+        g.replay()
+        torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
-    for i in range(steps):
-        step(i)
+    if g is not None:
+        g.replay()
+    else:
+        for i in range(steps):
+            step(i)
     t1.record(stream)
     torch.cuda.synchronize()
     barrier(world)
@@ -464,7 +477,7 @@ def time_tp(comm, M, N, K, steps, warmup, world, rank):
         x, wq, s, b, y, ws = sets[i % 3]
         dist.tp_quantized_matmul(comm, x, wq, s, b, N, GS, BITS, out=y, workspace=ws)
 
-    t = _events_time(step, steps, warmup, world)
+    t = _events_time(step, steps, warmup, world, graph=M <= 32)
     assert nb.take_device_error() == 0
     return t
 
@@ -506,25 +519,64 @@ def time_ep(comm, T, steps, warmup, world, rank):
     return t
 
 
+def time_tp_fused(comm, M, N, K, steps, warmup, world, rank):
+    """time_tp with the all-gather fused into the kernel's stores (peer
+    writes into the symmetric arena over NVLink)."""
+    import torch
+    import neurons_b200 as nb
+    from neurons_b200 import dist
+    _, rows = dist.tp_shard(N, world, rank)
+    g = torch.Generator(device="cuda").manual_seed(3000 + rank)
+    sets = []
+    ybytes = (M * N * 2 + 255) // 256 * 256
+    for i in range(3):
+        w = torch.randn(rows, K, device="cuda", generator=g) * 0.02
+        wq, s, b = nb.quantize(w, GS, BITS, nb.SCHEME_MINMAX)
+        del w
+        x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+        sets.append((x, wq, s, b, comm.symmetric_tensor(i * ybytes, (M, N))))
+
+    def step(i):
+        x, wq, s, b, y = sets[i % 3]
+        dist.tp_quantized_matmul_fused(comm, x, wq, s, b, N, y, GS, BITS)
+
+    t = _events_time(step, steps, warmup, world, graph=M <= 32)
+    assert nb.take_device_error() == 0 and comm.take_error() == 0
+    return t
+
+
 def sharded_summary(world, rank, pk):
     """The tensor- and expert-parallel configurations at this N (strong
     scaling), for the JSON line."""
     from neurons_b200 import dist
     comm = dist.Comm()
-    out = {"note": "strong scaling: total work fixed, split over the ranks; NCCL all-gather "
-                   "(TP) and all-gather + reduce-scatter (EP); time = max over ranks"}
+    M0, N0 = WORKLOADS["prefill"]["M"], WORKLOADS["prefill"]["N"]
+    comm.symmetric_alloc(3 * ((M0 * N0 * 2 + 255) // 256 * 256))
+    out = {"note": "strong scaling: total work fixed, split over the ranks; TP: NCCL all-gather "
+                   "or the fused push (peer stores from the kernel), EP: NCCL all-gather + "
+                   "reduce-scatter; decode steps replayed from a CUDA graph; time = max over "
+                   "ranks"}
     M, N, K = WORKLOADS["prefill"]["M"], WORKLOADS["prefill"]["N"], WORKLOADS["prefill"]["K"]
     n = 30
     t = time_tp(comm, M, N, K, n, 3, world, rank)
     out["tp_prefill"] = {"workload": "x[2048,4096] . W[14336,4096]^T, rows split over ranks",
                          "us_per_step": t / n * 1e6,
                          "tflops": algo_flops(M, N, K) * n / t / 1e12}
+    t = time_tp_fused(comm, M, N, K, n, 3, world, rank)
+    out["tp_prefill_fused"] = {"workload": "as tp_prefill, columns pushed to every rank by the "
+                                           "GEMM's own stores over NVLink (no all-gather)",
+                               "us_per_step": t / n * 1e6,
+                               "tflops": algo_flops(M, N, K) * n / t / 1e12}
     d = WORKLOADS["decode"]
     n = 200
     t = time_tp(comm, d["M"], d["N"], d["K"], n, 5, world, rank)
     out["tp_decode"] = {"workload": "x[1,4096] . W[4096,4096]^T, rows split over ranks",
                         "us_per_step": t / n * 1e6,
                         "gbs": algo_bytes(d["M"], d["N"], d["K"]) * n / t / 1e9}
+    t = time_tp_fused(comm, d["M"], d["N"], d["K"], n, 5, world, rank)
+    out["tp_decode_fused"] = {"workload": "as tp_decode, columns pushed by the GEMV's stores",
+                              "us_per_step": t / n * 1e6,
+                              "gbs": algo_bytes(d["M"], d["N"], d["K"]) * n / t / 1e9}
     n = 10
     t = time_ep(comm, 2048, n, 3, world, rank)
     E, k, H, I = (QWEN3_MOE[v] for v in ("E", "top_k", "H", "I"))
@@ -657,9 +709,10 @@ def ours(args):
         line["moe"] = moe
     if args.workload == "prefill" and not args.no_sharded:
         line["sharded"] = sharded_summary(world, rank, pk)
-        # qmm + layout kernel per prefill step, one GEMV per decode step, nine
-        # kernels per expert-parallel step (NCCL's own kernels not counted)
-        line["gpu_launches"] += 2 * 30 + 200 + 9 * 10
+        # qmm + layout kernel per prefill step, one GEMV per decode step, ready +
+        # compute + done-wait per fused step, nine kernels per expert-parallel
+        # step (NCCL's own kernels not counted)
+        line["gpu_launches"] += 2 * 30 + 3 * 30 + 200 + 3 * 200 + 9 * 10
     if args.workload == "prefill" and not args.no_decode:
         t_r, rp, _ = time_replay(50, 3, world, seed=rank + 200)
         line["llama3b_decode"] = replay_summary(t_r, 50, rp, world, pk)

@@ -142,6 +142,37 @@ int nq_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I,
                   int group_size, void *workspace, size_t workspace_bytes,
                   uint16_t *y, void *stream);
 
+/* Output fan-out of a tensor-parallel quantized matmul: the call computes
+ * this rank's column shard and writes it into every rank's y through peer
+ * pointers (CUDA IPC mappings), instead of leaving an all-gather to a
+ * collective library.  No counterpart in the reference (one device); it is
+ * the compute step of nq_tp_quantized_matmul_fused (nq_dist.h), which sets
+ * these fields up and signals completion after it.  All pointers are valid in
+ * this process (peer mappings for other ranks).  *epoch is the call number
+ * (equal on every rank, increasing; read from device memory when the kernel
+ * runs, so a captured CUDA graph stays correct when replayed); ready[q] ==
+ * *epoch is set by rank q before its call (its earlier stream work has
+ * completed), and the kernel waits for every ready flag (bounded, 2 s; a
+ * timeout raises the device error word) before its first store.  The stores
+ * are complete when the kernel is. */
+#define NQ_MAX_RANKS 8
+typedef struct nq_push {
+    int nranks;
+    int rank;
+    const unsigned int *epoch;
+    void *dst[NQ_MAX_RANKS];
+    const unsigned int *ready;
+} nq_push_t;
+
+/* y_q[m, col0 + n] = (x . W^T)[m, n] on every rank q, y rows N_total apart
+ * (W: this rank's N rows).  M <= 32 needs K % 256 == 0 (and not 8-bit with
+ * group size 128); larger M takes the tensor-core path. */
+int nq_quantized_matmul_push(const uint16_t *x, int64_t M, const uint32_t *wq,
+                             const uint16_t *scales, const uint16_t *biases,
+                             int64_t N, int64_t K, int bits, int group_size,
+                             int64_t N_total, int64_t col0,
+                             const nq_push_t *push, void *stream);
+
 /* The switch step restricted to one shard of the experts, for expert
  * parallelism: the weights passed hold experts [e0, e0 + ne) of the E the
  * router chose from (gate/up w [ne, I, H*bits/32], down w [ne, H, ...]), and

@@ -53,6 +53,17 @@ int nq_comm_abort(nq_comm_t comm);
 int nq_comm_rank(nq_comm_t comm);
 int nq_comm_size(nq_comm_t comm);
 
+/* Allocates this rank's share of a symmetric arena of `bytes` (collective:
+ * every rank calls with the same size) and maps every other rank's share into
+ * this process (CUDA IPC).  Outputs of nq_tp_quantized_matmul_fused live
+ * there; nq_comm_symmetric_ptr(comm, offset) is this rank's address of a byte
+ * offset (the same offset names the same buffer on every rank). */
+int nq_comm_symmetric_alloc(nq_comm_t comm, size_t bytes);
+void *nq_comm_symmetric_ptr(nq_comm_t comm, size_t offset);
+/* Reads and clears the error word of the fused calls (bit 0: a wait for a
+ * peer timed out). */
+int nq_comm_take_error(nq_comm_t comm, unsigned int *value);
+
 /* ---- plans (host only; no GPU needed) ---- */
 
 /* Weight rows of rank `rank` of `nranks`: N must be a multiple of nranks. */
@@ -79,6 +90,18 @@ int nq_tp_quantized_matmul(nq_comm_t comm, const uint16_t *x, int64_t M,
                            int bits, int group_size, uint16_t *y,
                            void *workspace, size_t workspace_bytes,
                            void *stream);
+
+/* nq_tp_quantized_matmul with the all-gather fused into the compute: the
+ * kernel writes this rank's columns straight into every rank's y over
+ * NVLink (peer stores), behind a ready barrier (every rank has finished the
+ * stream work before the call) and followed by a done barrier (every rank's
+ * columns have landed).  y must be a buffer of the symmetric arena, at the
+ * same offset on every rank.  No workspace and no collective library call. */
+int nq_tp_quantized_matmul_fused(nq_comm_t comm, const uint16_t *x, int64_t M,
+                                 const uint32_t *w_shard, const uint16_t *s_shard,
+                                 const uint16_t *b_shard, int64_t N, int64_t K,
+                                 int bits, int group_size, uint16_t *y,
+                                 void *stream);
 
 /* The MoE switch step over T tokens in total, experts and tokens sharded
  * (nq_ep_shard, nq_ep_token_shard).  x_shard [T/P, H], topk_idx_shard and

@@ -6,6 +6,7 @@
 #include <string>
 
 #include "nq.h"
+#include "nq_common.cuh"
 #include "nq_internal.h"
 
 namespace nq {
@@ -208,6 +209,59 @@ int nq_quantized_matmul(const uint16_t *x, int64_t M, const uint32_t *wq, const 
     p.P = 1; p.M = (int)M; p.max_m = (int)M;
     p.y = y; p.y_ld = N;
     return from_cuda(nq::launch_gemv(p, st), "nq_quantized_matmul");
+}
+
+int nq_quantized_matmul_push(const uint16_t *x, int64_t M, const uint32_t *wq,
+                             const uint16_t *scales, const uint16_t *biases, int64_t N, int64_t K,
+                             int bits, int group_size, int64_t N_total, int64_t col0,
+                             const nq_push_t *push, void *stream) {
+    const char *what = "nq_quantized_matmul_push";
+    if (int rc = check_quant(N, K, bits, group_size, what)) return rc;
+    if (M <= 0 || N <= 0) return fail(NQ_INVALID_INPUT, std::string(what) + ": M and N must be > 0");
+    if (!x || !wq || !scales || !biases || !push)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": NULL pointer");
+    if (push->nranks < 1 || push->nranks > NQ_MAX_RANKS || push->rank < 0 ||
+        push->rank >= push->nranks)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": need 0 <= rank < nranks <= 8");
+    if (col0 < 0 || col0 + N > N_total)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": columns outside [0, N_total)");
+    if (!push->ready || !push->epoch)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": NULL flag pointer");
+    for (int q = 0; q < push->nranks; ++q)
+        if (!push->dst[q]) return fail(NQ_INVALID_INPUT, std::string(what) + ": NULL destination");
+    if (!aligned16(x) || !aligned16(wq))
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": x and wq must be 16-byte aligned");
+    if (int rc = need_device(what)) return rc;
+    nq::PushDev pd;
+    pd.n = push->nranks;
+    pd.epoch = push->epoch;
+    pd.ready = push->ready;
+    const char *self = static_cast<const char *>(push->dst[push->rank]);
+    for (int q = 0; q < pd.n; ++q) pd.delta[q] = static_cast<const char *>(push->dst[q]) - self;
+    uint16_t *y = static_cast<uint16_t *>(push->dst[push->rank]) + col0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (M >= tc_threshold()) {
+        nq::TcGemmArgs a;
+        a.x = x; a.x_ld = K; a.M = M;
+        a.w = wq; a.s = scales; a.b = biases;
+        a.N = N; a.K = K; a.bits = bits; a.gs = group_size;
+        a.y = y; a.y_ld = N_total;
+        a.push = &pd;
+        if (!nq::tc_gemm_supported(a))
+            return fail(NQ_INVALID_INPUT, std::string(what) + ": shape not served by the fused path");
+        return from_cuda(nq::launch_tc_gemm(a, st), what);
+    }
+    nq::GemvProblems p;
+    p.w = wq; p.s = scales; p.b = biases;
+    p.N = N; p.K = K; p.bits = bits; p.gs = group_size;
+    p.x = x; p.x_ld = K;
+    p.P = 1; p.M = (int)M; p.max_m = (int)M;
+    p.y = y; p.y_ld = N_total;
+    p.push = &pd;
+    const cudaError_t e = nq::launch_gemv(p, st);
+    if (e == cudaErrorNotSupported)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": shape not served by the fused path");
+    return from_cuda(e, what);
 }
 
 int nq_gather_qmm(const uint16_t *x, int64_t x_batch, int64_t M, const int32_t *lhs_indices,

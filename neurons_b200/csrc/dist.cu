@@ -12,11 +12,25 @@
 #include "nq.h"
 #include "nq_dist.h"
 
+// Symmetric arena: the same number of bytes on every rank, mapped into every
+// other rank's address space with CUDA IPC.  A 4 KB header holds the flags of
+// the fused tensor-parallel calls; the rest is for the callers' outputs.
+//   ready[8] @ 0, done[8] @ 128, error word of the finish kernel @ 384
+constexpr size_t kArenaHeader = 4096;
+//   epoch (the fused calls made, advanced by the ready kernel) @ 448
+//   table of the ready-flag addresses this rank writes (one per rank) @ 512
+//   table of the done-flag addresses this rank writes (one per rank) @ 640
+constexpr size_t kReadyOff = 0, kDoneOff = 128, kErrOff = 384,
+                 kEpochOff = 448, kTableOff = 512, kDoneTableOff = 640;
+
 struct nq_comm_s {
     ncclComm_t nccl = nullptr;
     int rank = 0;
     int size = 1;
     int device = 0;
+    char *arena = nullptr;                 // this rank's arena (header + data)
+    size_t arena_bytes = 0;                // data bytes
+    char *peer[NQ_MAX_RANKS] = {};         // every rank's arena in this process (self included)
 };
 
 namespace {
@@ -116,6 +130,67 @@ EpWorkspace ep_carve(void *base, int64_t T, int64_t E, int64_t top_k, int64_t H,
     return w;
 }
 
+// Advances the call number and sets this rank's ready flag to it in every
+// rank's arena, once the stream's earlier work has completed.  Launched as a
+// programmatic dependent: the compute kernel after it may start (and fetch
+// its weights) at once; it reads the flags only after its own
+// griddepcontrol.wait, i.e. after this kernel completed.
+__global__ void push_ready_kernel(unsigned int *const *flags, int n, unsigned int *epoch) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int q = threadIdx.x;
+    const unsigned int e = *epoch + 1;
+    __syncwarp();
+    if (q == 0) *epoch = e;
+    if (q < n) asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flags[q]), "r"(e)
+                            : "memory");
+}
+
+// After the compute grid (whose completion, awaited by griddepcontrol.wait,
+// means all its stores -- peer stores included -- are performed): publish
+// this rank's done flag to every rank, then wait (bounded) until every rank's
+// done flag here reached the call number.  When this kernel completes, every
+// rank's columns are in this rank's y.
+__global__ void push_finish_kernel(unsigned int *const *done_remote, const unsigned int *done_local,
+                                   int n, const unsigned int *epoch_p, unsigned int *err) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int q = threadIdx.x;
+    const unsigned int epoch = *epoch_p;
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    if (q < n)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(done_remote[q]), "r"(epoch)
+                     : "memory");
+    if (q >= n) return;
+    unsigned long long t0, t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    while (true) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(done_local + q)
+                     : "memory");
+        if ((int)(v - epoch) >= 0) return;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 > 2000000000ull) {
+            atomicOr(err, 1u);
+            return;
+        }
+    }
+}
+
+cudaError_t launch_pdl_1warp(cudaStream_t st, void (*kern)(unsigned int *const *, const unsigned int *, int, const unsigned int *, unsigned int *),
+                             unsigned int *const *a, const unsigned int *b, int n,
+                             const unsigned int *e, unsigned int *err) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a, b, n, e, err);
+}
+
 unsigned grid_for(int64_t n) {
     const int64_t b = (n + 255) / 256;
     return (unsigned)(b < 148 * 16 ? (b > 0 ? b : 1) : 148 * 16);
@@ -156,8 +231,17 @@ int nq_comm_init(nq_comm_t *comm, int nranks, int rank, const unsigned char id[N
     return NQ_SUCCESS;
 }
 
+static void release_arena(nq_comm_t comm) {
+    for (int q = 0; q < comm->size; ++q)
+        if (comm->peer[q] && q != comm->rank) cudaIpcCloseMemHandle(comm->peer[q]);
+    if (comm->arena) cudaFree(comm->arena);
+    comm->arena = nullptr;
+    for (auto &p : comm->peer) p = nullptr;
+}
+
 int nq_comm_destroy(nq_comm_t comm) {
     if (!comm) return NQ_SUCCESS;
+    release_arena(comm);
     const int rc = from_nccl(ncclCommDestroy(comm->nccl), "nq_comm_destroy");
     delete comm;
     return rc;
@@ -165,6 +249,7 @@ int nq_comm_destroy(nq_comm_t comm) {
 
 int nq_comm_abort(nq_comm_t comm) {
     if (!comm) return NQ_SUCCESS;
+    release_arena(comm);
     const int rc = from_nccl(ncclCommAbort(comm->nccl), "nq_comm_abort");
     delete comm;
     return rc;
@@ -172,6 +257,140 @@ int nq_comm_abort(nq_comm_t comm) {
 
 int nq_comm_rank(nq_comm_t comm) { return comm ? comm->rank : -1; }
 int nq_comm_size(nq_comm_t comm) { return comm ? comm->size : -1; }
+
+int nq_comm_symmetric_alloc(nq_comm_t comm, size_t bytes) {
+    const char *what = "nq_comm_symmetric_alloc";
+    if (!comm) return fail(NQ_INVALID_INPUT, std::string(what) + ": NULL communicator");
+    if (comm->arena) return fail(NQ_INVALID_INPUT, std::string(what) + ": already allocated");
+    if (comm->size > NQ_MAX_RANKS)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": more than 8 ranks");
+    bytes = (bytes + 255) & ~size_t(255);
+    char *base = nullptr;
+    if (int rc = from_cuda(cudaMalloc(&base, kArenaHeader + bytes), what)) return rc;
+    cudaIpcMemHandle_t *all = nullptr;
+    cudaIpcMemHandle_t mine;
+    int rc = from_cuda(cudaMemset(base, 0, kArenaHeader), what);
+    if (!rc) rc = from_cuda(cudaIpcGetMemHandle(&mine, base), what);
+    // every rank's handle, through the communicator
+    void *dev = nullptr;
+    if (!rc) rc = from_cuda(cudaMalloc(&dev, sizeof(cudaIpcMemHandle_t) * comm->size), what);
+    if (!rc) rc = from_cuda(cudaMemcpy(static_cast<char *>(dev) + sizeof(mine) * comm->rank, &mine,
+                                       sizeof(mine), cudaMemcpyHostToDevice),
+                            what);
+    if (!rc) rc = from_nccl(ncclAllGather(static_cast<char *>(dev) + sizeof(mine) * comm->rank, dev,
+                                          sizeof(mine), ncclUint8, comm->nccl, nullptr),
+                            what);
+    if (!rc) rc = from_cuda(cudaDeviceSynchronize(), what);
+    if (!rc) {
+        all = new cudaIpcMemHandle_t[comm->size];
+        rc = from_cuda(cudaMemcpy(all, dev, sizeof(mine) * comm->size, cudaMemcpyDeviceToHost), what);
+    }
+    if (dev) cudaFree(dev);
+    comm->arena = base;
+    comm->arena_bytes = bytes;
+    for (int q = 0; !rc && q < comm->size; ++q) {
+        if (q == comm->rank) {
+            comm->peer[q] = base;
+            continue;
+        }
+        void *p = nullptr;
+        rc = from_cuda(cudaIpcOpenMemHandle(&p, all[q], cudaIpcMemLazyEnablePeerAccess), what);
+        comm->peer[q] = static_cast<char *>(p);
+    }
+    delete[] all;
+    if (!rc) {
+        unsigned int *ready_dst[NQ_MAX_RANKS];
+        for (int q = 0; q < comm->size; ++q)
+            ready_dst[q] = reinterpret_cast<unsigned int *>(comm->peer[q] + kReadyOff) + comm->rank;
+        rc = from_cuda(cudaMemcpy(base + kTableOff, ready_dst, sizeof(void *) * comm->size,
+                                  cudaMemcpyHostToDevice),
+                       what);
+        unsigned int *done_dst[NQ_MAX_RANKS];
+        for (int q = 0; q < comm->size; ++q)
+            done_dst[q] = reinterpret_cast<unsigned int *>(comm->peer[q] + kDoneOff) + comm->rank;
+        if (!rc)
+            rc = from_cuda(cudaMemcpy(base + kDoneTableOff, done_dst, sizeof(void *) * comm->size,
+                                      cudaMemcpyHostToDevice),
+                           what);
+    }
+    if (rc) release_arena(comm);
+    return rc;
+}
+
+void *nq_comm_symmetric_ptr(nq_comm_t comm, size_t offset) {
+    if (!comm || !comm->arena || offset >= comm->arena_bytes) return nullptr;
+    return comm->arena + kArenaHeader + offset;
+}
+
+int nq_comm_take_error(nq_comm_t comm, unsigned int *value) {
+    if (!comm || !value) return fail(NQ_INVALID_INPUT, "nq_comm_take_error: NULL argument");
+    *value = 0;
+    if (!comm->arena) return NQ_SUCCESS;
+    unsigned int zero = 0;
+    if (int rc = from_cuda(cudaMemcpy(value, comm->arena + kErrOff, sizeof(unsigned int),
+                                      cudaMemcpyDeviceToHost),
+                           "nq_comm_take_error"))
+        return rc;
+    return from_cuda(cudaMemcpy(comm->arena + kErrOff, &zero, sizeof(zero), cudaMemcpyHostToDevice),
+                     "nq_comm_take_error");
+}
+
+int nq_tp_quantized_matmul_fused(nq_comm_t comm, const uint16_t *x, int64_t M,
+                                 const uint32_t *w_shard, const uint16_t *s_shard,
+                                 const uint16_t *b_shard, int64_t N, int64_t K, int bits,
+                                 int group_size, uint16_t *y, void *stream) {
+    const char *what = "nq_tp_quantized_matmul_fused";
+    if (!comm) return fail(NQ_INVALID_INPUT, std::string(what) + ": NULL communicator");
+    if (!comm->arena)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": call nq_comm_symmetric_alloc first");
+    int64_t row0, rows;
+    if (int rc = split(N, comm->size, comm->rank, &row0, &rows, what)) return rc;
+    if (M <= 0) return fail(NQ_INVALID_INPUT, std::string(what) + ": M must be > 0");
+    char *data = comm->arena + kArenaHeader;
+    const char *yc = reinterpret_cast<const char *>(y);
+    if (yc < data || yc + (size_t)M * N * sizeof(uint16_t) > data + comm->arena_bytes ||
+        (reinterpret_cast<uintptr_t>(y) & 15))
+        return fail(NQ_INVALID_INPUT,
+                    std::string(what) + ": y must lie in the symmetric arena, 16-byte aligned");
+    const size_t off = (size_t)(yc - data);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    unsigned int *epoch = reinterpret_cast<unsigned int *>(comm->arena + kEpochOff);
+    // ready: this rank's earlier stream work is done; tell every rank
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(1);
+        cfg.blockDim = dim3(32);
+        cfg.stream = st;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr.val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        if (int rc = from_cuda(
+                cudaLaunchKernelEx(&cfg, push_ready_kernel,
+                                   reinterpret_cast<unsigned int *const *>(comm->arena + kTableOff),
+                                   comm->size, epoch),
+                what))
+            return rc;
+    }
+    nq_push_t p;
+    std::memset(&p, 0, sizeof(p));
+    p.nranks = comm->size;
+    p.rank = comm->rank;
+    p.epoch = epoch;
+    p.ready = reinterpret_cast<const unsigned int *>(comm->arena + kReadyOff);
+    for (int q = 0; q < comm->size; ++q) p.dst[q] = comm->peer[q] + kArenaHeader + off;
+    if (int rc = from_nq(nq_quantized_matmul_push(x, M, w_shard, s_shard, b_shard, rows, K, bits,
+                                                  group_size, N, row0, &p, stream),
+                         what))
+        return rc;
+    return from_cuda(
+        launch_pdl_1warp(st, push_finish_kernel,
+                         reinterpret_cast<unsigned int *const *>(comm->arena + kDoneTableOff),
+                         reinterpret_cast<const unsigned int *>(comm->arena + kDoneOff),
+                         comm->size, epoch, reinterpret_cast<unsigned int *>(comm->arena + kErrOff)),
+        what);
+}
 
 int nq_tp_shard(int64_t N, int nranks, int rank, int64_t *row0, int64_t *rows) {
     return split(N, nranks, rank, row0, rows, "nq_tp_shard");

@@ -64,6 +64,7 @@ struct TcParams {
     const uint16_t *s, *b;
     uint16_t *y;
     unsigned int *err;
+    PushDev push;  // tensor-parallel fan-out of the stores (n == 0: local only)
 };
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort,
@@ -245,7 +246,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             load_sb(kb + 2 * kSbAhead, sq[kSbAhead - 1], bq[kSbAhead - 1]);
         }
         // ------------------------------------------------ epilogue
-        if (wait_or_abort(accfull, 0, abort, prm.err) && !*abort) {
+        bool acc_ok = wait_or_abort(accfull, 0, abort, prm.err) && !*abort;
+        if (prm.push.n && !push_wait_ready(prm.push, prm.err)) acc_ok = false;
+        if (acc_ok) {
             tc_fence_after();
             const int64_t nrow = n0 + r;
             const int part = warp >> 2;  // quarter of the accumulator columns
@@ -258,7 +261,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 16; ++j) {
                         const int64_t m = m0 + c0 + j;
                         if (m < prm.M)
-                            prm.y[m * prm.y_ld + nrow] = f32_to_bf16(__uint_as_float(acc[j]));
+                            push_store(prm.push, prm.y + m * prm.y_ld + nrow,
+                                       f32_to_bf16(__uint_as_float(acc[j])));
                     }
                 }
             }
@@ -305,6 +309,7 @@ cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
     prm.b = a.b;
     prm.y = a.y;
     prm.err = device_error_word();
+    if (a.push) prm.push = *a.push;
     auto kern = tc_qgemm_kernel<BITS, BM>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::kSmemBytes);

@@ -57,6 +57,7 @@ struct GemvParams {
     int s_cta;      // K slices handled by the warps of one CTA (1, 2 or 4)
     int mx;         // tokens staged per pass (async path)
     unsigned int *err;
+    PushDev push;   // tensor-parallel fan-out of the stores (n == 0: local only)
 };
 
 __device__ __forceinline__ uint4 ldg_stream16(const void *p) {
@@ -926,7 +927,9 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
                 cl.sync();
             }
             if (!indexed) pdl_wait();  // (no-op once the producer's copies landed)
-            if (blockIdx.y == 0) {
+            bool store_ok = true;
+            if (prm.push.n && blockIdx.y == 0) store_ok = push_wait_ready(prm.push, prm.err);
+            if (blockIdx.y == 0 && store_ok) {
 #pragma unroll
                 for (int r = 0; r < RT; ++r)
 #pragma unroll
@@ -941,9 +944,12 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
                             const int64_t row =
                                 prm.y_rows ? (int64_t)prm.y_rows[off + m] : (int64_t)off + m;
                             if (prm.out_f32)
-                                static_cast<float *>(prm.y)[row * prm.y_ld + n] = v;
+                                push_store(prm.push, static_cast<float *>(prm.y) + row * prm.y_ld + n,
+                                           v);
                             else
-                                static_cast<uint16_t *>(prm.y)[row * prm.y_ld + n] = f32_to_bf16(v);
+                                push_store(prm.push,
+                                           static_cast<uint16_t *>(prm.y) + row * prm.y_ld + n,
+                                           f32_to_bf16(v));
                         }
             }
         }
@@ -1029,6 +1035,7 @@ cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
     prm.kb_total = (int)((prm.Kw + 15) / 16);
     prm.kb_full = (int)(prm.Kw / 16);
     prm.err = device_error_word();
+    if (q.push) prm.push = *q.push;
 
     const bool dual = q.w2 != nullptr;
     const int max_m = std::max(1, q.max_m);
@@ -1077,6 +1084,7 @@ cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
     }
 
     // ---- register-fed kernel (when no tensor map can be encoded)
+    if (q.push) return cudaErrorNotSupported;  // the output fan-out is in the TMA-fed kernel only
     const int rt = (!dual && nt == 1 && q.N >= 64) ? 2 : 1;
     const int64_t row_groups = (q.N + 16 * rt - 1) / (16 * rt);
     const int64_t tasks = row_groups * (int64_t)q.P;

@@ -325,6 +325,65 @@ __device__ __forceinline__ void bar_sync(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// ---------------------------------------------- tensor-parallel output push
+// A kernel that computes one rank's column shard of y can write it straight
+// into every rank's y (peer memory mapped with CUDA IPC) instead of handing
+// it to an all-gather.  Per call number `epoch` (the same on every rank,
+// increasing; in device memory, advanced by the ready kernel, so a CUDA graph
+// of the calls stays correct on every replay):
+//   * before the call, every rank's ready kernel sets ready[rank] = epoch in
+//     every rank's memory (its stream's earlier work, which may still read
+//     the buffers being written, has completed);
+//   * a storing warp waits until all `ready` flags reached epoch, then stores
+//     each value once per rank;
+//   * after the kernel, a finish kernel (which the compute grid's completion
+//     -- all its stores performed -- releases) publishes done[rank] = epoch
+//     to every rank and waits for every rank's done flag.
+// Every wait is bounded (kWaitLimitNs) and raises the timeout bit.
+constexpr int kMaxRanks = 8;
+
+struct PushDev {
+    int n = 0;                           // ranks written; 0: plain local stores
+    const unsigned *epoch = nullptr;     // this call's number (device memory)
+    long long delta[kMaxRanks];          // bytes from the local y element to rank q's copy
+    const unsigned *ready = nullptr;     // this rank's ready flags [n]
+};
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Lane 0 of the calling warp waits for every rank's ready flag; false on timeout.
+__device__ __forceinline__ bool push_wait_ready(const PushDev &p, unsigned int *err) {
+    bool ok = true;
+    if ((threadIdx.x & 31) == 0) {
+        const unsigned long long t0 = global_timer_ns();
+        const unsigned epoch = *p.epoch;
+        for (int q = 0; q < p.n && ok; ++q) {
+            while ((int)(ld_acquire_sys(p.ready + q) - epoch) < 0) {
+                if (global_timer_ns() - t0 > kWaitLimitNs) {
+                    atomicOr(err, kErrWaitTimeout);
+                    ok = false;
+                    break;
+                }
+            }
+        }
+    }
+    return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
+template <typename T>
+__device__ __forceinline__ void push_store(const PushDev &p, T *local, T v) {
+    if (p.n == 0) {
+        *local = v;
+        return;
+    }
+    for (int q = 0; q < p.n; ++q)
+        *reinterpret_cast<T *>(reinterpret_cast<char *>(local) + p.delta[q]) = v;
+}
+
 // Programmatic dependent launch: wait for the producing grid / let the next
 // grid start its prologue.  Both are no-ops without the launch attribute.
 __device__ __forceinline__ void pdl_wait() {

@@ -10,6 +10,8 @@
 
 namespace nq {
 
+struct PushDev;
+
 // Thread-local last-error message behind nq_last_error().
 void set_error(const std::string &msg);
 const char *last_error();
@@ -54,6 +56,7 @@ struct GemvProblems {
     int swiglu = 0;                    // 1: y = bf16(silu(x.w^T) * (x.w2^T))
     int max_m = 1;                     // upper bound of tokens per problem
     int tile_m = 0;                    // tokens per pass to size for (0: from max_m)
+    const PushDev *push = nullptr;     // tensor-parallel fan-out of the stores
 };
 
 cudaError_t launch_gemv(const GemvProblems &p, cudaStream_t stream);
@@ -70,6 +73,7 @@ struct TcGemmArgs {
     int bits = 4, gs = 64;
     uint16_t *y = nullptr;         // [M, N] bf16 (row stride y_ld)
     int64_t y_ld = 0;
+    const PushDev *push = nullptr; // tensor-parallel fan-out of the stores
 };
 
 bool tc_gemm_supported(const TcGemmArgs &a);

@@ -41,6 +41,10 @@ SIGNATURES = {
     "nq_comm_abort": (I, [P]),
     "nq_comm_rank": (I, [P]),
     "nq_comm_size": (I, [P]),
+    "nq_comm_symmetric_alloc": (I, [P, U64]),
+    "nq_comm_symmetric_ptr": (P, [P, U64]),
+    "nq_comm_take_error": (I, [P, ctypes.POINTER(ctypes.c_uint)]),
+    "nq_tp_quantized_matmul_fused": (I, [P, P, I64, P, P, P, I64, I64, I, I, P, P]),
     "nq_tp_shard": (I, [I64, I, I, PI64, PI64]),
     "nq_ep_shard": (I, [I64, I, I, PI64, PI64]),
     "nq_ep_token_shard": (I, [I64, I, I, PI64, PI64]),
@@ -126,7 +130,31 @@ class Comm:
                                         group=group)
             ident = ctypes.create_string_buffer(box[0], NQ_COMM_ID_BYTES)
         self.handle = P()
+        self.arena_bytes = 0
         _check(dist_lib().nq_comm_init(ctypes.byref(self.handle), self.size, self.rank, ident))
+
+    def symmetric_alloc(self, nbytes):
+        """Collective: allocate the symmetric arena (same size on every rank)."""
+        _check(dist_lib().nq_comm_symmetric_alloc(self.handle, nbytes))
+        self.arena_bytes = nbytes
+
+    def symmetric_tensor(self, offset, shape, dtype=torch.bfloat16):
+        """A torch view of the arena at a byte offset (the same buffer on every rank)."""
+        n = 1
+        for d in shape:
+            n *= d
+        nbytes = n * torch.empty(0, dtype=dtype).element_size()
+        if offset % 256 or offset + nbytes > self.arena_bytes:
+            raise NQError(1, "symmetric_tensor: outside the arena or not 256-byte aligned")
+        ptr = dist_lib().nq_comm_symmetric_ptr(self.handle, offset)
+        if not ptr:
+            raise NQError(1, "symmetric_tensor: no arena")
+        return _wrap_device(ptr, shape, dtype)
+
+    def take_error(self):
+        v = ctypes.c_uint(0)
+        _check(dist_lib().nq_comm_take_error(self.handle, ctypes.byref(v)))
+        return v.value
 
     def close(self):
         if self.handle:
@@ -141,6 +169,35 @@ class Comm:
 
 def _ptr(t):
     return P(t.data_ptr()) if t is not None else None
+
+
+def _wrap_device(ptr, shape, dtype):
+    """A torch tensor over device memory owned by the library (no copy)."""
+    import numpy as np  # noqa: F401  (dtype sizes only)
+    n = 1
+    for d in shape:
+        n *= d
+    nbytes = n * torch.empty(0, dtype=dtype).element_size()
+    dev = torch.cuda.current_device()
+
+    class _Mem:
+        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                    "version": 3, "strides": None}
+    t = torch.as_tensor(_Mem(), device=f"cuda:{dev}")
+    return t.view(dtype).view(shape)
+
+
+def tp_quantized_matmul_fused(comm, x, wq_shard, s_shard, b_shard, N, out, group_size=64, bits=4):
+    """tp_quantized_matmul with the all-gather fused into the kernel's stores:
+    `out` ([M, N] bf16) must be a symmetric_tensor of the communicator."""
+    ops._need(x, "x", (torch.bfloat16,))
+    ops._need(wq_shard, "w", ops._PACKED)
+    K = int(x.shape[-1])
+    M = x.numel() // K
+    _check(dist_lib().nq_tp_quantized_matmul_fused(
+        comm.handle, _ptr(x), M, _ptr(wq_shard), _ptr(s_shard), _ptr(b_shard), N, K, bits,
+        group_size, _ptr(out), ops._stream()))
+    return out
 
 
 def tp_quantized_matmul(comm, x, wq_shard, s_shard, b_shard, N, group_size=64, bits=4, out=None,

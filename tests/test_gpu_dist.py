@@ -32,6 +32,7 @@ def _worker(rank, world, port, q):
         import neurons_b200 as nb
         from neurons_b200 import dist
         comm = dist.Comm()
+        comm.symmetric_alloc(8 << 20)
         g = torch.Generator(device="cuda").manual_seed(0)
         for (M, N, K, bits) in ((1, 4096, 4096, 4), (7, 2048, 1024, 8), (300, 2048, 1024, 4)):
             w = torch.randn(N, K, device="cuda", generator=g) * 0.02
@@ -43,6 +44,15 @@ def _worker(rank, world, port, q):
                                          b[r0:r0 + rows], N, 64, bits)
             torch.cuda.synchronize()
             out[f"tp{M}"] = (_rel(y, ref), torch.equal(y[:, r0:r0 + rows], ref[:, r0:r0 + rows]))
+            # the fused variant: every rank's columns pushed over NVLink; three
+            # calls on the same symmetric buffer (epochs, buffer reuse)
+            yf = comm.symmetric_tensor(0, (M, N))
+            for _ in range(3):
+                yf.zero_()
+                dist.tp_quantized_matmul_fused(comm, x, wq[r0:r0 + rows], s[r0:r0 + rows],
+                                               b[r0:r0 + rows], N, yf, 64, bits)
+            torch.cuda.synchronize()
+            out[f"fused{M}"] = (_rel(yf, ref), torch.equal(yf, y))
         E, k, H, I = 16, 4, 512, 256
         gate, up, down = (nb.quantize(torch.randn(E, n, kk, device="cuda", generator=g) * 0.02)
                           for n, kk in ((I, H), (I, H), (H, I)))
@@ -60,6 +70,7 @@ def _worker(rank, world, port, q):
             torch.cuda.synchronize()
             out[f"ep{T}"] = (_rel(y, ref[t0:t0 + nt]), True)
         out["device_error"] = (float(nb.take_device_error()), True)
+        out["comm_error"] = (float(comm.take_error()), True)
         comm.close()
     except Exception as e:
         out["error"] = repr(e)
@@ -83,7 +94,10 @@ def test_two_rank_tensor_and_expert_parallel():
         p.join(timeout=120)
     for r, out in res.items():
         assert "error" not in out, (r, out)
-        assert out["device_error"][0] == 0
+        assert out["device_error"][0] == 0 and out["comm_error"][0] == 0
+        for key in ("fused1", "fused7", "fused300"):
+            rel, same_as_nccl = out[key]
+            assert rel < 1e-2 and same_as_nccl, (r, key, out[key])
         for key in ("tp1", "tp7", "tp300"):
             rel, same_cols = out[key]
             assert rel < 1e-2 and same_cols, (r, key, out[key])
