@@ -24,8 +24,9 @@ ROOT = os.path.dirname(HERE)
 INCLUDE = os.path.join(ROOT, "include")
 
 CU_SOURCES = ["abi.cu", "quant.cu", "gemv.cu", "gemm_tc.cu", "gemm_tc_moe.cu", "moe.cu"]
-CPP_SOURCES = ["cuda_backend.cpp"]
-HEADERS = ["nq_common.cuh", "nq_internal.h", "cuda_backend.h", "compute_types.h"]
+CPP_SOURCES = ["cuda_backend.cpp", "model_loader.cpp"]
+HEADERS = ["nq_common.cuh", "nq_internal.h", "cuda_backend.h", "compute_types.h",
+           "model_loader.h"]
 
 DIST_LIB = os.path.join(HERE, "libnq_dist.so")
 DIST_SOURCE = "dist.cu"

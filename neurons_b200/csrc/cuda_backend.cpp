@@ -144,6 +144,12 @@ Result<void> lin(const DeviceTensor &x, const std::string &key, const WeightMap 
     const DeviceTensor &s = sit->second;
     auto bit = wm.find(key + ".biases");
     const DeviceTensor *b = bit == wm.end() ? nullptr : &bit->second;
+    if (w.dtype != DType::U32 && w.dtype != DType::I32)
+        return std::unexpected(Error{ErrorCode::InvalidModel, key + ".weight: packed codes must be uint32"});
+    if (s.dtype != DType::BF16 || (b && b->dtype != DType::BF16))
+        return std::unexpected(Error{ErrorCode::InvalidModel,
+                                     key + ": scales and biases must be bf16 (the dequantized "
+                                           "values are bf16(bf16(s*q) + b))"});
     const int nb = bits(w, s, gs);
     const int64_t K = x.dim(-1);
     const int64_t M = x.numel() / K;

@@ -45,7 +45,7 @@ public:
     static BackendType best_available_backend();
 };
 
-enum class DType { BF16, F32, U32, I32 };
+enum class DType { BF16, F32, U32, I32, F16 };
 
 // A non-owning view of a device tensor (row-major, contiguous).
 struct DeviceTensor {

@@ -49,6 +49,7 @@ struct GemvParams {
     int P, M, E, x_batch;
     const int32_t *expert, *m_count, *m_offset, *x_rows, *lhs, *y_rows;
     int expert_is_p, x_from_offset;
+    int x_div;      // > 0: problem p reads x batch p / x_div (pairs of top_k slots)
     void *y;
     int64_t y_ld;
     int out_f32, swiglu;
@@ -282,7 +283,8 @@ __global__ void __launch_bounds__(128) qgemv_kernel(const GemvParams prm) {
     }
     const int Mp = prm.m_count ? prm.m_count[p] : prm.M;
     const int off = prm.m_offset ? prm.m_offset[p] : p * prm.M;
-    int xi = prm.lhs ? prm.lhs[p] : (prm.x_batch == prm.P ? p : 0);
+    int xi = prm.lhs ? prm.lhs[p]
+                     : (prm.x_div > 0 ? p / prm.x_div : (prm.x_batch == prm.P ? p : 0));
     if (xi < 0 || xi >= prm.x_batch) {
         bad = true;
         xi = 0;
@@ -697,7 +699,8 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
     }
     const int Mp = prm.m_count ? prm.m_count[p] : prm.M;
     const int off = prm.m_offset ? prm.m_offset[p] : p * prm.M;
-    int xi = prm.lhs ? prm.lhs[p] : (prm.x_batch == prm.P ? p : 0);
+    int xi = prm.lhs ? prm.lhs[p]
+                     : (prm.x_div > 0 ? p / prm.x_div : (prm.x_batch == prm.P ? p : 0));
     if (xi < 0 || xi >= prm.x_batch) {
         bad = true;
         xi = 0;
@@ -1025,6 +1028,7 @@ cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
     prm.m_offset = q.m_offset;
     prm.x_rows = q.x_rows;
     prm.lhs = q.lhs;
+    prm.x_div = q.x_div;
     prm.y_rows = q.y_rows;
     prm.expert_is_p = q.expert_is_p ? 1 : 0;
     prm.x_from_offset = q.x_from_offset ? 1 : 0;

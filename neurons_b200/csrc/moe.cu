@@ -22,6 +22,8 @@ constexpr int kMaxTopK = 32;
 // equal logits prefer the lower expert index; output in descending order.
 __global__ void route_kernel(const uint16_t *__restrict__ logits, int64_t T, int E, int top_k,
                              int32_t *__restrict__ idx, float *__restrict__ scores) {
+    pdl_launch_dependents();
+    pdl_wait();  // the logits come from the previous kernel
     const int lane = threadIdx.x & 31;
     const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= T) return;
@@ -158,11 +160,6 @@ __global__ void group_rows_kernel(const uint16_t *__restrict__ x, int64_t H,
     for (int64_t i = lane; i < H / 8; i += 32) dst[i] = src[i];
 }
 
-__global__ void pair_token_kernel(int64_t pairs, int top_k, int32_t *__restrict__ tok) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < pairs) tok[i] = (int32_t)(i / top_k);
-}
-
 // sum_j bf16(score[t, j]) * d[t*k + j, n] over the slots j routed to experts
 // [e0, e0 + ne), slot order 0..k-1; y gets it rounded to bf16, or y_partial
 // gets the fp32 sum (the share of one expert shard)
@@ -170,6 +167,8 @@ __global__ void combine_kernel(const float *__restrict__ d, const float *__restr
                                const int32_t *__restrict__ idx, int e0, int ne, int64_t T,
                                int64_t H, int top_k, uint16_t *__restrict__ y,
                                float *__restrict__ y_partial) {
+    pdl_launch_dependents();
+    pdl_wait();  // d comes from the down projection
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over T * H / 4
     if (i >= T * (H / 4)) return;
     const int64_t t = i / (H / 4);
@@ -196,6 +195,24 @@ __global__ void combine_kernel(const float *__restrict__ d, const float *__restr
 }
 
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Launch as a programmatic dependent of the previous kernel on the stream:
+// the kernel may start early and waits (griddepcontrol.wait) before it reads
+// what that kernel produced.
+template <typename... Args>
+cudaError_t launch_pdl(void (*kern)(Args...), unsigned blocks, unsigned threads,
+                       cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(threads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
 
 // Workspace layout (each region 256-byte aligned), P = T * top_k pairs:
 //   counts[E], offsets[E], cursor[E], pos_token[P], pos_pair[P]   int32
@@ -254,9 +271,8 @@ cudaError_t launch_moe_route(const uint16_t *logits, int64_t T, int64_t E, int64
                              int32_t *idx, float *scores, cudaStream_t stream) {
     if (T == 0) return cudaSuccess;
     const int warps = 8;
-    route_kernel<<<(unsigned)((T + warps - 1) / warps), warps * 32, 0, stream>>>(
-        logits, T, (int)E, (int)top_k, idx, scores);
-    return cudaGetLastError();
+    return launch_pdl(route_kernel, (unsigned)((T + warps - 1) / warps), warps * 32, stream, logits,
+                      T, (int)E, (int)top_k, idx, scores);
 }
 
 size_t moe_workspace_bytes(int64_t T, int64_t E, int64_t top_k, int64_t H, int64_t I) {
@@ -358,9 +374,8 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
             d.y = ws.d;
             d.y_ld = H;
             if ((e = launch_tc_moe(d, stream)) != cudaSuccess) return e;
-            combine_kernel<<<cblocks, thr, 0, stream>>>(ws.d, scores, idx, (int)e0, (int)E, T, H,
-                                                        (int)top_k, y, y_partial);
-            return cudaGetLastError();
+            return launch_pdl(combine_kernel, cblocks, thr, stream, (const float *)ws.d, scores, idx,
+                              (int)e0, (int)E, T, H, (int)top_k, y, y_partial);
         }
         // gate/up: problem = expert, its tokens gathered from x, h rows in grouped order
         up.P = (int)E;
@@ -382,12 +397,11 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
         dn.max_m = up.max_m;
         dn.tile_m = up.tile_m;
     } else {
-        pair_token_kernel<<<pblocks, thr, 0, stream>>>(P, (int)top_k, ws.pos_token);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        // pair i reads token i / top_k
         up.P = (int)P;
         up.M = 1;
         up.expert = idx;
-        up.lhs = ws.pos_token;
+        up.x_div = (int)top_k;
         up.x_batch = (int)T;
         up.max_m = 1;
         dn.P = (int)P;
@@ -398,9 +412,8 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
     }
     if ((e = launch_gemv(up, stream)) != cudaSuccess) return e;
     if ((e = launch_gemv(dn, stream)) != cudaSuccess) return e;
-    combine_kernel<<<cblocks, thr, 0, stream>>>(ws.d, scores, idx, (int)e0, (int)E, T, H,
-                                                (int)top_k, y, y_partial);
-    return cudaGetLastError();
+    return launch_pdl(combine_kernel, cblocks, thr, stream, (const float *)ws.d, scores, idx,
+                      (int)e0, (int)E, T, H, (int)top_k, y, y_partial);
 }
 
 }  // namespace nq

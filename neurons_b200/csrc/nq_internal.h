@@ -47,6 +47,7 @@ struct GemvProblems {
     const int32_t *x_rows = nullptr;   // x row of (p, m); nullptr -> see x_from_offset
     bool x_from_offset = false;        // x row of (p, m) = off(p) + m (else xi(p)*M + m)
     const int32_t *lhs = nullptr;      // [P] x batch of problem p (gather_qmm lhs)
+    int x_div = 0;                     // > 0 (no lhs): x batch of problem p is p / x_div
     int x_batch = 1;
     void *y = nullptr;
     int64_t y_ld = 0;                  // elements between y rows
