@@ -705,7 +705,11 @@ def ours(args):
         for T, n in ((1, 500), (64, 200), (2048, 20)):
             t_m, b_m, f_m, _ = time_moe(T, n, 3, world, seed=rank + 300 + T)
             moe[f"T{T}"] = moe_summary(T, t_m, n, b_m, f_m, world, pk)
-            line["gpu_launches"] += n * (7 if T * 8 > 128 else 5)
+            # router + (pair mode: up, down, combine | grouped: count, scan,
+            # fill, [group_rows on the tensor-core path], up, down, combine)
+            P = T * QWEN3_MOE["top_k"]
+            line["gpu_launches"] += n * (4 if P <= QWEN3_MOE["E"] else
+                                         (8 if P >= 8 * QWEN3_MOE["E"] else 7))
         line["moe"] = moe
     if args.workload == "prefill" and not args.no_sharded:
         line["sharded"] = sharded_summary(world, rank, pk)
@@ -800,7 +804,7 @@ def ours_moe(args, world, rank, local, pk):
     t, byts, flops, clk = time_moe(T, args.steps, args.warmup, world, seed=rank,
                                    clocks=ClockSampler(local))
     s = moe_summary(T, t, args.steps, byts, flops, world, pk)
-    tensor = T * QWEN3_MOE["top_k"] >= 16 * QWEN3_MOE["E"]
+    tensor = T * QWEN3_MOE["top_k"] >= 8 * QWEN3_MOE["E"]
     line = {"metric": METRIC, "value": s["tflops"] if tensor else s["gbs"],
             "unit": "TFLOP/s" if tensor else "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3, "higher_is_better": True,

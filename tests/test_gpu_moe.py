@@ -160,8 +160,8 @@ def test_golden_switch(oracle, nqlib):
                                        (3, 16, 4, 256, 128), (64, 16, 4, 256, 128),
                                        (100, 8, 2, 128, 64), (600, 4, 2, 256, 128)])
 def test_switch_matches_oracle(oracle, nqlib, T, E, k, H, I):
-    """pair mode (T*k <= E), grouped GEMV mode (E < T*k < 16 E) and the grouped
-    tensor-core mode (T*k >= 16 E; (600, 4, 2) puts ~300 tokens on every expert,
+    """pair mode (T*k <= E), grouped GEMV mode (E < T*k < 8 E) and the grouped
+    tensor-core mode (T*k >= 8 E; (600, 4, 2) puts ~300 tokens on every expert,
     more than one 256-token tile)."""
     rng = np.random.default_rng(T * 31 + E)
     gate = experts(oracle, rng, E, I, H)
