@@ -585,7 +585,14 @@ def sharded_summary(world, rank, pk):
                            "us_per_step": t / n * 1e6,
                            "tflops": 2 * 2048 * k * 3 * I * H * n / t / 1e12}
     comm.close()
-    return out
+    # this rank's kernels: per prefill step the shard's quantized matmul (1 or 2
+    # kernels) plus the layout kernel (NCCL) or plus the ready and finish kernels
+    # (fused); one GEMV per decode step (plus ready and finish when fused); nine
+    # kernels per expert-parallel step.  NCCL's own kernels are not counted.
+    import neurons_b200 as nb
+    q = nb.quantized_matmul_launches(M, dist.tp_shard(N, world, rank)[1], K, GS, BITS)
+    launches = 30 * (q + 1) + 30 * (q + 2) + 200 + 200 * 3 + 10 * 9
+    return out, launches
 
 
 class CpuSample:
@@ -656,7 +663,8 @@ def ours(args):
     t_dev, per_launch, sets, clk = time_device(M, N, K, args.steps, args.warmup, world,
                                                seed=rank, clocks=ClockSampler(local))
     flops, byts = algo_flops(M, N, K), algo_bytes(M, N, K)
-    launches = args.steps
+    per_call = nb.quantized_matmul_launches(M, N, K, GS, BITS)  # 2: split wave tail
+    launches = args.steps * per_call
     if M > 1:
         value = world * flops * args.steps / t_dev / 1e12
         unit = "TFLOP/s"
@@ -673,6 +681,9 @@ def ours(args):
                 "frac": achieved / pk["hbm_gbs"], "peak_source": pk["source"],
                 "algorithmic_bytes_per_launch": byts}
     roof["traffic"] = ncu_traffic(args.workload)
+    # one call = the whole-tile grid, plus a clustered tail kernel when the last
+    # wave is split; "achieved" is per call
+    roof["kernels_per_call"] = per_call
     if args.kernel_only:
         if rank == 0:
             print(json.dumps({"workload": args.workload, "value": value, "unit": unit,
@@ -712,11 +723,8 @@ def ours(args):
                                          (8 if P >= 8 * QWEN3_MOE["E"] else 7))
         line["moe"] = moe
     if args.workload == "prefill" and not args.no_sharded:
-        line["sharded"] = sharded_summary(world, rank, pk)
-        # qmm + layout kernel per prefill step, one GEMV per decode step, ready +
-        # compute + done-wait per fused step, nine kernels per expert-parallel
-        # step (NCCL's own kernels not counted)
-        line["gpu_launches"] += 2 * 30 + 3 * 30 + 200 + 3 * 200 + 9 * 10
+        line["sharded"], n_sh = sharded_summary(world, rank, pk)
+        line["gpu_launches"] += n_sh
     if args.workload == "prefill" and not args.no_decode:
         t_r, rp, _ = time_replay(50, 3, world, seed=rank + 200)
         line["llama3b_decode"] = replay_summary(t_r, 50, rp, world, pk)
@@ -727,7 +735,7 @@ def ours(args):
         1e12 if M > 1 else 1e9)
     line["e2e"] = {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": h2d,
                    "d2h_bytes_per_step": d2h}
-    line["gpu_launches"] += min(args.steps, 50)
+    line["gpu_launches"] += min(args.steps, 50) * per_call
     if rank == 0 and world == 1 and not args.no_cpu:
         cb = cpu_baseline(M, N, K)
         line["cpu_baseline"] = {

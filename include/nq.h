@@ -99,6 +99,13 @@ int nq_quantized_matmul(const uint16_t *x, int64_t M, const uint32_t *wq,
                         int64_t N, int64_t K, int bits, int group_size,
                         uint16_t *y, void *stream);
 
+/* Number of kernels one nq_quantized_matmul call of this shape launches on the
+ * current device (no reference counterpart: profiling aid).  1 for the GEMV
+ * and for most tensor-core problems; 2 when the tensor-core grid's last wave
+ * is split along K (a clustered tail kernel, then the whole tiles); 0 for
+ * M == 0 or N == 0; a negative status for invalid arguments. */
+int nq_quantized_matmul_launches(int64_t M, int64_t N, int64_t K, int bits, int group_size);
+
 /* mx::gather_qmm(x, w, scales, biases, lhs_indices, rhs_indices,
  * transpose=true, gs, bits).
  *   x: [x_batch, M, K] bf16;  w: [E, N, K*bits/32];  scales/biases [E, N, K/gs]

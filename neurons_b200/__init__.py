@@ -10,11 +10,12 @@ a decode-step replay of LlamaModel's quantized linears (replay.py).
 from ._lib import LIB_PATH, NQError, lib
 from .ops import (SCHEME_MINMAX, SCHEME_MLX_AFFINE, bits, dequantize, gather_qmm, lin,
                   moe_partial_workspace_size, moe_route, moe_switch, moe_switch_partial,
-                  moe_workspace_size, quantize, quantized_matmul, take_device_error)
+                  moe_workspace_size, quantize, quantized_matmul, quantized_matmul_launches,
+                  take_device_error)
 
 __all__ = [
     "LIB_PATH", "NQError", "lib", "SCHEME_MINMAX", "SCHEME_MLX_AFFINE", "bits", "dequantize",
     "gather_qmm", "lin", "moe_partial_workspace_size", "moe_route", "moe_switch",
     "moe_switch_partial", "moe_workspace_size", "quantize",
-    "quantized_matmul", "take_device_error",
+    "quantized_matmul", "quantized_matmul_launches", "take_device_error",
 ]

@@ -29,6 +29,7 @@ SIGNATURES = {
     "nq_quantize": (I, [P, I, I64, I64, I, I, I, P, P, P, P]),
     "nq_dequantize": (I, [P, P, P, I64, I64, I, I, P, P]),
     "nq_quantized_matmul": (I, [P, I64, P, P, P, I64, I64, I, I, P, P]),
+    "nq_quantized_matmul_launches": (I, [I64, I64, I64, I, I]),
     "nq_gather_qmm": (I, [P, I64, I64, P, P, I64, P, P, P, I64, I64, I64, I, I, P, P]),
     "nq_moe_route": (I, [P, I64, I64, I64, P, P, P]),
     "nq_moe_workspace_size": (U64, [I64, I64, I64, I64, I64]),

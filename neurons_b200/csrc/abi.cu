@@ -211,6 +211,23 @@ int nq_quantized_matmul(const uint16_t *x, int64_t M, const uint32_t *wq, const 
     return from_cuda(nq::launch_gemv(p, st), "nq_quantized_matmul");
 }
 
+int nq_quantized_matmul_launches(int64_t M, int64_t N, int64_t K, int bits, int group_size) {
+    if (int rc = check_quant(N, K, bits, group_size, "nq_quantized_matmul_launches")) return rc;
+    if (M < 0) return fail(NQ_INVALID_INPUT, "nq_quantized_matmul_launches: M must be >= 0");
+    if (M == 0 || N == 0) return 0;
+    if (int rc = need_device("nq_quantized_matmul_launches")) return rc;
+    if (M >= tc_threshold()) {
+        // the shape alone decides; any 16-byte aligned operands take the same path
+        static const uint4 aligned_probe[1] = {};
+        nq::TcGemmArgs a;
+        a.x = reinterpret_cast<const uint16_t *>(aligned_probe); a.x_ld = K; a.M = M;
+        a.w = reinterpret_cast<const uint32_t *>(aligned_probe);
+        a.N = N; a.K = K; a.bits = bits; a.gs = group_size; a.y_ld = N;
+        if (const int n = nq::tc_gemm_launches(a)) return n;
+    }
+    return 1;
+}
+
 int nq_quantized_matmul_push(const uint16_t *x, int64_t M, const uint32_t *wq,
                              const uint16_t *scales, const uint16_t *biases, int64_t N, int64_t K,
                              int bits, int group_size, int64_t N_total, int64_t col0,

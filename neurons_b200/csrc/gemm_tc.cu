@@ -22,10 +22,21 @@
 //               from shared memory, fp32 accumulator (128 lanes x BM columns)
 //               in TMEM; tcgen05.commit releases stages back to the producer.
 //   Epilogue: warps 0..15 read the accumulator with tcgen05.ld (lane = weight
-//   row, column = token; a quarter of the columns each) and store bf16 y.
-// Every mbarrier wait is bounded; on a timeout the CTA raises the device
-// error word, stops issuing work, lets in-flight operations drain and frees
-// its TMEM before returning.
+//   row, column = token; a quarter of the columns each), stage the bf16 tile
+//   in the (now idle) ring's shared memory and one thread writes it with a
+//   TMA tensor store -- the CTA leaves as soon as the store has read shared
+//   memory.  (Tensor-parallel fan-out and outputs a tensor map cannot
+//   describe keep per-thread stores.)
+// Wave tail: one CTA fits an SM, so a tile count just above a multiple of the
+// SM count leaves a last wave of a few CTAs that takes as long as a full one
+// (2048 x 14336 at 256 x 128 tiles: 896 = 6 x 148 + 8).  The last `rem` tiles
+// are split along K over a cluster of S CTAs each (S = 2, 4 or 8).  Every CTA
+// of a cluster stages its fp32 partial tile in its own shared memory (free
+// once the main loop is done); after a cluster barrier each CTA sums 1/S of
+// the tile's tokens over the S partials through distributed shared memory and
+// stores them.  The split kernel is launched first and lets the whole-tile
+// grid start beside it (programmatic dependent launch), so the tail runs on a
+// few SMs while the others already work through the whole tiles.
 #include <cuda.h>
 
 #include <mutex>
@@ -43,6 +54,7 @@ constexpr int kStageArrivals = 8;   // of the 16 dequant warps, those working on
 constexpr int kProducerWarp = 16;
 constexpr int kMmaWarp = 17;
 constexpr int kThreads = 576;
+constexpr int kSplitMax = 8;      // CTAs (one cluster) per split tail tile, at most
 
 template <int BITS, int BM>
 struct TcCfg {
@@ -53,7 +65,7 @@ struct TcCfg {
     static constexpr int kACol0 = BM;                                  // first A-stage column
     static constexpr int kTmemCols = 512;
     static_assert(kACol0 + kStages * 32 <= kTmemCols, "TMEM budget");
-    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 512 /*barriers*/;
     static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
@@ -61,11 +73,32 @@ struct TcParams {
     int64_t M, N, K, x_ld, y_ld;
     int gs_shift;  // log2(group size)
     int num_kb;
+    int n_tiles;      // weight-row tiles; tile t: rows (t % n_tiles) * 128, tokens (t / n_tiles) * BM
+    int main_tiles;   // tiles computed whole, one CTA each; the rest are split along K
+    int split;        // CTAs (one cluster) per split tile: 2, 4 or 8
+    int tma_store;    // whole tiles leave through the y tensor map
     const uint16_t *s, *b;
     uint16_t *y;
     unsigned int *err;
     PushDev push;  // tensor-parallel fan-out of the stores (n == 0: local only)
 };
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+
+// 16 bytes of CTA `rank`'s shared memory at the offset of `local` in this CTA
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(rank));
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(remote)
+                 : "memory");
+    return v;
+}
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort,
                                               unsigned int *err) {
@@ -82,10 +115,14 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
     }
 }
 
-template <int BITS, int BM>
+// SPLIT = false: one CTA per tile on the (weight tile, token tile) grid.
+// SPLIT = true: the tail -- a 1-D grid of prm.split CTAs per tile, for the
+// tiles from prm.main_tiles on.
+template <int BITS, int BM, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_qgemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
-                    const __grid_constant__ CUtensorMap tmap_w, const TcParams prm) {
+                    const __grid_constant__ CUtensorMap tmap_w,
+                    const __grid_constant__ CUtensorMap tmap_y, const TcParams prm) {
     using Cfg = TcCfg<BITS, BM>;
     constexpr int S = Cfg::kStages;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -103,9 +140,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int64_t n0 = (int64_t)blockIdx.x * kBlockW;
-    const int64_t m0 = (int64_t)blockIdx.y * BM;
-    const int num_kb = prm.num_kb;
+    // tile origin and this CTA's k-blocks [kb0, kb0 + num_kb).  (The whole-tile
+    // instance reads the origin straight from blockIdx: deriving it by division
+    // measurably slows the main loop.)
+    int tile = 0, ks = 0, nsplit = 1, kb0 = 0, num_kb = prm.num_kb;
+    int64_t n0 = (int64_t)blockIdx.x * kBlockW, m0 = (int64_t)blockIdx.y * BM;
+    if constexpr (!SPLIT) {
+        // the last row's tail tiles belong to the split launch (uniform over the CTA,
+        // before any barrier or TMEM)
+        if ((int)(blockIdx.y * gridDim.x + blockIdx.x) >= prm.main_tiles) return;
+    } else {
+        // the whole-tile grid is launched after this one as a programmatic
+        // dependent: let it fill the other SMs now
+        pdl_launch_dependents();
+        nsplit = prm.split;
+        tile = prm.main_tiles + (int)blockIdx.x / nsplit;
+        ks = (int)blockIdx.x % nsplit;
+        n0 = (int64_t)(tile % prm.n_tiles) * kBlockW;
+        m0 = (int64_t)(tile / prm.n_tiles) * BM;
+        kb0 = (int)(((int64_t)ks * prm.num_kb) / nsplit);
+        num_kb = (int)(((int64_t)(ks + 1) * prm.num_kb) / nsplit) - kb0;
+    }
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -120,6 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kProducerWarp && lane == 0) {
         prefetch_tmap(&tmap_x);
         prefetch_tmap(&tmap_w);
+        if (!SPLIT && prm.tma_store) prefetch_tmap(&tmap_y);
     }
     if (warp == kMmaWarp) {
         tmem_alloc(tmem_holder, Cfg::kTmemCols);
@@ -133,9 +189,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kProducerWarp) {
         if (lane == 0) {
             const uint32_t bytes = Cfg::kXStageBytes + Cfg::kWStageBytes;
-            for (int kb = 0; kb < num_kb; ++kb) {
-                const int s = kb % S;
-                const uint32_t ph = (uint32_t)(kb / S) & 1u;
+            for (int i = 0; i < num_kb; ++i) {
+                const int s = i % S;
+                const uint32_t ph = (uint32_t)(i / S) & 1u;
+                const int kb = kb0 + i;
                 if (!wait_or_abort(&empty[s], ph ^ 1u, abort, prm.err)) break;
                 mbar_expect_tx(&full[s], bytes);
                 tma_load_2d(xs + s * Cfg::kXStageBytes, &tmap_x, &full[s], kb * kBlockK, (int32_t)m0);
@@ -146,9 +203,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16_f32(kBlockW, BM);
-            for (int kb = 0; kb < num_kb; ++kb) {
-                const int s = kb % S;
-                const uint32_t ph = (uint32_t)(kb / S) & 1u;
+            for (int i = 0; i < num_kb; ++i) {
+                const int s = i % S;
+                const uint32_t ph = (uint32_t)(i / S) & 1u;
                 if (!wait_or_abort(&full[s], ph, abort, prm.err)) break;
                 if (!wait_or_abort(&afull[s], ph, abort, prm.err)) break;
                 tc_fence_after();
@@ -158,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t a_tmem = tmem_base + (uint32_t)(Cfg::kACol0 + s * 32 + j * 8);
                     // +32 bytes per 16 bf16 of K inside the 128-byte swizzled row
                     umma_ts(tmem_base, a_tmem, bdesc + (uint64_t)(j * 2), idesc,
-                            (kb > 0 || j > 0) ? 1u : 0u);
+                            (i > 0 || j > 0) ? 1u : 0u);
                 }
                 umma_commit(&empty[s]);
             }
@@ -168,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------ dequantizers
         const int q = warp & 3;          // TMEM lane quadrant
         const int h = (warp >> 2) & 1;   // which 32 codes of the stage
-        const int par = warp >> 3;       // which stages: kb % 2 == par
+        const int par = warp >> 3;       // which stages: (kb - kb0) % 2 == par
         const int r = q * 32 + lane;     // weight row inside the tile
         const int64_t n = n0 + r;
         const bool row_ok = n < prm.N;
@@ -179,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int k = kb * kBlockK + 32 * h;
             sv = 0;
             bv = 0;
-            if (row_ok && kb < num_kb && k < prm.K) {
+            if (row_ok && kb < kb0 + num_kb && k < prm.K) {
                 sv = srow[k >> prm.gs_shift];
                 bv = brow[k >> prm.gs_shift];
             }
@@ -189,11 +246,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // warp's iterations before its use, which covers an HBM round trip.
         uint16_t sq[kSbAhead], bq[kSbAhead];
 #pragma unroll
-        for (int i = 0; i < kSbAhead; ++i) load_sb(par + 2 * i, sq[i], bq[i]);
+        for (int i = 0; i < kSbAhead; ++i) load_sb(kb0 + par + 2 * i, sq[i], bq[i]);
         const uint32_t t_lane = (uint32_t)(q * 32) << 16;
-        for (int kb = par; kb < num_kb; kb += 2) {
-            const int s = kb % S;
-            const uint32_t ph = (uint32_t)(kb / S) & 1u;
+        for (int it = par; it < num_kb; it += 2) {
+            const int kb = kb0 + it;
+            const int s = it % S;
+            const uint32_t ph = (uint32_t)(it / S) & 1u;
             if (!wait_or_abort(&full[s], ph, abort, prm.err)) break;
             tc_fence_after();
             uint32_t out[16];
@@ -247,11 +305,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // ------------------------------------------------ epilogue
         bool acc_ok = wait_or_abort(accfull, 0, abort, prm.err) && !*abort;
-        if (prm.push.n && !push_wait_ready(prm.push, prm.err)) acc_ok = false;
+        const int part = warp >> 2;  // quarter of the accumulator columns
+        if constexpr (SPLIT) {
+            // the partial tile into this CTA's shared memory, [token][row] fp32
+            // (every MMA and every dequantizer read of the ring is done)
+            float *part_sm = reinterpret_cast<float *>(smem);
+            if (acc_ok) {
+                tc_fence_after();
+                for (int c0 = part * (BM / 4); c0 < (part + 1) * (BM / 4); c0 += 16) {
+                    uint32_t acc[16];
+                    tmem_ld_32x32b_x16(tmem_base + t_lane + (uint32_t)c0, acc);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) part_sm[(c0 + j) * kBlockW + r] = __uint_as_float(acc[j]);
+                }
+            }
+            acc_ok = false;
+        }
+        if (!SPLIT && prm.tma_store) {
+            // bf16 tile [BM tokens][128 rows] in shared memory, then one TMA store
+            uint8_t *stage = smem;
+            if (acc_ok) {
+                tc_fence_after();
+                for (int c0 = part * (BM / 4); c0 < (part + 1) * (BM / 4); c0 += 16) {
+                    uint32_t acc[16];
+                    tmem_ld_32x32b_x16(tmem_base + t_lane + (uint32_t)c0, acc);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        *reinterpret_cast<uint16_t *>(stage + ((c0 + j) * kBlockW + r) * 2) =
+                            f32_to_bf16(__uint_as_float(acc[j]));
+                }
+            }
+            fence_proxy_async_smem();
+            bar_sync(1, 16 * 32);
+            if (threadIdx.x == 0 && acc_ok) {
+                tma_store_2d(&tmap_y, stage, (int32_t)n0, (int32_t)m0);
+                bulk_commit_group();
+                bulk_wait_group_read0();
+            }
+            acc_ok = false;
+        }
+        if (prm.push.n && acc_ok && !push_wait_ready(prm.push, prm.err)) acc_ok = false;
         if (acc_ok) {
             tc_fence_after();
             const int64_t nrow = n0 + r;
-            const int part = warp >> 2;  // quarter of the accumulator columns
             for (int c0 = part * (BM / 4); c0 < (part + 1) * (BM / 4); c0 += 16) {
                 uint32_t acc[16];
                 tmem_ld_32x32b_x16(tmem_base + t_lane + (uint32_t)c0, acc);
@@ -269,6 +367,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+    if constexpr (SPLIT) {
+        // sum this CTA's share of the tile's tokens over the cluster's partials
+        cluster_sync_all();
+        const int tpc = BM / nsplit;
+        const int tok0 = ks * tpc;
+        bool store_ok = !*abort;
+        if (prm.push.n && !push_wait_ready(prm.push, prm.err)) store_ok = false;
+        const uint32_t part_u32 = smem_u32(smem);
+        for (int qd = threadIdx.x; qd < tpc * (kBlockW / 4); qd += kThreads) {
+            const int tok = tok0 + qd / (kBlockW / 4);
+            const int row = (qd % (kBlockW / 4)) * 4;
+            const uint32_t off = part_u32 + (uint32_t)((tok * kBlockW + row) * 4);
+            float4 src[kSplitMax];
+#pragma unroll
+            for (int c = 0; c < kSplitMax; ++c)
+                src[c] = c < nsplit ? ld_dsmem_f4(off, (uint32_t)c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 v = src[0];
+#pragma unroll
+            for (int c = 1; c < kSplitMax; ++c) {
+                v.x += src[c].x;
+                v.y += src[c].y;
+                v.z += src[c].z;
+                v.w += src[c].w;
+            }
+            const int64_t m = m0 + tok, nr = n0 + row;
+            if (!store_ok || m >= prm.M) continue;
+            uint16_t *dst = prm.y + m * prm.y_ld + nr;
+            if (nr + 4 <= prm.N && (reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+                const uint2 pk = make_uint2(pack_bf2(v.x, v.y), pack_bf2(v.z, v.w));
+                push_store(prm.push, reinterpret_cast<uint2 *>(dst), pk);
+            } else {
+                const float e[4] = {v.x, v.y, v.z, v.w};
+                for (int i = 0; i < 4; ++i)
+                    if (nr + i < prm.N) push_store(prm.push, dst + i, f32_to_bf16(e[i]));
+            }
+        }
+        cluster_sync_all();  // the peers' reads of this CTA's partial are done
+    } else {
+        // (launched after the split tail as its programmatic dependent: completing
+        // only after the tail grid keeps the stream's order for later work)
+        if (prm.split > 1) pdl_wait();
+    }
     tc_fence_before();
     __syncthreads();
     if (warp == kMmaWarp) {
@@ -285,6 +425,74 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------- host side
 
+// CTAs per tail tile (1: no split): the last T % W tiles (one CTA per SM on W
+// SMs) are split along K when they would leave more than half the SMs idle;
+// S is a power of two (it divides the token tile), at most 8 (a portable
+// cluster) and leaves at least two k-blocks per CTA.
+int tail_split(int64_t T, int W, int num_kb) {
+    const int64_t rem = T % W;
+    if (rem == 0 || rem > W / 2) return 1;
+    int S = 1;
+    while (S * 2 <= kSplitMax && rem * S * 2 <= W && num_kb >= 4 * S) S *= 2;
+    return S;
+}
+
+// Clusters of S split-tail CTAs that can be resident at once on this device
+// (asked once per device and S).
+template <int BITS, int BM>
+int max_clusters(int S) {
+    using Cfg = TcCfg<BITS, BM>;
+    constexpr int kDev = 64;
+    static std::mutex mu;
+    static int cache[kDev][kSplitMax + 1];
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kDev || S > kSplitMax) {
+        cudaGetLastError();
+        return 0;
+    }
+    std::lock_guard<std::mutex> lk(mu);
+    if (cache[d][S] == 0) {
+        auto kern = tc_qgemm_kernel<BITS, BM, true>;
+        int clusters = 0;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Cfg::kSmemBytes) == cudaSuccess) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)(S * 64), 1, 1);
+            cfg.blockDim = dim3(kThreads, 1, 1);
+            cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+            cudaLaunchAttribute attr;
+            attr.id = cudaLaunchAttributeClusterDimension;
+            attr.val.clusterDim.x = (unsigned)S;
+            attr.val.clusterDim.y = 1;
+            attr.val.clusterDim.z = 1;
+            cfg.attrs = &attr;
+            cfg.numAttrs = 1;
+            if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) clusters = 0;
+        }
+        cudaGetLastError();
+        cache[d][S] = clusters > 0 ? clusters : -1;
+    }
+    return cache[d][S];
+}
+
+// How a problem is cut: tiles [0, main_tiles) whole, the rest split over
+// `split` CTAs each (split == 1: no split tail).
+template <int BITS, int BM>
+void plan_bm(const TcGemmArgs &a, int64_t *main_tiles, int *split) {
+    const int64_t tiles = ((a.N + kBlockW - 1) / kBlockW) * ((a.M + BM - 1) / BM);
+    const int num_kb = (int)((a.K + kBlockK - 1) / kBlockK);
+    *main_tiles = tiles;
+    *split = 1;
+    int S = tail_split(tiles, sm_count(), num_kb);
+    const int64_t rem = tiles % sm_count();
+    // every cluster of the tail should be resident at once
+    while (S > 1 && max_clusters<BITS, BM>(S) < rem) S /= 2;
+    if (S > 1) {
+        *main_tiles = tiles - rem;
+        *split = S;
+    }
+}
+
 template <int BITS, int BM>
 cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
     using Cfg = TcCfg<BITS, BM>;
@@ -297,7 +505,14 @@ cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
                      kBlockK * BITS / 32, kBlockW,
                      BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
         return cudaErrorInvalidValue;
+    CUtensorMap my;
+    const bool y_map = !a.push && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.y_ld % 8 == 0 &&
+                       make_map_2d(&my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.y, (uint64_t)a.N,
+                                   (uint64_t)a.M, (uint64_t)a.y_ld * 2, kBlockW, BM,
+                                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!y_map) my = mx;  // unused
     TcParams prm;
+    prm.tma_store = y_map ? 1 : 0;
     prm.M = a.M;
     prm.N = a.N;
     prm.K = a.K;
@@ -310,12 +525,56 @@ cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
     prm.y = a.y;
     prm.err = device_error_word();
     if (a.push) prm.push = *a.push;
-    auto kern = tc_qgemm_kernel<BITS, BM>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         Cfg::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    dim3 grid((unsigned)((a.N + kBlockW - 1) / kBlockW), (unsigned)((a.M + BM - 1) / BM), 1);
-    kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(mx, mw, prm);
+    const int64_t n_tiles = (a.N + kBlockW - 1) / kBlockW;
+    const int64_t tiles = n_tiles * ((a.M + BM - 1) / BM);
+    if (tiles > ((int64_t)1 << 30)) return cudaErrorInvalidValue;
+    prm.n_tiles = (int)n_tiles;
+    int64_t main_tiles = tiles;
+    plan_bm<BITS, BM>(a, &main_tiles, &prm.split);
+    prm.main_tiles = (int)main_tiles;
+    // The split tail first (an ordinary launch: it starts after the previous
+    // work on the stream), then the whole tiles on the (weight tile, token tile)
+    // grid as its programmatic dependent, so that they run beside the tail.
+    if (prm.split > 1) {
+        cudaError_t e = cudaFuncSetAttribute(tc_qgemm_kernel<BITS, BM, true>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Cfg::kSmemBytes);
+        if (e != cudaSuccess) return e;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)((tiles - prm.main_tiles) * prm.split), 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = (unsigned)prm.split;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, tc_qgemm_kernel<BITS, BM, true>, mx, mw, my, prm);
+        if (e != cudaSuccess) return e;
+    }
+    if (prm.main_tiles > 0) {
+        auto kern = tc_qgemm_kernel<BITS, BM, false>;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Cfg::kSmemBytes);
+        if (e != cudaSuccess) return e;
+        const int64_t full_rows = (prm.main_tiles + n_tiles - 1) / n_tiles;
+        if (full_rows > 65535) return cudaErrorInvalidValue;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)n_tiles, (unsigned)full_rows, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr.val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = prm.split > 1 ? 1 : 0;
+        e = cudaLaunchKernelEx(&cfg, kern, mx, mw, my, prm);
+        if (e != cudaSuccess) return e;
+    }
     return cudaGetLastError();
 }
 
@@ -368,6 +627,21 @@ bool tc_gemm_supported(const TcGemmArgs &a) {
     if ((a.x_ld * 2) % 16 || (a.K * a.bits / 8) % 16) return false;
     if (a.M > ((int64_t)1 << 31) - 1 || a.N > ((int64_t)1 << 31) - 1) return false;
     return encode_fn() != nullptr;
+}
+
+template <int BITS>
+int launches_bits(const TcGemmArgs &a) {
+    int64_t main_tiles = 0;
+    int split = 1;
+    if (a.M <= 64) plan_bm<BITS, 64>(a, &main_tiles, &split);
+    else if (a.M <= 128) plan_bm<BITS, 128>(a, &main_tiles, &split);
+    else plan_bm<BITS, 256>(a, &main_tiles, &split);
+    return (main_tiles > 0 ? 1 : 0) + (split > 1 ? 1 : 0);
+}
+
+int tc_gemm_launches(const TcGemmArgs &a) {
+    if (!tc_gemm_supported(a)) return 0;
+    return a.bits == 4 ? launches_bits<4>(a) : launches_bits<8>(a);
 }
 
 cudaError_t launch_tc_gemm(const TcGemmArgs &a, cudaStream_t stream) {

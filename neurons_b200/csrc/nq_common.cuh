@@ -172,6 +172,24 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *tmap, ui
         : "memory");
 }
 
+// TMA store of a 2-D box from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const void *tmap, const void *smem_src, int32_t c0,
+                                             int32_t c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+        "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until the committed bulk stores have read their shared-memory source.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
@@ -348,6 +366,12 @@ struct PushDev {
     long long delta[kMaxRanks];          // bytes from the local y element to rank q's copy
     const unsigned *ready = nullptr;     // this rank's ready flags [n]
 };
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
     unsigned v;

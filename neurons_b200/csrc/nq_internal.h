@@ -86,6 +86,9 @@ bool make_map_2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint6
                  uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
                  CUtensorMapSwizzle sw);
 cudaError_t launch_tc_gemm(const TcGemmArgs &a, cudaStream_t stream);
+// Kernel launches launch_tc_gemm makes for `a` on the current device (1, or 2
+// when the wave tail is split; 0 when the problem does not suit the path).
+int tc_gemm_launches(const TcGemmArgs &a);
 
 // True when cuTensorMapEncodeTiled could be resolved from the driver.
 bool tensor_maps_available();

@@ -104,6 +104,14 @@ def quantized_matmul(x, wq, scales, biases=None, transpose=True, group_size=64, 
     return out
 
 
+def quantized_matmul_launches(M, N, K, group_size=64, bits=4):
+    """Kernels one quantized_matmul of an [M, K] x [N, K]^T problem launches on the
+    current device: 1, or 2 when the tensor-core grid's last wave is split."""
+    n = lib().nq_quantized_matmul_launches(int(M), int(N), int(K), bits, group_size)
+    check(min(n, 0))
+    return n
+
+
 def gather_qmm(x, wq, scales, biases, lhs_indices=None, rhs_indices=None, transpose=True,
                group_size=64, bits=4, out=None):
     """MLX gather_qmm, transpose=True: out[i] = x[xi] . dequant(w[rhs[i]])^T, shape

@@ -75,6 +75,13 @@ def test_empty_shapes_are_noops(nqlib):
     assert nqlib.nq_moe_route(None, 0, 128, 8, None, None, None) == 0
 
 
+def test_launch_count_query_validates(nqlib):
+    assert nqlib.nq_quantized_matmul_launches(0, 4096, 4096, 4, 64) == 0
+    assert nqlib.nq_quantized_matmul_launches(8, 0, 4096, 4, 64) == 0
+    assert nqlib.nq_quantized_matmul_launches(8, 64, 96, 4, 64) == 1  # K % group_size
+    assert nqlib.nq_quantized_matmul_launches(-1, 64, 128, 4, 64) == 1
+
+
 def test_gather_rejects_bad_batch(nqlib):
     rc = nqlib.nq_gather_qmm(DUMMY, 3, 1, None, DUMMY, 8, DUMMY, DUMMY, DUMMY, 16, 32, 64, 4, 32,
                              DUMMY, None)

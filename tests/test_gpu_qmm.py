@@ -44,6 +44,28 @@ def test_gemv_path_ragged(oracle, nqlib, N, K):
     run_case(oracle, 1, N, K, 4, 32, seed=N)
 
 
+@pytest.mark.parametrize("bits,gs,M,N,K", [(8, 32, 1, 100, 8192), (4, 64, 4, 48, 4096),
+                                           (4, 128, 2, 33, 6144), (4, 32, 8, 24, 2048),
+                                           (8, 64, 3, 40, 3072)])
+def test_gemv_long_k_small_m(oracle, nqlib, bits, gs, M, N, K):
+    """Decode shapes whose weight k-blocks outnumber the per-CTA ring (the ring
+    wraps), scale spans that end inside a 64-group box, and up to 8 tokens."""
+    run_case(oracle, M, N, K, bits, gs, seed=K + M)
+
+
+def test_launch_count_query(nqlib):
+    """The tail split is a second kernel only where a grid's last wave would run
+    nearly empty (148 SMs): 2048 x 14336 has 896 = 6 x 148 + 8 tiles."""
+    import neurons_b200 as nb
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert nb.quantized_matmul_launches(1, 4096, 4096) == 1          # GEMV
+    tiles = (14336 // 128) * (2048 // 256)
+    assert nb.quantized_matmul_launches(2048, 14336, 4096) == (2 if 0 < tiles % sms <= sms // 2
+                                                               else 1)
+    assert nb.quantized_matmul_launches(256, 4096, 4096) == 1        # all tiles split: tail only
+    assert nb.quantized_matmul_launches(2048, 4096, 4096) in (1, 2)
+
+
 @pytest.mark.parametrize("M", [33, 64, 65, 100, 128, 129, 200, 256, 257, 512])
 def test_tc_path_m_sweep(oracle, nqlib, M):
     run_case(oracle, M, 256, 512, 4, 64, seed=M)
@@ -58,6 +80,27 @@ def test_tc_path_bits_groups(oracle, nqlib, bits, gs):
 @pytest.mark.parametrize("N,K", [(1, 64), (130, 96), (200, 160), (128, 4096), (257, 2048)])
 def test_tc_path_ragged(oracle, nqlib, N, K):
     run_case(oracle, 96, N, K, 4, 32, seed=N + K)
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 512, 512), (2048, 1280, 1024), (200, 640, 2048)])
+def test_tc_back_to_back_launches_are_ordered(oracle, nqlib, M, N, K):
+    """y2 = W2 y1 right after y1 = W1 x on the stream: the second GEMM reads
+    what the first one's tile stores (and split-tail clusters) wrote."""
+    import neurons_b200 as nb
+    rng = np.random.default_rng(M + N)
+    w1 = oracle.quantize(weights(rng, N, K), 4, 64, 0)
+    w2 = oracle.quantize(weights(rng, K, N), 4, 64, 0)
+    x = acts(rng, M, K)
+    d1 = [dev_u32(w1[0]), dev_bf16(w1[1]), dev_bf16(w1[2])]
+    d2 = [dev_u32(w2[0]), dev_bf16(w2[1]), dev_bf16(w2[2])]
+    xd = dev_bf16(x)
+    for _ in range(3):
+        y1 = nb.quantized_matmul(xd, *d1, True, 64, 4)
+        y2 = nb.quantized_matmul(y1, *d2, True, 64, 4)
+    torch.cuda.synchronize()
+    assert nb.take_device_error() == 0
+    assert_close(host_u16(y1), oracle.qmm(x, *w1, 4, 64), "tc chained stage 1")
+    assert_close(host_u16(y2), oracle.qmm(host_u16(y1), *w2, 4, 64), "tc chained stage 2")
 
 
 def test_golden_seeded_qmm(nqlib):
