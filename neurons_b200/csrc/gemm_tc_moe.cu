@@ -39,6 +39,7 @@ constexpr int kStageArrivals = 8;  // dequant warps working on one stage
 constexpr int kProducerWarp = 16;
 constexpr int kMmaWarp = 17;
 constexpr int kThreads = 576;
+constexpr int kXchgBytes = 8 * 2 * 16 * 32 * 4;  // up epilogue: 8 warp pairs x 2 buffers
 
 template <int BITS>
 struct MoeCfg {
@@ -52,7 +53,7 @@ struct MoeCfg {
     static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256 + kMaxTok * 4;
     static_assert(kSmemBytes <= 232448, "shared memory budget");
     // epilogue exchange of the up kernel: 8 warp pairs x 2 buffers x [16][32] fp32
-    static_assert(8 * 2 * 16 * 32 * 4 <= kStages * kXStageBytes, "exchange buffer");
+    static_assert(kXchgBytes + kMaxTok * 128 <= kStages * kXStageBytes, "exchange + h staging");
 };
 
 struct MoeTcParams {
@@ -65,6 +66,7 @@ struct MoeTcParams {
     const int32_t *rows;              // down: pair of grouped row
     void *y;                          // up: h [P, N] bf16 (grouped rows); down: d [P, N] fp32
     int64_t y_ld;
+    int h_map;                        // up: h leaves through tmap_h (16-row TMA stores)
     unsigned int *err;
 };
 
@@ -74,7 +76,8 @@ template <int BITS, bool UP>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_moe_kernel(const __grid_constant__ CUtensorMap tmap_w1,
                   const __grid_constant__ CUtensorMap tmap_w2,
-                  const __grid_constant__ CUtensorMap tmap_x, const MoeTcParams prm) {
+                  const __grid_constant__ CUtensorMap tmap_x,
+                  const __grid_constant__ CUtensorMap tmap_h, const MoeTcParams prm) {
     using Cfg = MoeCfg<BITS>;
     constexpr int S = Cfg::kStages;
     if ((int)blockIdx.y >= *prm.n_tiles) return;  // uniform: beyond the tile list
@@ -249,16 +252,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------ epilogue
         const bool ok = mbar_wait_or_abort(accfull, 0, abort, prm.err) && !*abort;
         if (ok) tc_fence_after();
-        const int part = warp >> 2;  // token columns [64 part, 64 part + 64)
+        const int part = warp >> 2;  // 16-token chunks part, part + 4, ...
         if constexpr (UP) {
             // Warp pair (q, q + 2) of a part: the up warp hands its 16 columns
             // to the gate warp through shared memory (the stages are idle now).
+            // 16-token chunks are dealt round-robin to the four parts.  With a
+            // whole 64-column block and aligned rows, h is staged as [token][64]
+            // bf16 and leaves through 16-row TMA stores (a box never reaches past
+            // the tile's own rows) plus 16-byte stores for the last count % 16.
             const bool is_up = q >= 2;
             const int pair_id = part * 2 + (q & 1);
             float *xbuf = reinterpret_cast<float *>(xs) + pair_id * (2 * 16 * 32);
+            uint8_t *hstage = xs + kXchgBytes;
             uint16_t *hout = static_cast<uint16_t *>(prm.y);
+            const bool staged = prm.h_map && nbase + kBlockW / 2 <= prm.N;
+            const int nchunks = (cnt + 15) >> 4;
             int it = 0;
-            for (int c0 = part * 64; c0 < part * 64 + 64 && c0 < cnt; c0 += 16, ++it) {
+            for (int ch = part; ch < nchunks; ch += 4, ++it) {
+                const int c0 = ch * 16;
                 uint32_t acc[16];
                 if (ok) {
                     tmem_ld_32x32b_x16(tmem_base + t_lane + (uint32_t)c0, acc);
@@ -275,17 +286,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 16; ++j) {
                         const int col = c0 + j;
                         if (col < cnt) {
-                            const float u = buf[j * 32 + lane];
-                            const float hv = silu_f32(__uint_as_float(acc[j])) * u;
-                            hout[(int64_t)(g0 + col) * prm.y_ld + nrow] = f32_to_bf16(hv);
+                            const uint16_t hv =
+                                f32_to_bf16(silu_f32(__uint_as_float(acc[j])) * buf[j * 32 + lane]);
+                            if (staged)
+                                *reinterpret_cast<uint16_t *>(hstage + col * 128 + r * 2) = hv;
+                            else
+                                hout[(int64_t)(g0 + col) * prm.y_ld + nrow] = hv;
                         }
                     }
+                }
+            }
+            if (staged) {
+                fence_proxy_async_smem();
+                bar_sync(9, 16 * 32);
+                if (ok) {
+                    const int groups = cnt >> 4;
+                    if (threadIdx.x == 0) {
+                        for (int gi = 0; gi < groups; ++gi)
+                            tma_store_2d(&tmap_h, hstage + gi * 16 * 128, (int32_t)nbase,
+                                         (int32_t)(g0 + gi * 16));
+                        bulk_commit_group();
+                    }
+                    const int rest0 = groups * 16;
+                    for (int v = threadIdx.x; v < (cnt - rest0) * 8; v += 16 * 32) {
+                        const int col = rest0 + (v >> 3), ck = v & 7;
+                        *reinterpret_cast<uint4 *>(hout + (int64_t)(g0 + col) * prm.y_ld + nbase +
+                                                   ck * 8) =
+                            *reinterpret_cast<const uint4 *>(hstage + col * 128 + ck * 16);
+                    }
+                    if (threadIdx.x == 0) bulk_wait_group_read0();
                 }
             }
         } else {
             float *dout = static_cast<float *>(prm.y);
             if (ok) {
-                for (int c0 = part * 64; c0 < part * 64 + 64 && c0 < cnt; c0 += 16) {
+                const int nchunks = (cnt + 15) >> 4;
+                for (int ch = part; ch < nchunks; ch += 4) {
+                    const int c0 = ch * 16;
                     uint32_t acc[16];
                     tmem_ld_32x32b_x16(tmem_base + t_lane + (uint32_t)c0, acc);
                     tmem_ld_wait();
@@ -335,7 +372,15 @@ cudaError_t launch_cfg(const TcMoeArgs &a, cudaStream_t stream) {
                      (uint64_t)a.x_rows_total, (uint64_t)a.x_ld * 2, kBlockK, kMaxTok,
                      CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
+    // up: h [P, N] bf16 through 16-row TMA stores when its rows are 16-byte aligned
+    CUtensorMap mh = mx;
+    const bool h_map = UP && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.y_ld % 8 == 0 &&
+                       make_map_2d(&mh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.y, (uint64_t)a.N,
+                                   (uint64_t)a.x_rows_total, (uint64_t)a.y_ld * 2, kBlockW / 2, 16,
+                                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!h_map) mh = mx;  // unused
     MoeTcParams prm;
+    prm.h_map = h_map ? 1 : 0;
     prm.N = a.N;
     prm.K = a.K;
     prm.G = a.K / a.gs;
@@ -356,7 +401,7 @@ cudaError_t launch_cfg(const TcMoeArgs &a, cudaStream_t stream) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)((a.N + wbox_rows - 1) / wbox_rows), (unsigned)a.max_tiles, 1);
-    kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(m1, m2, mx, prm);
+    kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(m1, m2, mx, mh, prm);
     return cudaGetLastError();
 }
 
