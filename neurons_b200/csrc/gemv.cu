@@ -535,7 +535,10 @@ __host__ __device__ inline TStageLayout tstage_layout(int bits, int nacc, int ro
     return L;
 }
 
-__host__ __device__ constexpr int tstages(int rt) { return rt == 2 ? 3 : 4; }
+// Ring depth: 3 stages for 32-row warps and for the gate/up pair (their
+// stages are twice as large), 4 otherwise -- sized so that the 128-row and
+// paired kernels fit three CTAs per SM.
+__host__ __device__ constexpr int tstages(int rt, bool dual) { return rt == 2 || dual ? 3 : 4; }
 
 __device__ __forceinline__ bool tma_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
                                          unsigned int *err) {
@@ -668,7 +671,7 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
                                                         const GemvParams prm) {
     constexpr int NACC = DUAL ? 2 : 1;
     constexpr int kRows = kTConsumers * 16 * RT;  // weight rows per CTA
-    constexpr int kStages = tstages(RT);
+    constexpr int kStages = tstages(RT, DUAL);
     constexpr int kCodesPerStage = kTStageWords * 32 / BITS;
     constexpr int kCodesPerKb = 16 * 32 / BITS;
     constexpr int kCodesPerLane = 4 * 32 / BITS;
@@ -966,7 +969,9 @@ cudaError_t launch_tma_variant(const CUtensorMap &m1, const CUtensorMap &m2,
     constexpr int NACC = DUAL ? 2 : 1;
     constexpr int kRows = kTConsumers * 16 * RT;
     const TStageLayout L = tstage_layout(BITS, NACC, kRows, prm.mx, 1 << prm.gs_shift);
-    const int smem = tstages(RT) * L.bytes + 1024 + 128 + kTConsumers * RT * NACC * NT * 4 * 32 * 4;
+    // the K-slice partial sums are only exchanged inside a cluster
+    const int red_bytes = cluster > 1 ? kTConsumers * RT * NACC * NT * 4 * 32 * 4 : 0;
+    const int smem = tstages(RT, DUAL) * L.bytes + 1024 + 128 + red_bytes;
     auto kern = qgemv_tma_kernel<BITS, NT, RT, DUAL>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
