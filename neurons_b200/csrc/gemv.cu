@@ -764,6 +764,10 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
                          L.s_row_bytes);
             }
         };
+        // The activation row of token tk of the current pass, held by lane tk
+        // (mx <= 32): looked up once per pass, not once per stage.
+        int cached_pass = -1;
+        int64_t lane_row = 0;
         auto issue_acts = [&](int t) {
             const int s = t % kStages;
             uint8_t *st = smem + s * L.bytes;
@@ -771,14 +775,21 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
             const int stage = st_lo + (t - pass * nst);
             const int m0 = pass * mx;
             const int code0 = stage * kCodesPerStage;
+            if (pass != cached_pass) {  // uniform over the warp
+                const int m = m0 + lane;
+                lane_row = 0;
+                if (lane < mx && m < Mp)
+                    lane_row = prm.x_rows ? (int64_t)prm.x_rows[off + m]
+                                          : (prm.x_from_offset ? (int64_t)off + m
+                                                               : (int64_t)xi * prm.M + m);
+                cached_pass = pass;
+            }
             for (int tk = 0; tk < mx; ++tk) {
                 const int m = m0 + tk;
                 const uint16_t *src = prm.x;
                 int nbytes = 0;
+                const int64_t row = __shfl_sync(0xffffffffu, lane_row, tk);
                 if (m < Mp) {
-                    const int64_t row = prm.x_rows ? (int64_t)prm.x_rows[off + m]
-                                        : (prm.x_from_offset ? (int64_t)off + m
-                                                             : (int64_t)xi * prm.M + m);
                     src = prm.x + row * prm.x_ld + code0;
                     nbytes = 16;
                 }
@@ -801,7 +812,8 @@ __global__ void __launch_bounds__(160) qgemv_tma_kernel(const __grid_constant__ 
             for (t = pre; t < total; ++t) {
                 const int s = t % kStages;
                 const uint32_t ph = (uint32_t)(t / kStages) & 1u;
-                if (!tma_wait(&empty[s], ph ^ 1u, abort, prm.err)) break;
+                // the whole warp stops together (issue_acts shuffles across it)
+                if (!__all_sync(0xffffffffu, tma_wait(&empty[s], ph ^ 1u, abort, prm.err))) break;
                 issue_weights(t);
                 issue_acts(t);
             }
