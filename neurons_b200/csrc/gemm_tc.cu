@@ -83,9 +83,10 @@ struct TcParams {
     PushDev push;  // tensor-parallel fan-out of the stores (n == 0: local only)
 };
 
+// Every thread of every CTA of the cluster.  The non-.aligned form: the
+// producer and MMA warps arrive right after loops that only one lane ran.
 __device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                     : "memory");
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
 // 16 bytes of CTA `rank`'s shared memory at the offset of `local` in this CTA
