@@ -4,7 +4,11 @@
 // creates the backend's stream; cleanup() releases it (mx::clear_cache there).
 #include "cuda_backend.h"
 
+#include <cublas_v2.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+
+#include <mutex>
 
 #include "nq.h"
 
@@ -124,6 +128,83 @@ BackendType BackendFactory::best_available_backend() {
 
 // ----------------------------------------------------------------- ops
 
+namespace {
+
+// cuBLAS for the dense (unquantized) linear only, loaded on first use so that
+// libnq.so itself depends on nothing but the CUDA runtime.
+struct CublasApi {
+    using CreateFn = cublasStatus_t (*)(cublasHandle_t *);
+    using SetStreamFn = cublasStatus_t (*)(cublasHandle_t, cudaStream_t);
+    using GemmExFn = cublasStatus_t (*)(cublasHandle_t, cublasOperation_t, cublasOperation_t, int,
+                                        int, int, const void *, const void *, cudaDataType, int,
+                                        const void *, cudaDataType, int, const void *, void *,
+                                        cudaDataType, int, cublasComputeType_t, cublasGemmAlgo_t);
+    CreateFn create = nullptr;
+    SetStreamFn set_stream = nullptr;
+    GemmExFn gemm = nullptr;
+    std::mutex mu;                    // a handle's stream binding + launch
+    cublasHandle_t handle[64] = {};   // one per device
+};
+
+CublasApi *cublas_api() {
+    static CublasApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libcublas.so.12", RTLD_NOW | RTLD_LOCAL);
+        if (!h) h = dlopen("libcublas.so", RTLD_NOW | RTLD_LOCAL);
+        if (!h) return;
+        api.create = reinterpret_cast<CublasApi::CreateFn>(dlsym(h, "cublasCreate_v2"));
+        api.set_stream = reinterpret_cast<CublasApi::SetStreamFn>(dlsym(h, "cublasSetStream_v2"));
+        api.gemm = reinterpret_cast<CublasApi::GemmExFn>(dlsym(h, "cublasGemmEx"));
+    });
+    return api.create && api.set_stream && api.gemm ? &api : nullptr;
+}
+
+// y[M, N] = x[M, K] . w[N, K]^T in bf16 with fp32 accumulation, the
+// `mx::matmul(x, swapaxes(w, 0, 1))` of mlx_ops::lin for weights without scales
+// (compute/src/compute/model/mlx_ops.h:40).
+Result<void> dense_lin(const DeviceTensor &x, const std::string &key, const DeviceTensor &w,
+                       DeviceTensor &y, void *stream) {
+    if (w.dtype != DType::BF16 || x.dtype != DType::BF16 || y.dtype != DType::BF16)
+        return std::unexpected(Error{ErrorCode::InvalidModel,
+                                     key + ": an unquantized linear needs bf16 weight, input and output"});
+    const int64_t K = x.dim(-1);
+    const int64_t M = K ? x.numel() / K : 0;
+    const int64_t N = w.dim(0);
+    if (w.shape.size() != 2 || w.dim(1) != K)
+        return std::unexpected(Error{ErrorCode::InvalidInput, key + ": x/W inner dimension mismatch"});
+    if (y.numel() != M * N)
+        return std::unexpected(Error{ErrorCode::InvalidInput, key + ": output has the wrong size"});
+    if (M == 0 || N == 0) return {};
+    if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+        return std::unexpected(Error{ErrorCode::InvalidInput, key + ": shape too large"});
+    CublasApi *api = cublas_api();
+    if (!api)
+        return std::unexpected(Error{ErrorCode::BackendNotAvailable,
+                                     key + ": an unquantized linear needs cuBLAS (libcublas.so.12)"});
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return std::unexpected(Error{ErrorCode::BackendNotAvailable, key + ": no CUDA device"});
+    }
+    std::lock_guard<std::mutex> lk(api->mu);
+    if (!api->handle[dev] && api->create(&api->handle[dev]) != CUBLAS_STATUS_SUCCESS) {
+        api->handle[dev] = nullptr;
+        return std::unexpected(Error{ErrorCode::ComputeError, key + ": cublasCreate failed"});
+    }
+    cublasHandle_t h = api->handle[dev];
+    const float alpha = 1.0f, beta = 0.0f;
+    // column-major view: y^T [N, M] = (w^T)^T [N, K] . x^T [K, M]
+    if (api->set_stream(h, static_cast<cudaStream_t>(stream)) != CUBLAS_STATUS_SUCCESS ||
+        api->gemm(h, CUBLAS_OP_T, CUBLAS_OP_N, (int)N, (int)M, (int)K, &alpha, w.data, CUDA_R_16BF,
+                  (int)K, x.data, CUDA_R_16BF, (int)K, &beta, y.data, CUDA_R_16BF, (int)N,
+                  CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
+        return std::unexpected(Error{ErrorCode::ComputeError, key + ": dense bf16 GEMM failed"});
+    return {};
+}
+
+}  // namespace
+
 namespace cuda_ops {
 
 int bits(const DeviceTensor &w, const DeviceTensor &s, int gs) {
@@ -137,10 +218,7 @@ Result<void> lin(const DeviceTensor &x, const std::string &key, const WeightMap 
         return std::unexpected(Error{ErrorCode::InvalidModel, "missing weight " + key + ".weight"});
     const DeviceTensor &w = wit->second;
     auto sit = wm.find(key + ".scales");
-    if (sit == wm.end())
-        return std::unexpected(Error{ErrorCode::InvalidModel,
-                                     key + ": unquantized (dense) weights are not served by the "
-                                           "quantized-matmul backend"});
+    if (sit == wm.end()) return dense_lin(x, key, w, y, stream);  // unquantized layer
     const DeviceTensor &s = sit->second;
     auto bit = wm.find(key + ".biases");
     const DeviceTensor *b = bit == wm.end() ? nullptr : &bit->second;

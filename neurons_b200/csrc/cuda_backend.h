@@ -90,9 +90,11 @@ namespace cuda_ops {
 // mlx_ops::bits: bits = round(32 * (w.shape[-1] / s.shape[-1]) / gs), 4 if not positive.
 int bits(const DeviceTensor &w, const DeviceTensor &s, int gs);
 
-// mlx_ops::lin: y = x . dequant(W)^T through nq_quantized_matmul when
-// "<key>.scales" exists (biases from "<key>.biases").  Dense (unquantized)
-// weights are outside this backend: ErrorCode::InvalidModel.
+// mlx_ops::lin (compute/src/compute/model/mlx_ops.h:28-42): y = x . dequant(W)^T
+// through nq_quantized_matmul when "<key>.scales" exists (biases from
+// "<key>.biases"); otherwise y = x . W^T for a bf16 W, as the reference's
+// mx::matmul fallback, through cuBLAS (loaded on first use; without it:
+// ErrorCode::BackendNotAvailable).
 Result<void> lin(const DeviceTensor &x, const std::string &key, const WeightMap &wm, int gs,
                  DeviceTensor &y, void *stream);
 

@@ -146,3 +146,23 @@ def test_lin_over_loaded_checkpoint(checker, oracle, tmp_path, bits, gs):
     assert out[-1][:2] == ["lin", "ok"], out
     y = np.fromfile(tmp_path / "y.bin", np.uint16).reshape(M, N)
     assert_close(y, oracle.qmm(x, wq, s, b, bits, gs), f"lin {bits}-bit g{gs}")
+
+
+@pytest.mark.gpu
+def test_lin_dense_weight_falls_back_to_matmul(checker, oracle, tmp_path):
+    """A layer stored without scales (an unquantized projection) goes through
+    mlx_ops::lin's plain matmul branch (mlx_ops.h:40): y = x . W^T, bf16 in,
+    fp32 accumulation, bf16 out."""
+    rng = np.random.default_rng(11)
+    N, K, M = 96, 256, 5
+    w = oracle.f32_to_bf16(weights(rng, N, K))
+    key = "lm_head"
+    write_safetensors(tmp_path / "model.safetensors", {key + ".weight": ("BF16", w)})
+    (tmp_path / "config.json").write_text(json.dumps({"model_type": "llama"}))
+    x = acts(rng, M, K)
+    x.tofile(tmp_path / "x.bin")
+    out = checker("lin", tmp_path, key, tmp_path / "x.bin", M, K, tmp_path / "y.bin")
+    assert out[-1][:2] == ["lin", "ok"], out
+    y = np.fromfile(tmp_path / "y.bin", np.uint16).reshape(M, N)
+    ref = oracle.bf16_to_f32(x).astype(np.float64) @ oracle.bf16_to_f32(w).astype(np.float64).T
+    assert_close(y, oracle.f32_to_bf16(ref.astype(np.float32)), "dense lin")
