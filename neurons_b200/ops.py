@@ -143,7 +143,9 @@ def lin(x, key, wm, gs, out=None):
     w = wm[key + ".weight"]
     s = wm.get(key + ".scales")
     if s is None:
-        raise NQError(2, f"{key}: dense (unquantized) weights are not served by this backend")
+        # the C++ cuda_ops::lin serves unquantized layers through cuBLAS; this
+        # mirror covers the quantized entry points only
+        raise NQError(2, f"{key}: unquantized weights: use cuda_ops::lin (C++) for them")
     b = wm.get(key + ".biases")
     return quantized_matmul(x, w, s, b, True, gs, bits(w, s, gs), out=out)
 
