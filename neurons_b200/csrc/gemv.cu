@@ -1063,9 +1063,15 @@ cudaError_t launch_gemv(const GemvProblems &q, cudaStream_t stream) {
     const int size_m = q.tile_m > 0 ? std::min(q.tile_m, max_m) : max_m;
     const int nt = size_m <= 8 ? 1 : (size_m <= 16 ? 2 : 4);
 
-    // ---- asynchronously fed kernel (the default)
+    // ---- asynchronously fed kernel (the default).  Its scale/bias spans are
+    // 4-16 byte cp.async copies: pointers aligned to less than 16 bytes (a
+    // legal bf16 sub-view) take the register-fed kernel, which reads them by
+    // element.
+    const uintptr_t sb_bits = reinterpret_cast<uintptr_t>(q.s) | reinterpret_cast<uintptr_t>(q.b) |
+                              reinterpret_cast<uintptr_t>(prm.s2) |
+                              reinterpret_cast<uintptr_t>(prm.b2);
     if (q.K % 256 == 0 && !(q.bits == 8 && q.gs == 128) &&
-        (reinterpret_cast<uintptr_t>(q.x) & 15) == 0 && q.x_ld % 8 == 0) {
+        (reinterpret_cast<uintptr_t>(q.x) & 15) == 0 && q.x_ld % 8 == 0 && (sb_bits & 15) == 0) {
         // 32 rows per consumer warp (shares the activation work between two
         // row tiles) unless that leaves fewer than ~2 CTAs per SM
         const int rt_t = (!dual && nt == 1 && ((q.N + 127) / 128) * (int64_t)q.P >= 2 * sm_count())

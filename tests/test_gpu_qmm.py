@@ -53,6 +53,29 @@ def test_gemv_long_k_small_m(oracle, nqlib, bits, gs, M, N, K):
     run_case(oracle, M, N, K, bits, gs, seed=K + M)
 
 
+@pytest.mark.parametrize("bits,gs", [(4, 32), (4, 64), (8, 32)])
+def test_gemv_scales_at_any_bf16_alignment(oracle, nqlib, bits, gs):
+    """Scales and biases handed over as views that start one bf16 element into
+    their buffers (2-byte aligned, as a slice of a larger tensor can be): the
+    result matches the oracle as with aligned buffers."""
+    import neurons_b200 as nb
+    rng = np.random.default_rng(bits * 7 + gs)
+    M, N, K = 3, 64, 1024
+    wq, s, b = oracle.quantize(weights(rng, N, K), bits, gs, 0)
+    x = acts(rng, M, K)
+    views = []
+    for t in (s, b):
+        buf = torch.empty(t.size + 1, dtype=torch.bfloat16, device="cuda")
+        v = buf[1:].view(t.shape)
+        v.copy_(dev_bf16(t))
+        assert v.data_ptr() % 16 == 2
+        views.append(v)
+    y = nb.quantized_matmul(dev_bf16(x), dev_u32(wq), views[0], views[1], True, gs, bits)
+    torch.cuda.synchronize()
+    assert nb.take_device_error() == 0
+    assert_close(host_u16(y), oracle.qmm(x, wq, s, b, bits, gs), f"offset scales b{bits} g{gs}")
+
+
 def test_launch_count_query(nqlib):
     """The tail split is a second kernel only where a grid's last wave would run
     nearly empty (148 SMs): 2048 x 14336 has 896 = 6 x 148 + 8 tiles."""
