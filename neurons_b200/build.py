@@ -25,8 +25,11 @@ INCLUDE = os.path.join(ROOT, "include")
 
 CU_SOURCES = ["abi.cu", "quant.cu", "gemv.cu", "gemm_tc.cu", "gemm_tc_moe.cu", "moe.cu"]
 CPP_SOURCES = ["cuda_backend.cpp", "model_loader.cpp"]
-HEADERS = ["nq_common.cuh", "nq_internal.h", "cuda_backend.h", "compute_types.h",
-           "model_loader.h"]
+HEADERS = ["nq_common.cuh", "nq_internal.h", "cuda_backend.h", "iface/compute_types.h",
+           "iface/compute_backend.h", "model_loader.h"]
+# The reference's interface headers, restated, for building libnq on its own
+# (inside the reference tree its own core/ headers take their place).
+IFACE = os.path.join(CSRC, "iface")
 
 DIST_LIB = os.path.join(HERE, "libnq_dist.so")
 DIST_SOURCE = "dist.cu"
@@ -72,6 +75,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         objs.append(o)
         if force or _newer(o, [s] + hdrs):
             subprocess.run(["g++", "-O2", "-std=c++23", "-fPIC", "-Wall", "-I" + INCLUDE,
+                            "-I" + IFACE,
                             "-I" + os.path.join(CUDA_HOME, "include"), "-c", s, "-o", o],
                            check=True)
     if force or _newer(LIB, objs):

@@ -1,4 +1,5 @@
-// cuda_backend.cpp -- CUDABackend, BackendFactory and the cuda_ops helpers.
+// cuda_backend.cpp -- CUDABackend and the cuda_ops helpers.  The factory and
+// the manager stay in the host application (see cuda_backend.h).
 // Lifecycle mirrors MLXBackend (compute/src/compute/backends/mlx/mlx_backend.cpp:30-50):
 // initialize() selects the device (mx::set_default_device(gpu) there) and
 // creates the backend's stream; cleanup() releases it (mx::clear_cache there).
@@ -86,44 +87,6 @@ Result<void> CUDABackend::synchronize() const {
         return std::unexpected(Error{ErrorCode::ComputeError,
                                      "kernel reported device error " + std::to_string(err)});
     return {};
-}
-
-// --------------------------------------------------------- BackendFactory
-// Same shape as compute/src/compute/core/compute_backend.cpp:9-32, with the
-// CUDA case added; Auto picks CUDA when an sm_100 device is present.
-
-Result<std::unique_ptr<ComputeBackend>> BackendFactory::create(BackendType type) {
-    switch (type) {
-        case BackendType::Auto:
-        case BackendType::CUDA: {
-            auto be = std::make_unique<CUDABackend>(0);
-            if (!be->is_available())
-                return std::unexpected(Error{ErrorCode::BackendNotAvailable, "CUDA not available"});
-            auto r = be->initialize();
-            if (!r)
-                return std::unexpected(Error{ErrorCode::BackendNotAvailable,
-                                             "CUDA backend failed to initialize: " +
-                                                 r.error().message});
-            return std::unique_ptr<ComputeBackend>(std::move(be));
-        }
-        case BackendType::MLX:
-            return std::unexpected(Error{ErrorCode::BackendNotAvailable,
-                                         "MLX backend only available on Apple Silicon with MLX "
-                                         "enabled"});
-        default:
-            return std::unexpected(Error{ErrorCode::UnknownError, "Unknown backend type"});
-    }
-}
-
-std::vector<BackendType> BackendFactory::available_backends() {
-    std::vector<BackendType> v;
-    if (CUDABackend(0).is_available()) v.push_back(BackendType::CUDA);
-    return v;
-}
-
-BackendType BackendFactory::best_available_backend() {
-    auto v = available_backends();
-    return v.empty() ? BackendType::Auto : v[0];
 }
 
 // ----------------------------------------------------------------- ops
@@ -230,6 +193,8 @@ Result<void> lin(const DeviceTensor &x, const std::string &key, const WeightMap 
                                            "values are bf16(bf16(s*q) + b))"});
     const int nb = bits(w, s, gs);
     const int64_t K = x.dim(-1);
+    if (K <= 0)
+        return std::unexpected(Error{ErrorCode::InvalidInput, key + ": x has an empty last dimension"});
     const int64_t M = x.numel() / K;
     const int64_t N = w.dim(0);
     if (w.dim(-1) * 32 / nb != K)

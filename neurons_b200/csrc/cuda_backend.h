@@ -1,7 +1,9 @@
 // cuda_backend.h -- the CUDA backend behind neurons' ComputeBackend interface
 // and the quantized-linear helpers the models call.
 //
-//   ComputeBackend / BackendFactory   mirror compute/src/compute/core/compute_backend.h:12-32
+//   ComputeBackend                    compute/src/compute/core/compute_backend.h:12-24, included
+//                                     from "compute_backend.h" (the reference's own header
+//                                     inside its tree; iface/ when libnq is built alone)
 //   CUDABackend                       takes the place of MLXBackend
 //                                     (compute/src/compute/backends/mlx/mlx_backend.h:11-25)
 //   cuda_ops::bits / cuda_ops::lin    mirror mlx_ops::bits / mlx_ops::lin
@@ -24,26 +26,9 @@
 #include <unordered_map>
 #include <vector>
 
-#include "compute_types.h"
+#include "compute_backend.h"
 
 namespace compute {
-
-class ComputeBackend {
-public:
-    virtual ~ComputeBackend() = default;
-    virtual BackendType type() const = 0;
-    virtual std::string name() const = 0;
-    virtual bool is_available() const = 0;
-    virtual Result<void> initialize() = 0;
-    virtual void cleanup() = 0;
-};
-
-class BackendFactory {
-public:
-    static Result<std::unique_ptr<ComputeBackend>> create(BackendType type);
-    static std::vector<BackendType> available_backends();
-    static BackendType best_available_backend();
-};
 
 enum class DType { BF16, F32, U32, I32, F16 };
 
@@ -63,6 +48,9 @@ struct DeviceTensor {
 
 using WeightMap = std::unordered_map<std::string, DeviceTensor>;
 
+// The CUDA backend.  BackendFactory / BackendManager are not defined in
+// libnq: the host's factory (compute_backend.cpp) gains a CUDA case that
+// constructs this class.
 class CUDABackend : public ComputeBackend {
 public:
     explicit CUDABackend(int device = 0);

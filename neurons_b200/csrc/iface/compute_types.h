@@ -1,7 +1,9 @@
 // compute_types.h -- error and backend types of the compute library, kept
 // interface-compatible with compute/src/compute/core/compute_types.h:9-32 so
 // that code written against the reference's Result<T>/ErrorCode compiles
-// unchanged; BackendType gains the CUDA enumerator.
+// unchanged; BackendType gains the CUDA enumerator, placed between MLX and
+// Auto (the reference's header takes the same one-line edit when libnq is
+// linked into it).  Used only when libnq is built on its own.
 #pragma once
 
 #include <expected>

@@ -1,10 +1,11 @@
 // backend_check.cpp -- exercises the C++ layer of libnq the way a reference
-// model would: BackendFactory / CUDABackend (compute_backend.cpp:9-32),
+// model would: CUDABackend's lifecycle (the MLXBackend counterpart,
+// mlx_backend.cpp:30-50),
 // cuda_ops::bits and cuda_ops::lin (mlx_ops.h:20-42), and the checkpoint
 // loader (model_loader.cpp:17-58, model_config.cpp:177-193).  Driven by
 // tests/test_cpp_backend.py; prints one "key value" line per result.
 //
-//   backend_check factory
+//   backend_check backend
 //   backend_check bits
 //   backend_check config <model_dir>
 //   backend_check header <file.safetensors>
@@ -36,13 +37,19 @@ static const char *code_name(ErrorCode c) {
 int main(int argc, char **argv) {
     if (argc < 2) return 2;
     const std::string cmd = argv[1];
-    if (cmd == "factory") {
-        auto be = BackendFactory::create(BackendType::CUDA);
-        std::printf("create_cuda %s\n", be ? "ok" : code_name(be.error().code));
-        auto mlx = BackendFactory::create(BackendType::MLX);
-        std::printf("create_mlx %s\n", mlx ? "ok" : code_name(mlx.error().code));
-        std::printf("available %zu\n", BackendFactory::available_backends().size());
-        if (be) std::printf("name %s\n", (*be)->name().c_str());
+    if (cmd == "backend") {
+        CUDABackend be(0);
+        std::printf("available %d\n", be.is_available() ? 1 : 0);
+        auto r = be.initialize();
+        std::printf("initialize %s\n", r ? "ok" : code_name(r.error().code));
+        std::printf("type_cuda %d\n", be.type() == BackendType::CUDA ? 1 : 0);
+        if (r) {
+            std::printf("stream %d\n", be.stream() != nullptr ? 1 : 0);
+            auto s = be.synchronize();
+            std::printf("synchronize %s\n", s ? "ok" : code_name(s.error().code));
+            be.cleanup();
+            std::printf("cleanup ok\n");
+        }
         return 0;
     }
     if (cmd == "bits") {

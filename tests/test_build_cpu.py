@@ -9,7 +9,8 @@ CSRC = os.path.join(ROOT, "neurons_b200", "csrc")
 
 def test_every_source_is_built():
     from neurons_b200 import build
-    files = set(os.listdir(CSRC))
+    files = {os.path.relpath(os.path.join(d, f), CSRC)
+             for d, _, fs in os.walk(CSRC) if "_build" not in d for f in fs}
     compiled = set(build.CU_SOURCES) | set(build.CPP_SOURCES) | {build.DIST_SOURCE}
     assert {f for f in files if f.endswith((".cu", ".cpp"))} == compiled
     assert {f for f in files if f.endswith((".h", ".cuh"))} == set(build.HEADERS)

@@ -1,5 +1,5 @@
 """The C++ layer of libnq, driven through tests/cpp/backend_check.cpp: the
-backend factory (compute_backend.cpp:9-32), cuda_ops::bits (mlx_ops.h:20-25),
+CUDABackend lifecycle (mlx_backend.cpp:30-50), cuda_ops::bits (mlx_ops.h:20-25),
 config.json's quantization block (model_config.cpp:177-193), the safetensors
 reader and loader (model_loader.cpp:17-58) and cuda_ops::lin over a loaded
 checkpoint (mlx_ops.h:28-42), the last one against the oracle on a GPU."""
@@ -21,6 +21,7 @@ def checker(nqlib, tmp_path_factory):
     exe = str(tmp_path_factory.mktemp("cpp") / "backend_check")
     lib_dir = os.path.join(ROOT, "neurons_b200")
     subprocess.run(["g++", "-std=c++23", "-O1", "-I" + os.path.join(lib_dir, "csrc"),
+                    "-I" + os.path.join(lib_dir, "csrc", "iface"),
                     "-I" + os.path.join(ROOT, "include"), "-I/usr/local/cuda/include",
                     os.path.join(ROOT, "tests", "cpp", "backend_check.cpp"), "-o", exe,
                     "-L" + lib_dir, "-lnq", "-L/usr/local/cuda/lib64", "-lcudart",
@@ -52,14 +53,15 @@ def write_safetensors(path, tensors, metadata=None):
             f.write(b)
 
 
-def test_factory(checker):
+def test_backend_lifecycle(checker):
     import torch
-    out = dict((r[0], r[1:]) for r in checker("factory"))
-    assert out["create_mlx"] == ["BackendNotAvailable"]
+    out = dict((r[0], r[1:]) for r in checker("backend"))
+    assert out["type_cuda"] == ["1"]
     if torch.cuda.is_available():
-        assert out["create_cuda"] == ["ok"] and int(out["available"][0]) == 1
+        assert out["available"] == ["1"] and out["initialize"] == ["ok"]
+        assert out["stream"] == ["1"] and out["synchronize"] == ["ok"] and out["cleanup"] == ["ok"]
     else:
-        assert out["create_cuda"] == ["BackendNotAvailable"] and out["available"] == ["0"]
+        assert out["available"] == ["0"] and out["initialize"] == ["BackendNotAvailable"]
 
 
 def test_bits_like_mlx_ops(checker, oracle):
