@@ -238,32 +238,66 @@ def time_device(M, N, K, steps, warmup, world, seed, clocks=None):
 
 
 def time_e2e(M, N, K, steps, warmup, world, seed):
-    """Through the public API with host buffers: pinned x -> device, qmm, y -> pinned host."""
+    """Through the public API with host buffers: every step copies its own x from
+    pinned host memory to the device, runs quantized_matmul and copies its own y
+    back to pinned host memory.  The copies are pipelined the way a serving loop
+    would run them: two device buffers for x and for y, the host->device copies
+    on one copy stream and the device->host copies on another, so step i+1's
+    input and step i-1's output cross PCIe while step i computes.  Every copy of
+    every step is inside the timed region, which ends when the last step's y
+    has reached host memory."""
     import torch
     import neurons_b200 as nb
     data = make_inputs(M, N, K, 1, seed + 1)
-    _, wq, s, b, y = data[0]
-    xh = torch.randn(M, K, generator=torch.Generator().manual_seed(seed)).to(
-        torch.bfloat16).pin_memory()
-    yh = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
-    stream = torch.cuda.current_stream()
+    _, wq, s, b, _ = data[0]
+    gen = torch.Generator().manual_seed(seed)
+    xh = [torch.randn(M, K, generator=gen).to(torch.bfloat16).pin_memory() for _ in range(2)]
+    yh = [torch.empty(M, N, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    xd = [torch.empty(M, K, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    yd = [torch.empty(M, N, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    compute = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ev = lambda: torch.cuda.Event()
+    x_ready = [ev(), ev()]     # x[j] on the device
+    x_free = [ev(), ev()]      # the GEMM that read xd[j] finished
+    y_ready = [ev(), ev()]     # the GEMM that wrote yd[j] finished
+    y_free = [ev(), ev()]      # yd[j] copied out
+    for j in range(2):
+        x_free[j].record(compute)
+        y_free[j].record(compute)
 
-    def step():
-        xd.copy_(xh, non_blocking=True)
-        nb.quantized_matmul(xd, wq, s, b, True, GS, BITS, out=y)
-        yh.copy_(y, non_blocking=True)
+    def run(n):
+        start = ev()
+        start.record(compute)  # the copy streams start after the region's start event
+        h2d.wait_event(start)
+        d2h.wait_event(start)
+        for i in range(n):
+            j = i % 2
+            h2d.wait_event(x_free[j])
+            with torch.cuda.stream(h2d):
+                xd[j].copy_(xh[j], non_blocking=True)
+            x_ready[j].record(h2d)
+            compute.wait_event(x_ready[j])
+            compute.wait_event(y_free[j])
+            nb.quantized_matmul(xd[j], wq, s, b, True, GS, BITS, out=yd[j])
+            x_free[j].record(compute)
+            y_ready[j].record(compute)
+            d2h.wait_event(y_ready[j])
+            with torch.cuda.stream(d2h):
+                yh[j].copy_(yd[j], non_blocking=True)
+            y_free[j].record(d2h)
+        done = ev()
+        done.record(d2h)
+        compute.wait_event(done)
 
-    for _ in range(warmup):
-        step()
+    run(warmup)
     torch.cuda.synchronize()
     barrier(world)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(steps):
-        step()
-    t1.record(stream)
+    t0.record(compute)
+    run(steps)
+    t1.record(compute)
     torch.cuda.synchronize()
     barrier(world)
     total = max_over_ranks(t0.elapsed_time(t1) / 1e3, world)
@@ -648,6 +682,42 @@ def cpu_baseline(M, N, K, target_s=12.0):
     return smp.result(smp.time())
 
 
+def torch_cpu_baseline(M, N, K, target_s=5.0):
+    """A second CPU figure: the whole workload as a dense bf16 matmul in torch on
+    every host thread, y = x . dequant(W)^T with the weights dequantized once
+    beforehand (by the oracle, outside the timed calls) -- what a CPU user
+    without a quantized kernel would run.  Repeated until ~target_s seconds."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    rng = np.random.default_rng(1)
+    wq, sc, bi = O.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32), BITS, GS,
+                            O.SCHEME_MINMAX)
+    wh = O.dequantize(wq, sc, bi, BITS, GS)
+    del wq, sc, bi
+    x = O.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    xt = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16)
+    wt = torch.from_numpy(wh.view(np.int16)).view(torch.bfloat16)
+    threads = os.cpu_count() or 1
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        y = xt @ wt.T  # warm-up
+        n, t = 0, time.perf_counter()
+        while True:
+            y = xt @ wt.T
+            n += 1
+            dt = time.perf_counter() - t
+            if dt >= target_s or n >= 100:
+                break
+    finally:
+        torch.set_num_threads(prev)
+    del y
+    sec = dt / n
+    return {"seconds_per_call": sec, "threads": threads, "calls": n,
+            "tflops": algo_flops(M, N, K) / sec / 1e12, "gbs": algo_bytes(M, N, K) / sec / 1e9}
+
+
 def ours(args):
     import torch
     world, rank, local = dist_setup(args.gpus)
@@ -743,6 +813,12 @@ def ours(args):
             "kind": "port",
             "sample": f"oracle qmm (fp64 accumulation) over all {M} tokens x {cb['rows']} of "
                       f"{N} weight rows, K={K}, {cb['seconds']:.1f} s"}
+        tc = torch_cpu_baseline(M, N, K)
+        line["cpu_baseline"]["torch_cpu_bf16"] = {
+            "value": tc["tflops"] if M > 1 else tc["gbs"], "unit": unit, "cores": tc["threads"],
+            "sample": f"torch bf16 x[{M},{K}] . W_hat[{N},{K}]^T on the whole workload, weights "
+                      f"dequantized beforehand, {tc['calls']} calls of "
+                      f"{tc['seconds_per_call'] * 1e3:.1f} ms"}
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

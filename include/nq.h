@@ -180,6 +180,18 @@ int nq_quantized_matmul_push(const uint16_t *x, int64_t M, const uint32_t *wq,
                              int64_t N_total, int64_t col0,
                              const nq_push_t *push, void *stream);
 
+/* Every check nq_quantized_matmul_push makes before it launches (arguments,
+ * alignment -- scales and biases included -- and whether a kernel serves the
+ * shape with the fan-out), without launching anything: NQ_SUCCESS when the
+ * call would be accepted, else the status and message it would fail with.
+ * nq_tp_quantized_matmul_fused runs it before its ready kernel, so a rejected
+ * call leaves the communicator's call count unchanged.  No counterpart in the
+ * reference (part of the fused tensor-parallel plumbing). */
+int nq_quantized_matmul_push_check(const uint16_t *x, int64_t M, const uint32_t *wq,
+                                   const uint16_t *scales, const uint16_t *biases,
+                                   int64_t N, int64_t K, int bits, int group_size,
+                                   int64_t N_total, int64_t col0, const nq_push_t *push);
+
 /* The switch step restricted to one shard of the experts, for expert
  * parallelism: the weights passed hold experts [e0, e0 + ne) of the E the
  * router chose from (gate/up w [ne, I, H*bits/32], down w [ne, H, ...]), and

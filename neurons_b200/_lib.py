@@ -39,6 +39,7 @@ SIGNATURES = {
                                  I, P, P]),
     "nq_moe_partial_workspace_size": (U64, [I64, I64, I64, I64, I64, I64]),
     "nq_quantized_matmul_push": (I, [P, I64, P, P, P, I64, I64, I, I, I64, I64, P, P]),
+    "nq_quantized_matmul_push_check": (I, [P, I64, P, P, P, I64, I64, I, I, I64, I64, P]),
     "nq_moe_switch_partial": (I, [P, I64, I64, I64, I64, I64, P, P, I64, I64, P, P, P, P, P, P, P,
                                   P, P, I, I, P, U64, P, P]),
 }

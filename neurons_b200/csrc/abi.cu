@@ -75,6 +75,9 @@ int fail(nq_status st, const std::string &msg) {
 
 int from_cuda(cudaError_t e, const char *what) {
     if (e == cudaSuccess) return NQ_SUCCESS;
+    // a rejected launch must not leave its status behind for the caller's next
+    // CUDA call (cudaGetLastError resets it; sticky errors stay sticky anyway)
+    cudaGetLastError();
     return fail(NQ_COMPUTE_ERROR, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
@@ -228,11 +231,15 @@ int nq_quantized_matmul_launches(int64_t M, int64_t N, int64_t K, int bits, int 
     return 1;
 }
 
-int nq_quantized_matmul_push(const uint16_t *x, int64_t M, const uint32_t *wq,
-                             const uint16_t *scales, const uint16_t *biases, int64_t N, int64_t K,
-                             int bits, int group_size, int64_t N_total, int64_t col0,
-                             const nq_push_t *push, void *stream) {
-    const char *what = "nq_quantized_matmul_push";
+}  // extern "C"
+
+// Everything nq_quantized_matmul_push checks before it launches, in one place,
+// so that a caller can validate a fused call before any other work of the
+// call is enqueued.  Device-independent checks come first.
+static int push_validate(const char *what, const uint16_t *x, int64_t M, const uint32_t *wq,
+                         const uint16_t *scales, const uint16_t *biases, int64_t N, int64_t K,
+                         int bits, int group_size, int64_t N_total, int64_t col0,
+                         const nq_push_t *push) {
     if (int rc = check_quant(N, K, bits, group_size, what)) return rc;
     if (M <= 0 || N <= 0) return fail(NQ_INVALID_INPUT, std::string(what) + ": M and N must be > 0");
     if (!x || !wq || !scales || !biases || !push)
@@ -248,7 +255,51 @@ int nq_quantized_matmul_push(const uint16_t *x, int64_t M, const uint32_t *wq,
         if (!push->dst[q]) return fail(NQ_INVALID_INPUT, std::string(what) + ": NULL destination");
     if (!aligned16(x) || !aligned16(wq))
         return fail(NQ_INVALID_INPUT, std::string(what) + ": x and wq must be 16-byte aligned");
+    if (M >= tc_threshold()) {
+        nq::TcGemmArgs a;
+        a.x = x; a.x_ld = K; a.M = M;
+        a.w = wq; a.s = scales; a.b = biases;
+        a.N = N; a.K = K; a.bits = bits; a.gs = group_size;
+        a.y_ld = N_total;
+        if ((a.x_ld * 2) % 16 || (K * bits / 8) % 16)
+            return fail(NQ_INVALID_INPUT,
+                        std::string(what) + ": K*bits/8 must be a multiple of 16 bytes");
+        if (int rc = need_device(what)) return rc;
+        if (!nq::tc_gemm_supported(a))
+            return fail(NQ_INVALID_INPUT, std::string(what) + ": shape not served by the fused path");
+        return NQ_SUCCESS;
+    }
+    nq::GemvProblems p;
+    p.w = wq; p.s = scales; p.b = biases;
+    p.N = N; p.K = K; p.bits = bits; p.gs = group_size;
+    p.x = x; p.x_ld = K;
+    if (const char *why = nq::gemv_push_unsupported(p))
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": " + why);
     if (int rc = need_device(what)) return rc;
+    if (!nq::tensor_maps_available())
+        return fail(NQ_BACKEND_NOT_AVAILABLE,
+                    std::string(what) + ": the driver provides no tensor-map encoder");
+    return NQ_SUCCESS;
+}
+
+extern "C" {
+
+int nq_quantized_matmul_push_check(const uint16_t *x, int64_t M, const uint32_t *wq,
+                                   const uint16_t *scales, const uint16_t *biases, int64_t N,
+                                   int64_t K, int bits, int group_size, int64_t N_total,
+                                   int64_t col0, const nq_push_t *push) {
+    return push_validate("nq_quantized_matmul_push", x, M, wq, scales, biases, N, K, bits,
+                         group_size, N_total, col0, push);
+}
+
+int nq_quantized_matmul_push(const uint16_t *x, int64_t M, const uint32_t *wq,
+                             const uint16_t *scales, const uint16_t *biases, int64_t N, int64_t K,
+                             int bits, int group_size, int64_t N_total, int64_t col0,
+                             const nq_push_t *push, void *stream) {
+    const char *what = "nq_quantized_matmul_push";
+    if (int rc = push_validate(what, x, M, wq, scales, biases, N, K, bits, group_size, N_total,
+                               col0, push))
+        return rc;
     nq::PushDev pd;
     pd.n = push->nranks;
     pd.epoch = push->epoch;
@@ -264,8 +315,6 @@ int nq_quantized_matmul_push(const uint16_t *x, int64_t M, const uint32_t *wq,
         a.N = N; a.K = K; a.bits = bits; a.gs = group_size;
         a.y = y; a.y_ld = N_total;
         a.push = &pd;
-        if (!nq::tc_gemm_supported(a))
-            return fail(NQ_INVALID_INPUT, std::string(what) + ": shape not served by the fused path");
         return from_cuda(nq::launch_tc_gemm(a, st), what);
     }
     nq::GemvProblems p;
@@ -275,10 +324,7 @@ int nq_quantized_matmul_push(const uint16_t *x, int64_t M, const uint32_t *wq,
     p.P = 1; p.M = (int)M; p.max_m = (int)M;
     p.y = y; p.y_ld = N_total;
     p.push = &pd;
-    const cudaError_t e = nq::launch_gemv(p, st);
-    if (e == cudaErrorNotSupported)
-        return fail(NQ_INVALID_INPUT, std::string(what) + ": shape not served by the fused path");
-    return from_cuda(e, what);
+    return from_cuda(nq::launch_gemv(p, st), what);
 }
 
 int nq_gather_qmm(const uint16_t *x, int64_t x_batch, int64_t M, const int32_t *lhs_indices,

@@ -355,6 +355,21 @@ int nq_tp_quantized_matmul_fused(nq_comm_t comm, const uint16_t *x, int64_t M,
     const size_t off = (size_t)(yc - data);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     unsigned int *epoch = reinterpret_cast<unsigned int *>(comm->arena + kEpochOff);
+    nq_push_t p;
+    std::memset(&p, 0, sizeof(p));
+    p.nranks = comm->size;
+    p.rank = comm->rank;
+    p.epoch = epoch;
+    p.ready = reinterpret_cast<const unsigned int *>(comm->arena + kReadyOff);
+    for (int q = 0; q < comm->size; ++q) p.dst[q] = comm->peer[q] + kArenaHeader + off;
+    // Every check of the compute step runs before anything is enqueued: a
+    // rejected call launches nothing and leaves the call count (the epoch)
+    // where it was.  (A rejection on some ranks only leaves the others' calls
+    // to end on their bounded waits, with the timeout bit set.)
+    if (int rc = from_nq(nq_quantized_matmul_push_check(x, M, w_shard, s_shard, b_shard, rows, K,
+                                                        bits, group_size, N, row0, &p),
+                         what))
+        return rc;
     // ready: this rank's earlier stream work is done; tell every rank
     {
         cudaLaunchConfig_t cfg = {};
@@ -373,13 +388,6 @@ int nq_tp_quantized_matmul_fused(nq_comm_t comm, const uint16_t *x, int64_t M,
                 what))
             return rc;
     }
-    nq_push_t p;
-    std::memset(&p, 0, sizeof(p));
-    p.nranks = comm->size;
-    p.rank = comm->rank;
-    p.epoch = epoch;
-    p.ready = reinterpret_cast<const unsigned int *>(comm->arena + kReadyOff);
-    for (int q = 0; q < comm->size; ++q) p.dst[q] = comm->peer[q] + kArenaHeader + off;
     if (int rc = from_nq(nq_quantized_matmul_push(x, M, w_shard, s_shard, b_shard, rows, K, bits,
                                                   group_size, N, row0, &p, stream),
                          what))

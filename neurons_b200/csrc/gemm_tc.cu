@@ -39,6 +39,7 @@
 // few SMs while the others already work through the whole tiles.
 #include <cuda.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "nq_common.cuh"
@@ -424,7 +425,272 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ----------------------------------------------------------------------------
+// CTA-pair kernel for the whole tiles of problems with 256-token tiles: two
+// CTAs (a cluster on two SMs) own 256 weight rows (128 each) x 256 tokens.
+// One tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16) reads both operands
+// from shared memory -- each CTA holds its 128 weight rows of A and its 128
+// tokens of B -- and writes each CTA's 128 x 256 fp32 accumulator in its own
+// TMEM.  Compared with the single-CTA kernel above, the dequantized weights go
+// to shared memory (16-byte st.shared into the canonical K-major layout, 128-
+// byte swizzle) instead of TMEM, and every SM reads only half of the token
+// tile per MMA, so the shared-memory traffic per MMA stays at the single-CTA
+// kernel's while the A-operand stores into TMEM are gone.
+//   warp 16  TMA producer (each CTA): its token half [128 x 64 bf16] and its
+//            code tile [128 rows x 32|64 B] per stage;
+//   warps 0..15 dequantizers (each CTA), as in the single-CTA kernel, writing
+//            A into the stage's A slot; the 8 warps of a stage then arrive on
+//            the EVEN CTA's afull barrier (so it counts both CTAs: 16);
+//   warp 17  allocates 256 TMEM columns over the pair (cta_group::2); in the
+//            even CTA one lane issues the MMAs and commits each stage to the
+//            empty barriers of both CTAs (multicast commit).
+// The epilogue is the single-CTA kernel's TMA-store epilogue, per CTA.
+// ----------------------------------------------------------------------------
+constexpr int kPairTok = 256;   // tokens per pair tile (UMMA N)
+constexpr int kPairHalf = 128;  // tokens staged by each CTA
+
+template <int BITS>
+struct PairCfg {
+    static constexpr int kXBytes = kPairHalf * kBlockK * 2;             // 16 KB
+    static constexpr int kABytes = kBlockW * kBlockK * 2;               // 16 KB
+    static constexpr int kWBytes = kBlockW * kBlockK * BITS / 8;        // 4 | 8 KB
+    static constexpr int kStages = 5;
+    static constexpr int kSmemBytes =
+        kStages * (kXBytes + kABytes + kWBytes) + 1024 /*align*/ + 512 /*barriers*/;
+    static_assert(kSmemBytes <= 232448, "shared memory budget");
+    static_assert(kPairTok * kBlockW * 2 <= kStages * (kXBytes + kABytes), "epilogue staging");
+};
+
+template <int BITS>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_qgemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                         const __grid_constant__ CUtensorMap tmap_w,
+                         const __grid_constant__ CUtensorMap tmap_y, const TcParams prm) {
+    using Cfg = PairCfg<BITS>;
+    constexpr int S = Cfg::kStages;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                ~uintptr_t(1023));
+    uint8_t *as = smem;                                   // S x A slot [128 rows][128 B], SW128
+    uint8_t *xs = smem + S * Cfg::kABytes;                // S x [128 tokens][128 B], SW128
+    uint8_t *ws = xs + S * Cfg::kXBytes;                  // S x [128 rows][32|64 B]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ws + S * Cfg::kWBytes);
+    uint64_t *full = bars;            // this CTA's TMA landed (x half + codes)
+    uint64_t *empty = bars + S;       // the pair's MMAs of the stage completed
+    uint64_t *afull = bars + 2 * S;   // (even CTA) A slots of both CTAs written
+    uint64_t *accfull = bars + 3 * S; // accumulator complete
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * S + 1);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    // both CTAs of a pair see the same tile index (even n-tile, same row)
+    if ((int)(blockIdx.y * gridDim.x + (blockIdx.x & ~1u)) >= prm.main_tiles) return;
+    const uint32_t rank = cluster_ctarank();
+    const int64_t n0 = (int64_t)blockIdx.x * kBlockW;  // this CTA's 128 weight rows
+    const int64_t m0 = (int64_t)blockIdx.y * kPairTok;  // the pair's 256 tokens
+    const int num_kb = prm.num_kb;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+            mbar_init(&afull[s], 2 * kStageArrivals);
+        }
+        mbar_init(accfull, 1);
+        *abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == kProducerWarp && lane == 0) {
+        prefetch_tmap(&tmap_x);
+        prefetch_tmap(&tmap_w);
+        prefetch_tmap(&tmap_y);
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc_pair(tmem_holder, kPairTok);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();  // barriers initialised and TMEM allocated in both CTAs
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            const uint32_t bytes = Cfg::kXBytes + Cfg::kWBytes;
+            for (int i = 0; i < num_kb; ++i) {
+                const int s = i % S;
+                const uint32_t ph = (uint32_t)(i / S) & 1u;
+                if (!wait_or_abort(&empty[s], ph ^ 1u, abort, prm.err)) break;
+                mbar_expect_tx(&full[s], bytes);
+                tma_load_2d(xs + s * Cfg::kXBytes, &tmap_x, &full[s], i * kBlockK,
+                            (int32_t)(m0 + kPairHalf * rank));
+                tma_load_2d(ws + s * Cfg::kWBytes, &tmap_w, &full[s], i * (kBlockK * BITS / 32),
+                            (int32_t)n0);
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_bf16_f32(2 * kBlockW, kPairTok);
+            for (int i = 0; i < num_kb; ++i) {
+                const int s = i % S;
+                const uint32_t ph = (uint32_t)(i / S) & 1u;
+                bool ok = mbar_try_wait_cluster(&afull[s], ph);
+                if (!ok) {
+                    const unsigned long long t0 = global_timer_ns();
+                    while (!(ok = mbar_try_wait_cluster(&afull[s], ph))) {
+                        if (*abort) break;
+                        if (global_timer_ns() - t0 > kWaitLimitNs) {
+                            *abort = 1;
+                            atomicOr(prm.err, kErrWaitTimeout);
+                            break;
+                        }
+                    }
+                }
+                if (!ok) break;
+                tc_fence_after();
+                const uint64_t adesc = smem_desc_k_sw128(smem_u32(as + s * Cfg::kABytes));
+                const uint64_t bdesc = smem_desc_k_sw128(smem_u32(xs + s * Cfg::kXBytes));
+#pragma unroll
+                for (int j = 0; j < kBlockK / 16; ++j)
+                    // +32 bytes per 16 bf16 of K inside the 128-byte swizzled rows
+                    umma_ss_pair(tmem_base, adesc + (uint64_t)(j * 2), bdesc + (uint64_t)(j * 2),
+                                 idesc, (i > 0 || j > 0) ? 1u : 0u);
+                umma_commit_pair(&empty[s], 3);
+            }
+            umma_commit_pair(accfull, 3);
+        }
+    } else {
+        // ------------------------------------------------ dequantizers
+        const int q = warp & 3;
+        const int h = (warp >> 2) & 1;
+        const int par = warp >> 3;
+        const int r = q * 32 + lane;     // weight row inside this CTA's 128
+        const int64_t n = n0 + r;
+        const bool row_ok = n < prm.N;
+        const int64_t G = prm.K >> prm.gs_shift;
+        const uint16_t *srow = prm.s + (row_ok ? n : 0) * G;
+        const uint16_t *brow = prm.b + (row_ok ? n : 0) * G;
+        auto load_sb = [&](int kb, uint16_t &sv, uint16_t &bv) {
+            const int k = kb * kBlockK + 32 * h;
+            sv = 0;
+            bv = 0;
+            if (row_ok && kb < num_kb && k < prm.K) {
+                sv = srow[k >> prm.gs_shift];
+                bv = brow[k >> prm.gs_shift];
+            }
+        };
+        uint16_t sq[kSbAhead], bq[kSbAhead];
+#pragma unroll
+        for (int i = 0; i < kSbAhead; ++i) load_sb(par + 2 * i, sq[i], bq[i]);
+        const uint32_t afull_leader0 = mapa_shared(smem_u32(afull), 0);
+        // this thread's row in the A slot: 128 B, 16-byte chunk c at (c ^ (r & 7))
+        const uint32_t a_row = (uint32_t)r * 128;
+        for (int it = par; it < num_kb; it += 2) {
+            const int s = it % S;
+            const uint32_t ph = (uint32_t)(it / S) & 1u;
+            if (!wait_or_abort(&full[s], ph, abort, prm.err)) break;
+            uint32_t out[16];
+            const uint8_t *wst = ws + s * Cfg::kWBytes;
+            if constexpr (BITS == 4) {
+                const uint4 v = *reinterpret_cast<const uint4 *>(
+                    wst + r * 32 + 16 * (h ^ ((r >> 2) & 1)));
+                const Dq4 d = make_dq4(sq[0], bq[0]);
+                const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t d0 = dq4_pair(q4_pair_biased(words[i], 0), d);
+                    const uint32_t d1 = dq4_pair(q4_pair_biased(words[i], 1), d);
+                    const uint32_t d2 = dq4_pair(q4_pair_biased(words[i], 2), d);
+                    const uint32_t d3 = dq4_pair(q4_pair_biased(words[i], 3), d);
+                    out[4 * i + 0] = prmt(d0, d1, 0x5410u);
+                    out[4 * i + 1] = prmt(d2, d3, 0x5410u);
+                    out[4 * i + 2] = prmt(d0, d1, 0x7632u);
+                    out[4 * i + 3] = prmt(d2, d3, 0x7632u);
+                }
+            } else {
+                const int x = (r >> 1) & 3;
+                const uint4 v0 = *reinterpret_cast<const uint4 *>(wst + r * 64 + 16 * ((2 * h) ^ x));
+                const uint4 v1 =
+                    *reinterpret_cast<const uint4 *>(wst + r * 64 + 16 * ((2 * h + 1) ^ x));
+                const Dq8 d = make_dq8(sq[0], bq[0]);
+                const uint32_t words[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    out[2 * i + 0] = dq8_pair(words[i], 0, 1, d);
+                    out[2 * i + 1] = dq8_pair(words[i], 2, 3, d);
+                }
+            }
+            // 32 codes = 4 chunks (4h .. 4h+3) of this row of the A slot
+            uint8_t *arow = as + s * Cfg::kABytes + a_row;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                *reinterpret_cast<uint4 *>(arow + (((4 * h + j) ^ (r & 7)) << 4)) =
+                    make_uint4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
+            fence_proxy_async_smem();  // the pair's tensor core reads the slot
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(afull_leader0 + (uint32_t)(s * 8));
+#pragma unroll
+            for (int i = 0; i + 1 < kSbAhead; ++i) {
+                sq[i] = sq[i + 1];
+                bq[i] = bq[i + 1];
+            }
+            load_sb(it + 2 * kSbAhead, sq[kSbAhead - 1], bq[kSbAhead - 1]);
+        }
+        // ------------------------------------------------ epilogue
+        bool acc_ok = wait_or_abort(accfull, 0, abort, prm.err) && !*abort;
+        const int part = warp >> 2;  // quarter of the accumulator columns (tokens)
+        const uint32_t t_lane = (uint32_t)(q * 32) << 16;
+        uint8_t *stage = smem;
+        if (acc_ok) {
+            tc_fence_after();
+            for (int c0 = part * (kPairTok / 4); c0 < (part + 1) * (kPairTok / 4); c0 += 16) {
+                uint32_t acc[16];
+                tmem_ld_32x32b_x16(tmem_base + t_lane + (uint32_t)c0, acc);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    *reinterpret_cast<uint16_t *>(stage + ((c0 + j) * kBlockW + r) * 2) =
+                        f32_to_bf16(__uint_as_float(acc[j]));
+            }
+        }
+        fence_proxy_async_smem();
+        bar_sync(1, 16 * 32);
+        if (threadIdx.x == 0 && acc_ok) {
+            tma_store_2d(&tmap_y, stage, (int32_t)n0, (int32_t)m0);
+            bulk_commit_group();
+            bulk_wait_group_read0();
+        }
+    }
+
+    // (launched after the split tail as its programmatic dependent: completing
+    // only after the tail grid keeps the stream's order for later work)
+    if (prm.split > 1) pdl_wait();
+    tc_fence_before();
+    cluster_sync_all();  // both CTAs are done with their TMEM and the shared operands
+    if (warp == kMmaWarp) {
+        if (*abort) {
+            const unsigned long long t0 = global_timer_ns();
+            while (global_timer_ns() - t0 < 10000000ull) {
+            }
+        }
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, kPairTok);
+    }
+}
+
 // ------------------------------------------------------------- host side
+
+// The CTA-pair kernel serves the whole 256-token tiles when the environment
+// sets NQ_TC_PAIR=1 (both kernels compute the same tiles; the single-CTA
+// kernel is the default while it is the faster one).
+bool pair_kernel_enabled() {
+    static const bool on = [] {
+        const char *v = getenv("NQ_TC_PAIR");
+        return v && v[0] == '1';
+    }();
+    return on;
+}
 
 // CTAs per tail tile (1: no split): the last T % W tiles (one CTA per SM on W
 // SMs) are split along K when they would leave more than half the SMs idle;
@@ -555,6 +821,43 @@ cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
         cfg.numAttrs = 1;
         e = cudaLaunchKernelEx(&cfg, tc_qgemm_kernel<BITS, BM, true>, mx, mw, my, prm);
         if (e != cudaSuccess) return e;
+    }
+    // Whole 256-token tiles go to the CTA-pair kernel when the tiles pair up
+    // (an even number of 128-row weight tiles per token tile, an even count of
+    // whole tiles) and the output leaves through the TMA-store epilogue.
+    if constexpr (BM == kPairTok) {
+        if (prm.main_tiles > 0 && pair_kernel_enabled() && n_tiles % 2 == 0 &&
+            prm.main_tiles % 2 == 0 && prm.tma_store) {
+            using PC = PairCfg<BITS>;
+            CUtensorMap mxh;
+            if (!make_map_2d(&mxh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, (uint64_t)a.K,
+                             (uint64_t)a.M, (uint64_t)a.x_ld * 2, kBlockK, kPairHalf,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+                return cudaErrorInvalidValue;
+            auto kern = tc_qgemm_pair_kernel<BITS>;
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 PC::kSmemBytes);
+            if (e != cudaSuccess) return e;
+            const int64_t full_rows = (prm.main_tiles + n_tiles - 1) / n_tiles;
+            if (full_rows > 65535) return cudaErrorInvalidValue;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)n_tiles, (unsigned)full_rows, 1);
+            cfg.blockDim = dim3(kThreads, 1, 1);
+            cfg.dynamicSmemBytes = PC::kSmemBytes;
+            cfg.stream = stream;
+            cudaLaunchAttribute attrs[2];
+            attrs[0].id = cudaLaunchAttributeClusterDimension;
+            attrs[0].val.clusterDim.x = 2;
+            attrs[0].val.clusterDim.y = 1;
+            attrs[0].val.clusterDim.z = 1;
+            attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attrs[1].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attrs;
+            cfg.numAttrs = prm.split > 1 ? 2 : 1;
+            e = cudaLaunchKernelEx(&cfg, kern, mxh, mw, my, prm);
+            if (e != cudaSuccess) return e;
+            return cudaGetLastError();
+        }
     }
     if (prm.main_tiles > 0) {
         auto kern = tc_qgemm_kernel<BITS, BM, false>;

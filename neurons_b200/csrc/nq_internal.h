@@ -62,6 +62,11 @@ struct GemvProblems {
 
 cudaError_t launch_gemv(const GemvProblems &p, cudaStream_t stream);
 
+// Why launch_gemv cannot serve p with an output fan-out (p.push), or nullptr
+// when its arguments allow it (the fan-out also needs tensor maps from the
+// driver: tensor_maps_available()).  Host-side only: no device work.
+const char *gemv_push_unsupported(const GemvProblems &p);
+
 // Dense path for larger M: TMA + tcgen05 GEMM with in-TMEM dequant.
 struct TcGemmArgs {
     const uint16_t *x = nullptr;   // [M, K] bf16 (row stride x_ld)

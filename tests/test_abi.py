@@ -117,3 +117,30 @@ def test_python_errors_carry_error_code():
     with pytest.raises(NQError) as ei:
         quantized_matmul(torch.zeros(1, 64, dtype=torch.bfloat16), None, None)
     assert ei.value.code == "InvalidInput"
+
+
+class NqPush(__import__("ctypes").Structure):
+    """nq_push_t (include/nq.h)."""
+    import ctypes as _c
+    _fields_ = [("nranks", _c.c_int), ("rank", _c.c_int), ("epoch", _c.c_void_p),
+                ("dst", _c.c_void_p * 8), ("ready", _c.c_void_p)]
+
+
+def test_push_check_names_misaligned_scales(nqlib):
+    """A fused tensor-parallel call whose scale shard is not 16-byte aligned is
+    rejected by the check that runs before the call enqueues anything (its
+    ready kernel included), and the message names the scales.  Pointers are
+    never dereferenced by the check, so this needs no device."""
+    import ctypes
+    p = NqPush()
+    p.nranks, p.rank, p.epoch, p.ready = 2, 0, 0x5000, 0x6000
+    p.dst[0], p.dst[1] = 0x7000, 0x8000
+    args = [ctypes.c_void_p(0x1000), 1, ctypes.c_void_p(0x2000), ctypes.c_void_p(0x3002),
+            ctypes.c_void_p(0x4000), 64, 512, 4, 64, 128, 0, ctypes.byref(p)]
+    rc = nqlib.nq_quantized_matmul_push_check(*args)
+    assert rc == 1, rc  # NQ_INVALID_INPUT
+    assert b"scales and biases must be 16-byte aligned" in nqlib.nq_last_error()
+    args[3] = ctypes.c_void_p(0x3000)
+    args[10] = 100  # columns [100, 164) outside N_total = 128
+    assert nqlib.nq_quantized_matmul_push_check(*args) == 1
+    assert b"columns outside" in nqlib.nq_last_error()

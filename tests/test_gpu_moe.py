@@ -206,3 +206,48 @@ def test_switch_partials_sum_to_the_full_step(oracle, nqlib, T):
     assert nb.take_device_error() == 0
     y = tot.to(torch.bfloat16)
     assert_close(host_u16(y), host_u16(full), f"partials T={T}")
+
+
+def test_switch_qwen3_T2048_sampled_tokens(oracle, nqlib):
+    """The benchmark's MoE layer at full size: Qwen3-30B-A3B dims (E=128, top-8,
+    H=2048, I=768, 4-bit g64), T=2048 tokens on the grouped tensor-core path
+    (about 128 tokens per expert, the busiest near 150; experts spanning more
+    than one 256-token tile are covered by the (600, 4, 2) case above).  Tokens
+    are independent given their routing, so a seeded sample of 64 tokens is
+    checked stage by stage against the oracle (h of every sampled pair, y of
+    every sampled token, and y end to end)."""
+    import neurons_b200 as nb
+    T, E, k, H, I = 2048, 128, 8, 2048, 768
+    g = torch.Generator(device="cuda").manual_seed(2048)
+    mats = []
+    for rows, cols in ((I, H), (I, H), (H, I)):
+        w = torch.randn(E, rows, cols, device="cuda", generator=g) * 0.02
+        mats.append(nb.quantize(w, 64, 4, nb.SCHEME_MLX_AFFINE))
+        del w
+    x = torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16)
+    logits = torch.randn(T, E, device="cuda", generator=g).to(torch.bfloat16)
+    idx, sc = nb.moe_route(logits, k)
+    ws = torch.zeros(nb.moe_workspace_size(T, E, k, H, I), dtype=torch.uint8, device="cuda")
+    y = nb.moe_switch(x, idx, sc, *mats, 64, 4, workspace=ws)
+    torch.cuda.synchronize()
+    assert nb.take_device_error() == 0
+    idx_h, sc_h = idx.cpu().numpy(), sc.cpu().numpy()
+    assert np.bincount(idx_h.reshape(-1), minlength=E).min() > 0, "every expert is used"
+    host = [(m[0].cpu().view(torch.int32).numpy().view(np.uint32), host_u16(m[1]),
+             host_u16(m[2])) for m in mats]
+    sample = np.sort(np.random.default_rng(0).choice(T, 64, replace=False))
+    x_h = host_u16(x)[sample]
+    h_all = workspace_hidden(ws, T, E, k, H, I).reshape(T, k, I)
+    h_s = h_all[sample].reshape(-1, I)
+    gate, up, down = host
+    assert_close(h_s, oracle.moe_hidden(x_h, idx_h[sample], gate, up, 4, 64, rounding=1),
+                 "T=2048 h (sampled pairs)")
+    y_s = host_u16(y)[sample]
+    assert_close(y_s, oracle.moe_combine(h_s, idx_h[sample], sc_h[sample], down, 4, 64,
+                                         rounding=1), "T=2048 y (sampled tokens)")
+    yy = oracle.bf16_to_f32(y_s).astype(np.float64)
+    for rounding in (1, 0):
+        r = oracle.bf16_to_f32(oracle.moe_switch(x_h, idx_h[sample], sc_h[sample], gate, up,
+                                                 down, 4, 64, rounding=rounding))
+        r = r.astype(np.float64)
+        assert np.linalg.norm(yy - r) / np.linalg.norm(r) < 1e-2, rounding

@@ -221,3 +221,79 @@ def test_back_to_back_launches_are_ordered(oracle, nqlib):
     assert_close(host_u16(y1), oracle.qmm(x, *w1, 4, 64), "chained stage 1")
     ref2 = oracle.qmm(host_u16(y1), *w2, 4, 64)
     assert_close(host_u16(y2), ref2, "chained stage 2")
+
+
+@pytest.mark.parametrize("N,K", [(14336, 4096), (4096, 14336)])
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("gs", [32, 64, 128])
+def test_mistral_mlp_sweep(oracle, nqlib, N, K, bits, gs):
+    """The parameter sweep on Mistral-7B MLP shapes (up 4096 -> 14336 and down
+    14336 -> 4096) at every bit width, group size and M in {1, 8, 32, 128, 512,
+    2048}: GEMV and tensor-core paths, seeded N(0, 0.02) weights quantized on the
+    device (MLX affine scheme) and N(0, 1) activations.  Every output of 48
+    sampled weight rows is checked against the oracle's matmul of the same
+    codes."""
+    import neurons_b200 as nb
+    g = torch.Generator(device="cuda").manual_seed(N + K + bits + gs)
+    w = torch.randn(N, K, device="cuda", generator=g) * 0.02
+    wq, s, b = nb.quantize(w, gs, bits, nb.SCHEME_MLX_AFFINE)
+    del w
+    rows = np.sort(np.random.default_rng(bits * gs).choice(N, 48, replace=False))
+    wq_h = wq.cpu().view(torch.int32).numpy().view(np.uint32)[rows]
+    s_h, b_h = host_u16(s)[rows], host_u16(b)[rows]
+    for M in (1, 8, 32, 128, 512, 2048):
+        x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+        y = nb.quantized_matmul(x, wq, s, b, True, gs, bits)
+        torch.cuda.synchronize()
+        assert nb.take_device_error() == 0
+        ref = oracle.qmm(host_u16(x), wq_h, s_h, b_h, bits, gs)
+        assert_close(host_u16(y)[:, rows], ref, f"mistral {N}x{K} b{bits} g{gs} M={M}")
+
+
+@pytest.mark.parametrize("M", [1, 2, 5, 8])
+@pytest.mark.parametrize("gs", [32, 64, 128])
+@pytest.mark.parametrize("N,K", [(16, 1024), (100, 2048), (3072, 3072), (1000, 4096), (40, 8192),
+                                 (33, 6144)])
+def test_row_group_gemv(oracle, nqlib, M, gs, N, K):
+    """The row-group decode kernel (4-bit, M <= 8, K a multiple of 128 split
+    exactly over 4..16 warps): ragged row counts, every group size, and slice
+    lengths of 2, 3, 4 and 8 k-blocks."""
+    run_case(oracle, M, N, K, 4, gs, seed=N + K + M + gs)
+
+
+def test_row_group_gemv_many_rows(oracle, nqlib):
+    """More row groups than 8 per SM: the long-slice configuration (LM-head
+    sized, here 20000 x 3072) with sampled rows against the oracle."""
+    import neurons_b200 as nb
+    rng = np.random.default_rng(20000)
+    N, K = 20000, 3072
+    wq, s, b = oracle.quantize(weights(rng, N, K), 4, 64, 1)
+    x = acts(rng, 3, K)
+    y = host_u16(nb.quantized_matmul(dev_bf16(x), dev_u32(wq), dev_bf16(s), dev_bf16(b), True,
+                                      64, 4))
+    torch.cuda.synchronize()
+    assert nb.take_device_error() == 0
+    rows = np.sort(rng.choice(N, 256, replace=False))
+    assert_close(y[:, rows], oracle.qmm(x, wq[rows], s[rows], b[rows], 4, 64), "20000x3072")
+    assert_close(y[:, -16:], oracle.qmm(x, wq[-16:], s[-16:], b[-16:], 4, 64), "last rows")
+
+
+def test_row_group_gemv_chained_launches(oracle, nqlib):
+    """Back-to-back row-group launches under programmatic dependent launch:
+    y2 = W2 y1 right after y1 = W1 x (the second kernel's weight loads run
+    ahead, its activation reads must wait for the first kernel)."""
+    import neurons_b200 as nb
+    rng = np.random.default_rng(4096)
+    w1 = oracle.quantize(weights(rng, 4096, 3072), 4, 64, 0)
+    w2 = oracle.quantize(weights(rng, 3072, 4096), 4, 64, 0)
+    x = acts(rng, 2, 3072)
+    d1 = [dev_u32(w1[0]), dev_bf16(w1[1]), dev_bf16(w1[2])]
+    d2 = [dev_u32(w2[0]), dev_bf16(w2[1]), dev_bf16(w2[2])]
+    xd = dev_bf16(x)
+    for _ in range(20):
+        y1 = nb.quantized_matmul(xd, *d1, True, 64, 4)
+        y2 = nb.quantized_matmul(y1, *d2, True, 64, 4)
+    torch.cuda.synchronize()
+    assert nb.take_device_error() == 0
+    assert_close(host_u16(y1), oracle.qmm(x, *w1, 4, 64), "row-group chain stage 1")
+    assert_close(host_u16(y2), oracle.qmm(host_u16(y1), *w2, 4, 64), "row-group chain stage 2")
