@@ -453,7 +453,7 @@ def moe_summary(T, t, steps, byts, flops, world, pk):
     return d
 
 
-def _events_time(step, steps, warmup, world, graph=False):
+def _events_time(step, steps, warmup, world, graph=False, clocks=None):
     """Device time of `steps` calls of step(i), bracketed by a barrier and a
     synchronize, CUDA events on the current stream, max over ranks.  With
     graph=True the steps are captured in one CUDA graph and replayed, as a
@@ -472,6 +472,8 @@ def _events_time(step, steps, warmup, world, graph=False):
         torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.start()
     stream = torch.cuda.current_stream()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -483,7 +485,10 @@ def _events_time(step, steps, warmup, world, graph=False):
             step(i)
     t1.record(stream)
     torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.last = clocks.stop()
     barrier(world)
+    del g
     return max_over_ranks(t0.elapsed_time(t1) / 1e3, world)
 
 
@@ -553,7 +558,7 @@ def time_ep(comm, T, steps, warmup, world, rank):
     return t
 
 
-def time_tp_fused(comm, M, N, K, steps, warmup, world, rank):
+def time_tp_fused(comm, M, N, K, steps, warmup, world, rank, clocks=None):
     """time_tp with the all-gather fused into the kernel's stores (peer
     writes into the symmetric arena over NVLink)."""
     import torch
@@ -574,12 +579,58 @@ def time_tp_fused(comm, M, N, K, steps, warmup, world, rank):
         x, wq, s, b, y = sets[i % 3]
         dist.tp_quantized_matmul_fused(comm, x, wq, s, b, N, y, GS, BITS)
 
-    t = _events_time(step, steps, warmup, world, graph=M <= 32)
+    t = _events_time(step, steps, warmup, world, graph=M <= 32, clocks=clocks)
     assert nb.take_device_error() == 0 and comm.take_error() == 0
     return t
 
 
-def sharded_summary(world, rank, pk):
+def time_e2e_tp(comm, M, N, K, steps, warmup, world, rank):
+    """The tensor-parallel call end to end: every rank copies the step's x from
+    pinned host memory (each rank needs all of x), runs its shard with the
+    output pushed to every rank, and rank 0 copies the whole y back to pinned
+    host memory (every rank holds all of y; the host reads one copy).  Copies
+    are inside the timed region, one stream, max over ranks."""
+    import torch
+    import neurons_b200 as nb
+    from neurons_b200 import dist
+    _, rows = dist.tp_shard(N, world, rank)
+    g = torch.Generator(device="cuda").manual_seed(4000 + rank)
+    w = torch.randn(rows, K, device="cuda", generator=g) * 0.02
+    wq, s, b = nb.quantize(w, GS, BITS, nb.SCHEME_MINMAX)
+    del w
+    xh = torch.randn(M, K, generator=torch.Generator().manual_seed(rank)).to(
+        torch.bfloat16).pin_memory()
+    yh = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
+    y = comm.symmetric_tensor(0, (M, N))
+
+    def step(i):
+        xd.copy_(xh, non_blocking=True)
+        dist.tp_quantized_matmul_fused(comm, xd, wq, s, b, N, y, GS, BITS)
+        if rank == 0:
+            yh.copy_(y, non_blocking=True)
+
+    t = _events_time(step, steps, warmup, world)
+    assert nb.take_device_error() == 0 and comm.take_error() == 0
+    return t, M * K * 2, (M * N * 2 if rank == 0 else 0)
+
+
+def tp_headline(M, N, K, steps, warmup, world, rank, local):
+    """N > 1 headline: the prefill problem split over the ranks by weight rows,
+    each rank's output columns pushed into every rank's y by the GEMM epilogue
+    (strong scaling: the total work is that of one single-GPU step)."""
+    from neurons_b200 import dist
+    comm = dist.Comm()
+    comm.symmetric_alloc(3 * ((M * N * 2 + 255) // 256 * 256))
+    clk = ClockSampler(local)
+    t = time_tp_fused(comm, M, N, K, steps, warmup, world, rank, clocks=clk)
+    n_e = min(steps, 50)
+    t_e, h2d, d2h = time_e2e_tp(comm, M, N, K, n_e, warmup, world, rank)
+    comm.close()
+    return t, getattr(clk, "last", None), (t_e, n_e, h2d, d2h)
+
+
+def sharded_summary(world, rank, pk, single=None):
     """The tensor- and expert-parallel configurations at this N (strong
     scaling), for the JSON line."""
     from neurons_b200 import dist
@@ -619,6 +670,14 @@ def sharded_summary(world, rank, pk):
                            "us_per_step": t / n * 1e6,
                            "tflops": 2 * 2048 * k * 3 * I * H * n / t / 1e12}
     comm.close()
+    # strong-scaling efficiency against the single-GPU step timed in this run:
+    # t(1 GPU) / (N * t(N GPUs))
+    single = single or {}
+    for key, ref in (("tp_prefill", "prefill_us"), ("tp_prefill_fused", "prefill_us"),
+                     ("ep_moe_T2048", "moe_T2048_us")):
+        if ref in single and key in out:
+            out[key]["efficiency"] = single[ref] / (world * out[key]["us_per_step"])
+            out[key]["single_gpu_us"] = single[ref]
     # this rank's kernels: per prefill step the shard's quantized matmul (1 or 2
     # kernels) plus the layout kernel (NCCL) or plus the ready and finish kernels
     # (fused); one GEMV per decode step (plus ready and finish when fused); nine
@@ -769,6 +828,34 @@ def ours(args):
                        "l2": f"rotating {sets} input sets of "
                              f"{(algo_bytes(M, N, K) + M * N * 2) / 2**20:.0f} MiB (> L2)"},
             "roofline": roof, "gpu_launches": launches, "clocks": clk}
+    tp_e2e = None
+    if world > 1 and args.workload == "prefill":
+        # strong scaling of the one problem; the replicas figure moves aside
+        t_tp, clk_tp, tp_e2e = tp_headline(M, N, K, args.steps, args.warmup, world, rank, local)
+        from neurons_b200 import dist
+        q = nb.quantized_matmul_launches(M, dist.tp_shard(N, world, rank)[1], K, GS, BITS)
+        line["replicas"] = {"value": value, "unit": unit, "scaling": "weak",
+                            "ms_per_step": t_dev / args.steps * 1e3,
+                            "parallelism": f"replicas x{world} (independent token batches)",
+                            "roofline": roof}
+        per_step = t_tp / args.steps
+        line["value"] = flops / per_step / 1e12
+        line["ms_per_step"] = per_step * 1e3
+        line["scaling"] = "strong"
+        line["config"]["parallelism"] = (
+            f"tp{world}: weight rows split over the ranks, each rank's output columns "
+            "pushed into every rank's y by its GEMM epilogue over NVLink (peer stores)")
+        line["tp_efficiency"] = (t_dev / args.steps) / (world * per_step)
+        share = flops / world / per_step / 1e12
+        line["roofline"] = {"bound": "tensor", "achieved": share, "peak": pk["bf16_tflops"],
+                            "unit": "TFLOP/s", "frac": share / pk["bf16_tflops"],
+                            "peak_source": pk["source"] + " (burst bf16 GEMM)",
+                            "algorithmic_flops_per_launch": flops // world,
+                            "note": "this rank's share of the flops over the whole step (its "
+                                    "GEMM, the ready/finish handshakes and the pushes)",
+                            "traffic": None, "kernels_per_call": q + 2}
+        line["clocks"] = clk_tp
+        line["gpu_launches"] += args.steps * (q + 2)
     if args.workload != "decode" and not args.no_decode:
         d = WORKLOADS["decode"]
         dsteps = 2000
@@ -793,19 +880,30 @@ def ours(args):
                                          (8 if P >= 8 * QWEN3_MOE["E"] else 7))
         line["moe"] = moe
     if args.workload == "prefill" and not args.no_sharded:
-        line["sharded"], n_sh = sharded_summary(world, rank, pk)
+        single = {"prefill_us": t_dev / args.steps * 1e6}
+        if "moe" in line:
+            single["moe_T2048_us"] = line["moe"]["T2048"]["us_per_step"]
+        line["sharded"], n_sh = sharded_summary(world, rank, pk, single)
         line["gpu_launches"] += n_sh
     if args.workload == "prefill" and not args.no_decode:
         t_r, rp, _ = time_replay(50, 3, world, seed=rank + 200)
         line["llama3b_decode"] = replay_summary(t_r, 50, rp, world, pk)
         line["gpu_launches"] += 50 * rp.launches_per_token()
         del rp
-    t_e, h2d, d2h = time_e2e(M, N, K, min(args.steps, 50), args.warmup, world, seed=rank)
-    e2e_val = world * (flops if M > 1 else byts) * min(args.steps, 50) / t_e / (
-        1e12 if M > 1 else 1e9)
-    line["e2e"] = {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": h2d,
-                   "d2h_bytes_per_step": d2h}
-    line["gpu_launches"] += min(args.steps, 50) * per_call
+    if tp_e2e is not None:
+        t_e, n_e, h2d, d2h = tp_e2e
+        line["e2e"] = {"value": flops * n_e / t_e / 1e12, "unit": unit, "h2d_bytes_per_step": h2d,
+                       "d2h_bytes_per_step": d2h,
+                       "note": "tensor parallel: x copied in on every rank, y copied out from "
+                               "rank 0, one stream"}
+        line["gpu_launches"] += n_e * line["roofline"]["kernels_per_call"]
+    else:
+        t_e, h2d, d2h = time_e2e(M, N, K, min(args.steps, 50), args.warmup, world, seed=rank)
+        e2e_val = world * (flops if M > 1 else byts) * min(args.steps, 50) / t_e / (
+            1e12 if M > 1 else 1e9)
+        line["e2e"] = {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": h2d,
+                       "d2h_bytes_per_step": d2h}
+        line["gpu_launches"] += min(args.steps, 50) * per_call
     if rank == 0 and world == 1 and not args.no_cpu:
         cb = cpu_baseline(M, N, K)
         line["cpu_baseline"] = {

@@ -78,6 +78,7 @@ struct TcParams {
     int main_tiles;   // tiles computed whole, one CTA each; the rest are split along K
     int split;        // CTAs (one cluster) per split tile: 2, 4 or 8
     int tma_store;    // whole tiles leave through the y tensor map
+    int push_vec;     // fan-out of whole tiles by 16-byte stores (rows of y 16-byte aligned)
     const uint16_t *s, *b;
     uint16_t *y;
     unsigned int *err;
@@ -348,6 +349,44 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             acc_ok = false;
         }
+        if (!SPLIT && prm.push.n && prm.push_vec) {
+            // Tensor-parallel fan-out: the bf16 tile [BM tokens][128 rows] is
+            // staged in the idle ring, then every thread pushes 16-byte pieces of
+            // token rows (256 contiguous bytes of y each) to every rank's y.
+            uint8_t *stage = smem;
+            if (acc_ok) {
+                tc_fence_after();
+                for (int c0 = part * (BM / 4); c0 < (part + 1) * (BM / 4); c0 += 16) {
+                    uint32_t acc[16];
+                    tmem_ld_32x32b_x16(tmem_base + t_lane + (uint32_t)c0, acc);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        *reinterpret_cast<uint16_t *>(stage + ((c0 + j) * kBlockW + r) * 2) =
+                            f32_to_bf16(__uint_as_float(acc[j]));
+                }
+            }
+            bar_sync(1, 16 * 32);
+            // every lane of every storing warp takes part in the (bounded) wait
+            const bool ready = push_wait_ready(prm.push, prm.err);
+            if (acc_ok && ready) {
+                const int64_t rows_left = prm.N - n0;
+                for (int q = threadIdx.x; q < BM * (kBlockW / 8); q += 16 * 32) {
+                    const int tok = q / (kBlockW / 8), ch = q % (kBlockW / 8);
+                    const int64_t m = m0 + tok;
+                    if (m >= prm.M || ch * 8 >= rows_left) continue;
+                    const uint4 v = *reinterpret_cast<const uint4 *>(stage + (tok * kBlockW + ch * 8) * 2);
+                    uint16_t *dst = prm.y + m * prm.y_ld + n0 + ch * 8;
+                    if (ch * 8 + 8 <= rows_left) {
+                        push_store(prm.push, reinterpret_cast<uint4 *>(dst), v);
+                    } else {
+                        const uint16_t *e = reinterpret_cast<const uint16_t *>(&v);
+                        for (int i = 0; i < rows_left - ch * 8; ++i) push_store(prm.push, dst + i, e[i]);
+                    }
+                }
+            }
+            acc_ok = false;
+        }
         if (prm.push.n && acc_ok && !push_wait_ready(prm.push, prm.err)) acc_ok = false;
         if (acc_ok) {
             tc_fence_after();
@@ -440,10 +479,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 //            code tile [128 rows x 32|64 B] per stage;
 //   warps 0..15 dequantizers (each CTA), as in the single-CTA kernel, writing
 //            A into the stage's A slot; the 8 warps of a stage then arrive on
-//            the EVEN CTA's afull barrier (so it counts both CTAs: 16);
-//   warp 17  allocates 256 TMEM columns over the pair (cta_group::2); in the
-//            even CTA one lane issues the MMAs and commits each stage to the
-//            empty barriers of both CTAs (multicast commit).
+//            their own CTA's afull barrier;
+//   warp 17  allocates 256 TMEM columns over the pair (cta_group::2).  In the
+//            odd CTA one lane forwards each completed afull phase to the even
+//            CTA's peer barrier (one remote arrival per stage, from a thread
+//            with no loads in flight: a cluster-scope release waits for the
+//            releasing thread's outstanding loads, and the dequantizers always
+//            have scale prefetches in flight).  In the even CTA one lane waits
+//            for both, issues the MMAs and commits each stage to the empty
+//            barriers of both CTAs (multicast commit).
 // The epilogue is the single-CTA kernel's TMA-store epilogue, per CTA.
 // ----------------------------------------------------------------------------
 constexpr int kPairTok = 256;   // tokens per pair tile (UMMA N)
@@ -477,9 +521,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *bars = reinterpret_cast<uint64_t *>(ws + S * Cfg::kWBytes);
     uint64_t *full = bars;            // this CTA's TMA landed (x half + codes)
     uint64_t *empty = bars + S;       // the pair's MMAs of the stage completed
-    uint64_t *afull = bars + 2 * S;   // (even CTA) A slots of both CTAs written
+    uint64_t *afull = bars + 2 * S;   // this CTA's A slot written (8 warps)
     uint64_t *accfull = bars + 3 * S; // accumulator complete
-    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * S + 1);
+    uint64_t *pafull = bars + 3 * S + 1;  // (even CTA) the odd CTA's A slot written
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 4 * S + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -495,7 +540,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
-            mbar_init(&afull[s], 2 * kStageArrivals);
+            mbar_init(&afull[s], kStageArrivals);
+            mbar_init(&pafull[s], 1);
         }
         mbar_init(accfull, 1);
         *abort = 0;
@@ -530,15 +576,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp == kMmaWarp) {
+        if (lane == 0 && rank == 1) {
+            // forward each afull phase of this CTA to the even CTA
+            const uint32_t peer0 = mapa_shared(smem_u32(pafull), 0);
+            for (int i = 0; i < num_kb; ++i) {
+                const int s = i % S;
+                if (!wait_or_abort(&afull[s], (uint32_t)(i / S) & 1u, abort, prm.err)) break;
+                mbar_arrive_cluster(peer0 + (uint32_t)(s * 8));
+            }
+        }
         if (lane == 0 && rank == 0) {
             constexpr uint32_t idesc = idesc_bf16_f32(2 * kBlockW, kPairTok);
             for (int i = 0; i < num_kb; ++i) {
                 const int s = i % S;
                 const uint32_t ph = (uint32_t)(i / S) & 1u;
-                bool ok = mbar_try_wait_cluster(&afull[s], ph);
+                if (!wait_or_abort(&afull[s], ph, abort, prm.err)) break;
+                bool ok = mbar_try_wait_cluster(&pafull[s], ph);
                 if (!ok) {
                     const unsigned long long t0 = global_timer_ns();
-                    while (!(ok = mbar_try_wait_cluster(&afull[s], ph))) {
+                    while (!(ok = mbar_try_wait_cluster(&pafull[s], ph))) {
                         if (*abort) break;
                         if (global_timer_ns() - t0 > kWaitLimitNs) {
                             *abort = 1;
@@ -583,7 +639,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint16_t sq[kSbAhead], bq[kSbAhead];
 #pragma unroll
         for (int i = 0; i < kSbAhead; ++i) load_sb(par + 2 * i, sq[i], bq[i]);
-        const uint32_t afull_leader0 = mapa_shared(smem_u32(afull), 0);
         // this thread's row in the A slot: 128 B, 16-byte chunk c at (c ^ (r & 7))
         const uint32_t a_row = (uint32_t)r * 128;
         for (int it = par; it < num_kb; it += 2) {
@@ -629,7 +684,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     make_uint4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
             fence_proxy_async_smem();  // the pair's tensor core reads the slot
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(afull_leader0 + (uint32_t)(s * 8));
+            if (lane == 0) mbar_arrive(&afull[s]);
 #pragma unroll
             for (int i = 0; i + 1 < kSbAhead; ++i) {
                 sq[i] = sq[i + 1];
@@ -663,6 +718,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+    // Lanes 1..31 of the producer and MMA warps wait here for their lane 0:
+    // parked in the cluster barrier instead, they starve lane 0's loop (its
+    // waits were observed microseconds late).
+    __syncwarp();
     // (launched after the split tail as its programmatic dependent: completing
     // only after the tail grid keeps the stream's order for later work)
     if (prm.split > 1) pdl_wait();
@@ -780,6 +839,7 @@ cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
     if (!y_map) my = mx;  // unused
     TcParams prm;
     prm.tma_store = y_map ? 1 : 0;
+    prm.push_vec = a.push && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.y_ld % 8 == 0 ? 1 : 0;
     prm.M = a.M;
     prm.N = a.N;
     prm.K = a.K;

@@ -440,22 +440,25 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t local, uint32_t rank) {
     return r;
 }
 
-// Arrive (release, cluster scope) on an mbarrier in another CTA of the cluster.
+// Arrive on an mbarrier in another CTA of the cluster (release at CTA scope,
+// the form cluster pipelines use: a cluster-scope release measured ~0.8 us
+// per arrival, blocking the issuing thread).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar)
-                 : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
 }
 
-// Wait with acquire at cluster scope (the phase may have been completed by
-// arrivals from the peer CTA).
+// Test (without suspending) with acquire at cluster scope: the phase may be
+// completed by arrivals from the peer CTA, which -- measured -- do not wake a
+// thread suspended in mbarrier.try_wait promptly (microseconds late), so
+// the waiter polls.
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+        : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     return ok != 0;
 }
