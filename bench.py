@@ -443,6 +443,38 @@ def time_moe(T, steps, warmup, world, seed, clocks=None):
     return max_over_ranks(total, world), byts, flops, clk
 
 
+def time_quant(steps, warmup, world, seed, pk):
+    """quantize (fp32 W -> codes + bf16 scales/biases, the MLX edge-snapped
+    scheme) and dequantize (codes + scales/biases -> bf16 W) of the prefill
+    weight [14336, 4096] at 4-bit g64.  Two rotating weight sets; every call
+    reads or writes more than L2.  Algorithmic bytes: what the call must read
+    and write once."""
+    import torch
+    import neurons_b200 as nb
+    rows, K = WORKLOADS["prefill"]["N"], WORKLOADS["prefill"]["K"]
+    g = torch.Generator(device="cuda").manual_seed(5000 + seed)
+    ws = [torch.randn(rows, K, device="cuda", generator=g) * 0.02 for _ in range(2)]
+    qs = [nb.quantize(w, GS, BITS, nb.SCHEME_MLX_AFFINE) for w in ws]
+    out_q = [tuple(torch.empty_like(t) for t in q) for q in qs]
+    out_w = torch.empty(rows, K, dtype=torch.bfloat16, device="cuda")
+    packed = rows * K * BITS // 8 + rows * (K // GS) * 4
+    res = {"workload": f"W [{rows},{K}], {BITS}-bit g{GS}"}
+    t = _events_time(lambda i: nb.dequantize(*qs[i % 2], GS, BITS, out=out_w), steps, warmup,
+                     world)
+    b = packed + rows * K * 2
+    res["dequantize"] = {"us_per_call": t / steps * 1e6, "gbs": b * steps / t / 1e9,
+                         "frac": b * steps / t / 1e9 / pk["hbm_gbs"],
+                         "algorithmic_bytes_per_call": b}
+    t = _events_time(lambda i: nb.quantize(ws[i % 2], GS, BITS, nb.SCHEME_MLX_AFFINE,
+                                           out=out_q[i % 2]), steps, warmup, world)
+    b = packed + rows * K * 4
+    res["quantize"] = {"us_per_call": t / steps * 1e6, "gbs": b * steps / t / 1e9,
+                       "frac": b * steps / t / 1e9 / pk["hbm_gbs"],
+                       "algorithmic_bytes_per_call": b}
+    assert nb.take_device_error() == 0
+    return res
+
+
 def moe_summary(T, t, steps, byts, flops, world, pk):
     sec = t / steps
     d = {"T": T, "us_per_step": sec * 1e6, "gbs": world * byts / sec / 1e9,
@@ -558,6 +590,41 @@ def time_ep(comm, T, steps, warmup, world, rank):
     return t
 
 
+def time_ep_fused(comm, T, steps, warmup, world, rank, arena_offset):
+    """time_ep with the dispatch and the combine as an all-to-all over NVLink
+    (peer stores into the symmetric arena) instead of NCCL collectives."""
+    import torch
+    import neurons_b200 as nb
+    from neurons_b200 import dist
+    E, k, H, I = (QWEN3_MOE[v] for v in ("E", "top_k", "H", "I"))
+    _, ne = dist.ep_shard(E, world, rank)
+    _, nt = dist.ep_token_shard(T, world, rank)
+    g = torch.Generator(device="cuda").manual_seed(2500 + rank)
+    sets = []
+    for _ in range(2):
+        W = []
+        for n, kk in ((I, H), (I, H), (H, I)):
+            w = torch.randn(ne, n, kk, device="cuda", generator=g) * 0.02
+            W.append(nb.quantize(w, GS, BITS, nb.SCHEME_MINMAX))
+            del w
+        x = torch.randn(nt, H, device="cuda", generator=g).to(torch.bfloat16)
+        logits = torch.randn(nt, E, device="cuda", generator=g).to(torch.bfloat16)
+        sets.append((x, logits, W))
+    ws = torch.empty(dist.ep_fused_workspace_size(T, E, k, H, I, world), dtype=torch.uint8,
+                     device="cuda")
+    y = torch.empty(nt, H, dtype=torch.bfloat16, device="cuda")
+
+    def step(i):
+        x, logits, W = sets[i % 2]
+        idx, sc = nb.moe_route(logits, k)
+        dist.ep_moe_switch_fused(comm, x, T, idx, sc, W[0], W[1], W[2], E, arena_offset, GS, BITS,
+                                 workspace=ws, out=y)
+
+    t = _events_time(step, steps, warmup, world)
+    assert nb.take_device_error() == 0 and comm.take_error() == 0
+    return t
+
+
 def time_tp_fused(comm, M, N, K, steps, warmup, world, rank, clocks=None):
     """time_tp with the all-gather fused into the kernel's stores (peer
     writes into the symmetric arena over NVLink)."""
@@ -636,11 +703,13 @@ def sharded_summary(world, rank, pk, single=None):
     from neurons_b200 import dist
     comm = dist.Comm()
     M0, N0 = WORKLOADS["prefill"]["M"], WORKLOADS["prefill"]["N"]
-    comm.symmetric_alloc(3 * ((M0 * N0 * 2 + 255) // 256 * 256))
+    ep_off = 3 * ((M0 * N0 * 2 + 255) // 256 * 256)
+    comm.symmetric_alloc(ep_off + dist.ep_fused_arena_size(2048, QWEN3_MOE["top_k"],
+                                                           QWEN3_MOE["H"], world))
     out = {"note": "strong scaling: total work fixed, split over the ranks; TP: NCCL all-gather "
                    "or the fused push (peer stores from the kernel), EP: NCCL all-gather + "
-                   "reduce-scatter; decode steps replayed from a CUDA graph; time = max over "
-                   "ranks"}
+                   "reduce-scatter, or the all-to-all over peer memory; decode steps replayed "
+                   "from a CUDA graph; time = max over ranks"}
     M, N, K = WORKLOADS["prefill"]["M"], WORKLOADS["prefill"]["N"], WORKLOADS["prefill"]["K"]
     n = 30
     t = time_tp(comm, M, N, K, n, 3, world, rank)
@@ -669,12 +738,18 @@ def sharded_summary(world, rank, pk, single=None):
                                        "split over ranks",
                            "us_per_step": t / n * 1e6,
                            "tflops": 2 * 2048 * k * 3 * I * H * n / t / 1e12}
+    t = time_ep_fused(comm, 2048, n, 3, world, rank, ep_off)
+    out["ep_moe_T2048_fused"] = {"workload": "as ep_moe_T2048, tokens dispatched to the ranks "
+                                             "holding their experts and partial sums returned by "
+                                             "peer stores over NVLink (all-to-all, no NCCL)",
+                                 "us_per_step": t / n * 1e6,
+                                 "tflops": 2 * 2048 * k * 3 * I * H * n / t / 1e12}
     comm.close()
     # strong-scaling efficiency against the single-GPU step timed in this run:
     # t(1 GPU) / (N * t(N GPUs))
     single = single or {}
     for key, ref in (("tp_prefill", "prefill_us"), ("tp_prefill_fused", "prefill_us"),
-                     ("ep_moe_T2048", "moe_T2048_us")):
+                     ("ep_moe_T2048", "moe_T2048_us"), ("ep_moe_T2048_fused", "moe_T2048_us")):
         if ref in single and key in out:
             out[key]["efficiency"] = single[ref] / (world * out[key]["us_per_step"])
             out[key]["single_gpu_us"] = single[ref]
@@ -684,7 +759,9 @@ def sharded_summary(world, rank, pk, single=None):
     # kernels per expert-parallel step.  NCCL's own kernels are not counted.
     import neurons_b200 as nb
     q = nb.quantized_matmul_launches(M, dist.tp_shard(N, world, rank)[1], K, GS, BITS)
-    launches = 30 * (q + 1) + 30 * (q + 2) + 200 + 200 * 3 + 10 * 9
+    # the all-to-all step: router, ready, dispatch, exchange, the shard's switch
+    # step (count, scan, fill, group_rows, gate/up, down, combine), combined, final
+    launches = 30 * (q + 1) + 30 * (q + 2) + 200 + 200 * 3 + 10 * 9 + 10 * 13
     return out, launches
 
 
@@ -879,6 +956,9 @@ def ours(args):
             line["gpu_launches"] += n * (4 if P <= QWEN3_MOE["E"] else
                                          (8 if P >= 8 * QWEN3_MOE["E"] else 7))
         line["moe"] = moe
+    if args.workload == "prefill" and not args.no_quant:
+        line["quant"] = time_quant(50, 3, world, rank, pk)
+        line["gpu_launches"] += 2 * 50
     if args.workload == "prefill" and not args.no_sharded:
         single = {"prefill_us": t_dev / args.steps * 1e6}
         if "moe" in line:
@@ -1046,6 +1126,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-lines")
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE sub-line")
+    ap.add_argument("--no-quant", action="store_true",
+                    help="skip the quantize/dequantize sub-line")
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the tensor/expert-parallel sub-line")
     ap.add_argument("--kernel-only", action="store_true",

@@ -216,6 +216,34 @@ int nq_moe_switch_partial(const uint16_t *x, int64_t T, int64_t H, int64_t I,
                           void *workspace, size_t workspace_bytes,
                           float *y_partial, void *stream);
 
+/* Where nq_moe_switch_partial_push writes its fp32 partial sums: the call's
+ * T tokens are nranks regions of rows_per_rank rows (T = nranks *
+ * rows_per_rank); token q * rows_per_rank + i goes to row dst_row0 + i of
+ * dst[q] (fp32, H per row; a peer mapping for another rank), and rows i >=
+ * count[q] (device memory, read when the kernel runs) are padding and are not
+ * written.  No counterpart in the reference: the combine step of the
+ * expert-parallel switch (nq_ep_moe_switch_fused, nq_dist.h). */
+typedef struct nq_rows_push {
+    int nranks;
+    int64_t rows_per_rank;
+    int64_t dst_row0;
+    const int32_t *count;
+    float *dst[NQ_MAX_RANKS];
+} nq_rows_push_t;
+
+/* nq_moe_switch_partial with the partial sums written through `push`
+ * instead of y_partial (same workspace size). */
+int nq_moe_switch_partial_push(const uint16_t *x, int64_t T, int64_t H, int64_t I,
+                               int64_t E, int64_t top_k, const int32_t *topk_idx,
+                               const float *topk_scores, int64_t e0, int64_t ne,
+                               const uint32_t *gate_w, const uint16_t *gate_s,
+                               const uint16_t *gate_b, const uint32_t *up_w,
+                               const uint16_t *up_s, const uint16_t *up_b,
+                               const uint32_t *down_w, const uint16_t *down_s,
+                               const uint16_t *down_b, int bits, int group_size,
+                               void *workspace, size_t workspace_bytes,
+                               const nq_rows_push_t *push, void *stream);
+
 /* nq_moe_switch without a workspace argument, for callers that cannot
  * allocate device memory themselves (an FFI host or a runtime that only
  * hands over the tensors it owns and exposes no allocator).  No counterpart

@@ -78,6 +78,12 @@ size_t nq_tp_workspace_size(int64_t M, int64_t N, int nranks);
 /* Workspace bytes of nq_ep_moe_switch for T tokens in total. */
 size_t nq_ep_workspace_size(int64_t T, int64_t E, int64_t top_k, int64_t H,
                             int64_t I, int nranks);
+/* Bytes of the symmetric arena that nq_ep_moe_switch_fused uses (its
+ * receive and return buffers), and of its local workspace.  0 when T or E is
+ * not a multiple of nranks. */
+size_t nq_ep_fused_arena_size(int64_t T, int64_t top_k, int64_t H, int nranks);
+size_t nq_ep_fused_workspace_size(int64_t T, int64_t E, int64_t top_k, int64_t H,
+                                  int64_t I, int nranks);
 
 /* ---- sharded calls (every rank calls, same shapes, same order) ---- */
 
@@ -119,6 +125,33 @@ int nq_ep_moe_switch(nq_comm_t comm, const uint16_t *x_shard, int64_t T,
                      const uint16_t *down_s, const uint16_t *down_b, int bits,
                      int group_size, void *workspace, size_t workspace_bytes,
                      uint16_t *y_shard, void *stream);
+
+/* nq_ep_moe_switch with the token exchange as an all-to-all over NVLink
+ * instead of an all-gather and a reduce-scatter, and no collective library
+ * call: each token row goes once to every rank that holds one of its
+ * experts (peer stores into that rank's receive buffer), each rank runs its
+ * experts over the rows it received and writes the fp32 partial sums
+ * straight back into the owners' return buffers, and each owner sums them
+ * in rank order and rounds to bf16.  Three bounded barriers on flags in the
+ * arena (ready, dispatched, combined; a timeout sets bit 0 of the error word
+ * and skips the remaining stores).  Same arguments and result as
+ * nq_ep_moe_switch, plus: the arena region at arena_offset (256-byte
+ * aligned, nq_ep_fused_arena_size bytes, the same offset on every rank) and
+ * a local workspace of nq_ep_fused_workspace_size bytes (256-byte aligned).
+ * Requires H % 8 == 0 and 16-byte aligned x, y and weights; every check runs
+ * before anything is enqueued. */
+int nq_ep_moe_switch_fused(nq_comm_t comm, const uint16_t *x_shard, int64_t T,
+                           int64_t H, int64_t I, int64_t E, int64_t top_k,
+                           const int32_t *topk_idx_shard,
+                           const float *topk_scores_shard,
+                           const uint32_t *gate_w, const uint16_t *gate_s,
+                           const uint16_t *gate_b, const uint32_t *up_w,
+                           const uint16_t *up_s, const uint16_t *up_b,
+                           const uint32_t *down_w, const uint16_t *down_s,
+                           const uint16_t *down_b, int bits, int group_size,
+                           size_t arena_offset, void *workspace,
+                           size_t workspace_bytes, uint16_t *y_shard,
+                           void *stream);
 
 #ifdef __cplusplus
 }

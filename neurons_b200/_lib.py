@@ -42,6 +42,8 @@ SIGNATURES = {
     "nq_quantized_matmul_push_check": (I, [P, I64, P, P, P, I64, I64, I, I, I64, I64, P]),
     "nq_moe_switch_partial": (I, [P, I64, I64, I64, I64, I64, P, P, I64, I64, P, P, P, P, P, P, P,
                                   P, P, I, I, P, U64, P, P]),
+    "nq_moe_switch_partial_push": (I, [P, I64, I64, I64, I64, I64, P, P, I64, I64, P, P, P, P, P, P,
+                                       P, P, P, I, I, P, U64, P, P]),
 }
 
 

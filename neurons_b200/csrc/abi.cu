@@ -390,7 +390,7 @@ static int moe_switch_checked(const char *what, const uint16_t *x, int64_t T, in
                               const uint16_t *up_b, const uint32_t *down_w, const uint16_t *down_s,
                               const uint16_t *down_b, int bits, int group_size, void *workspace,
                               size_t workspace_bytes, uint16_t *y, float *y_partial,
-                              void *stream) {
+                              void *stream, const nq::MoeRowsOut *rows_out = nullptr) {
     const std::string w(what);
     if (int rc = check_quant(I, H, bits, group_size, what)) return rc;
     if (int rc = check_quant(H, I, bits, group_size, what)) return rc;
@@ -402,7 +402,7 @@ static int moe_switch_checked(const char *what, const uint16_t *x, int64_t T, in
     if (T == 0) return NQ_SUCCESS;
     if (T * top_k > 65535 * 64) return fail(NQ_INVALID_INPUT, w + ": too many tokens for one call");
     if (!x || !topk_idx || !topk_scores || !gate_w || !gate_s || !gate_b || !up_w || !up_s ||
-        !up_b || !down_w || !down_s || !down_b || !(y || y_partial) || !workspace)
+        !up_b || !down_w || !down_s || !down_b || !(y || y_partial || rows_out) || !workspace)
         return fail(NQ_INVALID_INPUT, w + ": NULL pointer");
     const size_t need = nq::moe_partial_workspace_bytes(T, E, ne, top_k, H, I);
     if (workspace_bytes < need)
@@ -415,7 +415,7 @@ static int moe_switch_checked(const char *what, const uint16_t *x, int64_t T, in
     return from_cuda(nq::launch_moe_switch(x, T, H, I, E, top_k, topk_idx, topk_scores, e0, ne,
                                            gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s,
                                            down_b, bits, group_size, workspace, y, y_partial,
-                                           static_cast<cudaStream_t>(stream)),
+                                           static_cast<cudaStream_t>(stream), rows_out),
                      what);
 }
 
@@ -451,6 +451,38 @@ int nq_moe_switch_partial(const uint16_t *x, int64_t T, int64_t H, int64_t I, in
                               e0, ne, gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s,
                               down_b, bits, group_size, workspace, workspace_bytes, nullptr,
                               y_partial, stream);
+}
+
+int nq_moe_switch_partial_push(const uint16_t *x, int64_t T, int64_t H, int64_t I, int64_t E,
+                               int64_t top_k, const int32_t *topk_idx, const float *topk_scores,
+                               int64_t e0, int64_t ne, const uint32_t *gate_w,
+                               const uint16_t *gate_s, const uint16_t *gate_b, const uint32_t *up_w,
+                               const uint16_t *up_s, const uint16_t *up_b, const uint32_t *down_w,
+                               const uint16_t *down_s, const uint16_t *down_b, int bits,
+                               int group_size, void *workspace, size_t workspace_bytes,
+                               const nq_rows_push_t *push, void *stream) {
+    const char *what = "nq_moe_switch_partial_push";
+    if (!push) return fail(NQ_INVALID_INPUT, std::string(what) + ": NULL push");
+    if (push->nranks < 1 || push->nranks > NQ_MAX_RANKS || push->rows_per_rank <= 0 ||
+        push->rows_per_rank * push->nranks != T || push->dst_row0 < 0 || !push->count)
+        return fail(NQ_INVALID_INPUT,
+                    std::string(what) + ": need 1 <= nranks <= 8 regions of rows_per_rank rows "
+                                        "covering the T tokens, and counts");
+    nq::MoeRowsOut ro;
+    ro.n = push->nranks;
+    ro.per = push->rows_per_rank;
+    ro.row0 = push->dst_row0;
+    ro.count = push->count;
+    for (int q = 0; q < push->nranks; ++q) {
+        if (!push->dst[q] || !aligned16(push->dst[q]))
+            return fail(NQ_INVALID_INPUT,
+                        std::string(what) + ": every destination must be 16-byte aligned");
+        ro.dst[q] = push->dst[q];
+    }
+    return moe_switch_checked(what, x, T, H, I, E, top_k, topk_idx, topk_scores, e0, ne, gate_w,
+                              gate_s, gate_b, up_w, up_s, up_b, down_w, down_s, down_b, bits,
+                              group_size, workspace, workspace_bytes, nullptr, nullptr, stream,
+                              &ro);
 }
 
 }  // extern "C"

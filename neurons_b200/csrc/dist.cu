@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstring>
 #include <string>
 
@@ -20,8 +21,13 @@ constexpr size_t kArenaHeader = 4096;
 //   epoch (the fused calls made, advanced by the ready kernel) @ 448
 //   table of the ready-flag addresses this rank writes (one per rank) @ 512
 //   table of the done-flag addresses this rank writes (one per rank) @ 640
+//   expert-parallel flags: dispatched[8] @ 1024, combined[8] @ 1152, and the
+//   tables of the addresses this rank writes them to @ 1280 and @ 1408
 constexpr size_t kReadyOff = 0, kDoneOff = 128, kErrOff = 384,
-                 kEpochOff = 448, kTableOff = 512, kDoneTableOff = 640;
+                 kEpochOff = 448, kTableOff = 512, kDoneTableOff = 640,
+                 kDispOff = 1024, kCombOff = 1152, kDispTableOff = 1280, kCombTableOff = 1408;
+// bits of the arena's error word
+constexpr unsigned kCommErrTimeout = 1u;
 
 struct nq_comm_s {
     ncclComm_t nccl = nullptr;
@@ -76,16 +82,22 @@ int split(int64_t n, int nranks, int rank, int64_t *first, int64_t *count, const
     return NQ_SUCCESS;
 }
 
-// y[m, p * cols + j] = g[p][m][j]  (rank-major all-gather result -> row-major)
+// y[m, p * cols + j] = g[p][m][j]  (rank-major all-gather result -> row-major).
+// One CTA per (p, m) run of cols elements, moved in 16-byte pieces when the
+// run and both buffers allow it (cols % 8 == 0 and 16-byte aligned bases).
 __global__ void rank_major_to_rows(const uint16_t *__restrict__ g, int64_t M, int64_t cols,
-                                   int P, uint16_t *__restrict__ y) {
-    const int64_t total = (int64_t)P * M * cols;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t j = i % cols;
-        const int64_t m = (i / cols) % M;
-        const int64_t p = i / (cols * M);
-        y[m * cols * P + p * cols + j] = g[i];
+                                   int P, uint16_t *__restrict__ y, int vec) {
+    for (int64_t run = blockIdx.x; run < (int64_t)P * M; run += gridDim.x) {
+        const int64_t p = run / M, m = run % M;
+        const uint16_t *src = g + run * cols;
+        uint16_t *dst = y + m * cols * P + p * cols;
+        if (vec) {
+            const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
+            uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+            for (int64_t j = threadIdx.x; j < cols / 8; j += blockDim.x) d4[j] = s4[j];
+        } else {
+            for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) dst[j] = src[j];
+        }
     }
 }
 
@@ -191,6 +203,222 @@ cudaError_t launch_pdl_1warp(cudaStream_t st, void (*kern)(unsigned int *const *
     return cudaLaunchKernelEx(&cfg, kern, a, b, n, e, err);
 }
 
+// ---------------------------------------------------------------------------
+// Expert-parallel switch step with an all-to-all over peer memory.
+//
+// Rank r owns tokens [r * cap, (r + 1) * cap) (cap = T / P) and experts
+// [r * ne, (r + 1) * ne).  Each rank's EP region of the arena holds, for every
+// source rank q, the token rows q sent it and the partial results it gets back:
+//   recv_x   [P][cap][H] bf16    token rows, region q written by rank q
+//   recv_idx [P][cap][k] int32   their routing (all k slots, as routed)
+//   recv_sc  [P][cap][k] fp32
+//   recv_cnt [P]        int32    rows rank q sent (written by rank q)
+//   back     [P][cap][H] fp32    region d: rank d's partial sums for this
+//                                rank's tokens, at the rows this rank chose
+// A token goes once to every rank that holds at least one of its experts.
+// ---------------------------------------------------------------------------
+struct EpRegion {
+    size_t x = 0, idx = 0, sc = 0, cnt = 0, back = 0, bytes = 0;
+};
+
+EpRegion ep_region(int64_t cap, int64_t k, int64_t H, int P) {
+    EpRegion g;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = off;
+        off += align256(bytes);
+        return at;
+    };
+    g.x = take(sizeof(uint16_t) * P * cap * H);
+    g.idx = take(sizeof(int32_t) * P * cap * k);
+    g.sc = take(sizeof(float) * P * cap * k);
+    g.cnt = take(sizeof(int32_t) * P);
+    g.back = take(sizeof(float) * P * cap * H);
+    g.bytes = off;
+    return g;
+}
+
+struct EpPeers {
+    char *region[NQ_MAX_RANKS];  // every rank's EP region, mapped in this process
+};
+
+// this rank's local scratch: pos[cap][P] (row of token t in rank q's region q
+// of recv_x, -1: not sent), send_cnt[P], then the shard's switch workspace
+struct EpLocal {
+    int32_t *pos = nullptr, *send_cnt = nullptr;
+    void *sw = nullptr;
+    size_t sw_bytes = 0, bytes = 0;
+};
+
+EpLocal ep_local(void *base, int64_t T, int64_t E, int64_t k, int64_t H, int64_t I, int P) {
+    EpLocal l;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        char *p = static_cast<char *>(base) + off;
+        off += align256(bytes);
+        return p;
+    };
+    l.pos = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * (T / P) * P));
+    l.send_cnt = reinterpret_cast<int32_t *>(take(sizeof(int32_t) * P));
+    l.sw_bytes = nq_moe_partial_workspace_size(T, E, E / P, k, H, I);
+    l.sw = take(l.sw_bytes);
+    l.bytes = off;
+    return l;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long timer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait until flag >= epoch (wrapping compare); false on timeout.
+__device__ bool wait_flag(const unsigned *flag, unsigned epoch, unsigned *err) {
+    const unsigned long long t0 = timer_ns();
+    while ((int)(ld_acquire_sys_u32(flag) - epoch) < 0) {
+        if (timer_ns() - t0 > 2000000000ull) {
+            atomicOr(err, kCommErrTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
+// Dispatch: one warp per local token.  After every rank's ready flag reached
+// this call's number (their earlier calls no longer read their regions), the
+// token's destinations are the ranks of its valid slots; each takes the next
+// row of its region for this rank (atomic counter, so rows are in no fixed
+// order -- every row is computed on its own, so results do not depend on it),
+// and the warp writes the token's x row (16-byte stores) and routing there.
+__global__ void ep_dispatch_kernel(const uint16_t *__restrict__ x, const int32_t *__restrict__ idx,
+                                   const float *__restrict__ sc, int64_t cap, int64_t H, int k,
+                                   int E, int ne, int P, int rank, EpPeers peers, EpRegion rg,
+                                   int32_t *send_cnt, int32_t *pos, const unsigned *ready,
+                                   const unsigned *epoch_p, unsigned *err) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    if (warp >= cap) return;
+    int ok = 1;
+    if (lane == 0) {
+        const unsigned epoch = *epoch_p;
+        for (int q = 0; q < P && ok; ++q) ok = wait_flag(ready + q, epoch, err);
+    }
+    if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+    for (int64_t t = warp; t < cap; t += nwarps) {
+        const int e = lane < k ? idx[t * k + lane] : -1;
+        const float s = lane < k ? sc[t * k + lane] : 0.f;
+        const bool valid = lane < k && e >= 0 && e < E;
+        const unsigned mask = __reduce_or_sync(0xffffffffu, valid ? 1u << (e / ne) : 0u);
+        int p = -1;
+        if (lane < P && ((mask >> lane) & 1u)) p = atomicAdd(&send_cnt[lane], 1);
+        if (lane < P) pos[t * P + lane] = p;
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + t * H);
+        for (int q = 0; q < P; ++q) {
+            const int pq = __shfl_sync(0xffffffffu, p, q);
+            if (pq < 0) continue;
+            const int64_t row = (int64_t)rank * cap + pq;
+            uint4 *dx = reinterpret_cast<uint4 *>(peers.region[q] + rg.x) + row * (H / 8);
+            for (int64_t j = lane; j < H / 8; j += 32) dx[j] = src[j];
+            if (lane < k) {
+                // an out-of-range expert is passed on as it is: the receiver's
+                // switch step flags it in the device error word and skips it
+                reinterpret_cast<int32_t *>(peers.region[q] + rg.idx)[row * k + lane] = e;
+                reinterpret_cast<float *>(peers.region[q] + rg.sc)[row * k + lane] = s;
+            }
+        }
+    }
+}
+
+// After the dispatch grid: send every rank the number of rows written into
+// its region for this rank, publish this rank's dispatched flag everywhere,
+// wait (bounded) for every rank's, then mark the unused rows of every region
+// of this rank's own EP region as routed to e_pad with score 0 (an expert of
+// another rank, or with one rank a zero-weight slot) so that the switch step
+// skips or discards them.
+__global__ void ep_exchange_kernel(EpPeers peers, EpRegion rg, int P, int rank, int64_t cap, int k,
+                                   int e_pad, const int32_t *send_cnt,
+                                   unsigned int *const *disp_remote, const unsigned *disp_local,
+                                   const unsigned *epoch_p, unsigned *err) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    __shared__ int ok;
+    const int q = threadIdx.x;
+    const unsigned epoch = *epoch_p;
+    if (q == 0) ok = 1;
+    if (q < P) reinterpret_cast<int32_t *>(peers.region[q] + rg.cnt)[rank] = send_cnt[q];
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    if (q < P)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(disp_remote[q]), "r"(epoch)
+                     : "memory");
+    __syncthreads();
+    if (q < P && !wait_flag(disp_local + q, epoch, err)) ok = 0;
+    __syncthreads();
+    if (!ok) return;
+    char *mine = peers.region[rank];
+    const int32_t *cnt = reinterpret_cast<const int32_t *>(mine + rg.cnt);
+    int32_t *ridx = reinterpret_cast<int32_t *>(mine + rg.idx);
+    float *rsc = reinterpret_cast<float *>(mine + rg.sc);
+    const int64_t n = (int64_t)P * cap * k;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const int64_t row = i / k;
+        if (row % cap >= cnt[row / cap]) {
+            ridx[i] = e_pad;
+            rsc[i] = 0.f;
+        }
+    }
+}
+
+// y[t] = bf16(sum over ranks d = 0..P-1 that computed for token t of their
+// partial sums), in that order.
+__global__ void ep_final_kernel(const float *__restrict__ back, const int32_t *__restrict__ pos,
+                                int64_t cap, int64_t H, int P, uint16_t *__restrict__ y) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over cap * H / 4
+    if (i >= cap * (H / 4)) return;
+    const int64_t t = i / (H / 4), n = (i % (H / 4)) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int d = 0; d < P; ++d) {
+        const int p = pos[t * P + d];
+        if (p < 0) continue;
+        const float4 v = *reinterpret_cast<const float4 *>(back + ((int64_t)d * cap + p) * H + n);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+    }
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+    const __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t *>(&lo);
+    o.y = *reinterpret_cast<const uint32_t *>(&hi);
+    *reinterpret_cast<uint2 *>(y + t * H + n) = o;
+}
+
+template <typename... Args>
+cudaError_t launch_pdl_k(void (*kern)(Args...), unsigned blocks, unsigned threads, cudaStream_t st,
+                         Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(threads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 unsigned grid_for(int64_t n) {
     const int64_t b = (n + 255) / 256;
     return (unsigned)(b < 148 * 16 ? (b > 0 ? b : 1) : 148 * 16);
@@ -269,7 +497,7 @@ int nq_comm_symmetric_alloc(nq_comm_t comm, size_t bytes) {
     if (int rc = from_cuda(cudaMalloc(&base, kArenaHeader + bytes), what)) return rc;
     cudaIpcMemHandle_t *all = nullptr;
     cudaIpcMemHandle_t mine;
-    int rc = from_cuda(cudaMemset(base, 0, kArenaHeader), what);
+    int rc = from_cuda(cudaMemset(base, 0, kArenaHeader + bytes), what);
     if (!rc) rc = from_cuda(cudaIpcGetMemHandle(&mine, base), what);
     // every rank's handle, through the communicator
     void *dev = nullptr;
@@ -310,6 +538,19 @@ int nq_comm_symmetric_alloc(nq_comm_t comm, size_t bytes) {
             done_dst[q] = reinterpret_cast<unsigned int *>(comm->peer[q] + kDoneOff) + comm->rank;
         if (!rc)
             rc = from_cuda(cudaMemcpy(base + kDoneTableOff, done_dst, sizeof(void *) * comm->size,
+                                      cudaMemcpyHostToDevice),
+                           what);
+        unsigned int *disp_dst[NQ_MAX_RANKS], *comb_dst[NQ_MAX_RANKS];
+        for (int q = 0; q < comm->size; ++q) {
+            disp_dst[q] = reinterpret_cast<unsigned int *>(comm->peer[q] + kDispOff) + comm->rank;
+            comb_dst[q] = reinterpret_cast<unsigned int *>(comm->peer[q] + kCombOff) + comm->rank;
+        }
+        if (!rc)
+            rc = from_cuda(cudaMemcpy(base + kDispTableOff, disp_dst, sizeof(void *) * comm->size,
+                                      cudaMemcpyHostToDevice),
+                           what);
+        if (!rc)
+            rc = from_cuda(cudaMemcpy(base + kCombTableOff, comb_dst, sizeof(void *) * comm->size,
                                       cudaMemcpyHostToDevice),
                            what);
     }
@@ -458,7 +699,11 @@ int nq_tp_quantized_matmul(nq_comm_t comm, const uint16_t *x, int64_t M, const u
     if (int rc = from_nccl(
             ncclAllGather(mine, g, (size_t)(M * rows), ncclBfloat16, comm->nccl, st), what))
         return rc;
-    rank_major_to_rows<<<grid_for(M * N), 256, 0, st>>>(g, M, rows, P, y);
+    const int vec = rows % 8 == 0 && !(reinterpret_cast<uintptr_t>(g) & 15) &&
+                    !(reinterpret_cast<uintptr_t>(y) & 15);
+    const int64_t runs = (int64_t)P * M;
+    rank_major_to_rows<<<(unsigned)std::min<int64_t>(runs, 148 * 8), 128, 0, st>>>(g, M, rows, P,
+                                                                                   y, vec);
     return from_cuda(cudaGetLastError(), what);
 }
 
@@ -504,6 +749,133 @@ int nq_ep_moe_switch(nq_comm_t comm, const uint16_t *x_shard, int64_t T, int64_t
         return rc;
     f32_to_bf16_kernel<<<grid_for(nt * H), 256, 0, st>>>(w.mine, nt * H, y_shard);
     return from_cuda(cudaGetLastError(), what);
+}
+
+size_t nq_ep_fused_arena_size(int64_t T, int64_t top_k, int64_t H, int nranks) {
+    if (T <= 0 || top_k <= 0 || H <= 0 || nranks <= 0 || nranks > NQ_MAX_RANKS || T % nranks)
+        return 0;
+    return ep_region(T / nranks, top_k, H, nranks).bytes;
+}
+
+size_t nq_ep_fused_workspace_size(int64_t T, int64_t E, int64_t top_k, int64_t H, int64_t I,
+                                  int nranks) {
+    if (T <= 0 || E <= 0 || top_k <= 0 || H <= 0 || I <= 0 || nranks <= 0 ||
+        nranks > NQ_MAX_RANKS || T % nranks || E % nranks)
+        return 0;
+    return ep_local(nullptr, T, E, top_k, H, I, nranks).bytes;
+}
+
+int nq_ep_moe_switch_fused(nq_comm_t comm, const uint16_t *x_shard, int64_t T, int64_t H,
+                           int64_t I, int64_t E, int64_t top_k, const int32_t *topk_idx_shard,
+                           const float *topk_scores_shard, const uint32_t *gate_w,
+                           const uint16_t *gate_s, const uint16_t *gate_b, const uint32_t *up_w,
+                           const uint16_t *up_s, const uint16_t *up_b, const uint32_t *down_w,
+                           const uint16_t *down_s, const uint16_t *down_b, int bits,
+                           int group_size, size_t arena_offset, void *workspace,
+                           size_t workspace_bytes, uint16_t *y_shard, void *stream) {
+    const char *what = "nq_ep_moe_switch_fused";
+    if (!comm) return fail(NQ_INVALID_INPUT, std::string(what) + ": NULL communicator");
+    if (!comm->arena)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": call nq_comm_symmetric_alloc first");
+    const int P = comm->size, rank = comm->rank;
+    int64_t e0, ne, t0, cap;
+    if (int rc = split(E, P, rank, &e0, &ne, what)) return rc;
+    if (int rc = split(T, P, rank, &t0, &cap, what)) return rc;
+    // Every check runs before anything is enqueued; with the same shapes on
+    // every rank they agree, so no rank starts a call the others reject.
+    if (!x_shard || !topk_idx_shard || !topk_scores_shard || !y_shard || !workspace || !gate_w ||
+        !gate_s || !gate_b || !up_w || !up_s || !up_b || !down_w || !down_s || !down_b)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": NULL pointer");
+    if (top_k <= 0 || top_k > 32 || top_k > E || E > 1024 || H % 8 || H <= 0 || I <= 0)
+        return fail(NQ_INVALID_INPUT,
+                    std::string(what) + ": need 0 < top_k <= min(E, 32), E <= 1024, H % 8 == 0");
+    if ((bits != 4 && bits != 8) || (group_size != 32 && group_size != 64 && group_size != 128) ||
+        H % group_size || I % group_size)
+        return fail(NQ_INVALID_INPUT,
+                    std::string(what) + ": bits 4 or 8, group size 32/64/128 dividing H and I");
+    const uintptr_t a16 = reinterpret_cast<uintptr_t>(x_shard) |
+                          reinterpret_cast<uintptr_t>(y_shard) |
+                          reinterpret_cast<uintptr_t>(gate_w) | reinterpret_cast<uintptr_t>(up_w) |
+                          reinterpret_cast<uintptr_t>(down_w);
+    if (a16 & 15)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": x, y and weights must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": workspace must be 256-byte aligned");
+    const size_t need = nq_ep_fused_workspace_size(T, E, top_k, H, I, P);
+    if (need == 0 || workspace_bytes < need)
+        return fail(NQ_INVALID_INPUT,
+                    std::string(what) + ": workspace too small: need " + std::to_string(need));
+    const EpRegion rg = ep_region(cap, top_k, H, P);
+    if (arena_offset % 256 || arena_offset + rg.bytes > comm->arena_bytes)
+        return fail(NQ_INVALID_INPUT,
+                    std::string(what) + ": the EP region (nq_ep_fused_arena_size bytes at a "
+                                        "256-byte aligned offset) must lie in the arena");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    EpLocal loc = ep_local(workspace, T, E, top_k, H, I, P);
+    EpPeers peers;
+    for (int q = 0; q < NQ_MAX_RANKS; ++q)
+        peers.region[q] = q < P ? comm->peer[q] + kArenaHeader + arena_offset : nullptr;
+    unsigned int *epoch = reinterpret_cast<unsigned int *>(comm->arena + kEpochOff);
+    unsigned int *err = reinterpret_cast<unsigned int *>(comm->arena + kErrOff);
+    const int e_pad = P > 1 ? (int)((e0 + ne) % E) : 0;
+
+    if (int rc = from_cuda(cudaMemsetAsync(loc.send_cnt, 0, sizeof(int32_t) * P, st), what))
+        return rc;
+    // ready: this rank's earlier stream work (which read its region) is done
+    if (int rc = from_cuda(launch_pdl_k(push_ready_kernel, 1, 32, st,
+                                        reinterpret_cast<unsigned int *const *>(comm->arena +
+                                                                                kTableOff),
+                                        P, epoch),
+                           what))
+        return rc;
+    const unsigned dblocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>((cap + 7) / 8, 148 * 4));
+    if (int rc = from_cuda(
+            launch_pdl_k(ep_dispatch_kernel, dblocks, 256, st, x_shard, topk_idx_shard,
+                         topk_scores_shard, cap, H, (int)top_k, (int)E, (int)ne, P, rank, peers, rg,
+                         loc.send_cnt, loc.pos,
+                         reinterpret_cast<const unsigned *>(comm->arena + kReadyOff),
+                         (const unsigned *)epoch, err),
+            what))
+        return rc;
+    if (int rc = from_cuda(
+            launch_pdl_k(ep_exchange_kernel, 1, 256, st, peers, rg, P, rank, cap, (int)top_k,
+                         e_pad, (const int32_t *)loc.send_cnt,
+                         reinterpret_cast<unsigned int *const *>(comm->arena + kDispTableOff),
+                         reinterpret_cast<const unsigned *>(comm->arena + kDispOff),
+                         (const unsigned *)epoch, err),
+            what))
+        return rc;
+    // this rank's experts over every row it received; the partial sums go
+    // straight back into the token owners' regions
+    nq_rows_push_t push;
+    std::memset(&push, 0, sizeof(push));
+    push.nranks = P;
+    push.rows_per_rank = cap;
+    push.dst_row0 = (int64_t)rank * cap;
+    push.count = reinterpret_cast<const int32_t *>(peers.region[rank] + rg.cnt);
+    for (int q = 0; q < P; ++q) push.dst[q] = reinterpret_cast<float *>(peers.region[q] + rg.back);
+    char *mine = peers.region[rank];
+    if (int rc = from_nq(nq_moe_switch_partial_push(
+                             reinterpret_cast<const uint16_t *>(mine + rg.x), T, H, I, E, top_k,
+                             reinterpret_cast<const int32_t *>(mine + rg.idx),
+                             reinterpret_cast<const float *>(mine + rg.sc), e0, ne, gate_w, gate_s,
+                             gate_b, up_w, up_s, up_b, down_w, down_s, down_b, bits, group_size,
+                             loc.sw, loc.sw_bytes, &push, stream),
+                         what))
+        return rc;
+    // combined: every rank's partial sums for this rank's tokens have arrived
+    if (int rc = from_cuda(
+            launch_pdl_1warp(st, push_finish_kernel,
+                             reinterpret_cast<unsigned int *const *>(comm->arena + kCombTableOff),
+                             reinterpret_cast<const unsigned int *>(comm->arena + kCombOff), P,
+                             epoch, err),
+            what))
+        return rc;
+    const int64_t n4 = cap * (H / 4);
+    return from_cuda(launch_pdl_k(ep_final_kernel, (unsigned)((n4 + 255) / 256), 256, st,
+                                  reinterpret_cast<const float *>(mine + rg.back),
+                                  (const int32_t *)loc.pos, cap, H, P, y_shard),
+                     what);
 }
 
 }  // extern "C"

@@ -162,17 +162,26 @@ __global__ void group_rows_kernel(const uint16_t *__restrict__ x, int64_t H,
 
 // sum_j bf16(score[t, j]) * d[t*k + j, n] over the slots j routed to experts
 // [e0, e0 + ne), slot order 0..k-1; y gets it rounded to bf16, or y_partial
-// gets the fp32 sum (the share of one expert shard)
+// gets the fp32 sum (the share of one expert shard), or -- with ro.n > 0 --
+// the fp32 sum goes to rank q's buffer ro.dst[q] at row ro.row0 + i for the
+// token t = q * ro.per + i, rows i >= ro.count[q] being skipped (the
+// expert-parallel combine, written straight into the token owners' memory)
 __global__ void combine_kernel(const float *__restrict__ d, const float *__restrict__ scores,
                                const int32_t *__restrict__ idx, int e0, int ne, int64_t T,
                                int64_t H, int top_k, uint16_t *__restrict__ y,
-                               float *__restrict__ y_partial) {
+                               float *__restrict__ y_partial, const MoeRowsOut ro) {
     pdl_launch_dependents();
     pdl_wait();  // d comes from the down projection
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over T * H / 4
     if (i >= T * (H / 4)) return;
     const int64_t t = i / (H / 4);
     const int64_t n = (i % (H / 4)) * 4;
+    float *ro_dst = nullptr;
+    if (ro.n > 0) {
+        const int64_t q = t / ro.per, r = t % ro.per;
+        if (r >= ro.count[q]) return;
+        ro_dst = ro.dst[q] + (ro.row0 + r) * H + n;
+    }
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int j = 0; j < top_k; ++j) {
         const int l = idx[t * top_k + j] - e0;
@@ -183,6 +192,10 @@ __global__ void combine_kernel(const float *__restrict__ d, const float *__restr
         acc.y = __fmaf_rn(sc, v.y, acc.y);
         acc.z = __fmaf_rn(sc, v.z, acc.z);
         acc.w = __fmaf_rn(sc, v.w, acc.w);
+    }
+    if (ro_dst) {
+        *reinterpret_cast<float4 *>(ro_dst) = acc;
+        return;
     }
     if (y_partial) {
         *reinterpret_cast<float4 *>(y_partial + t * H + n) = acc;
@@ -298,15 +311,16 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
                               const uint16_t *gb, const uint32_t *uw, const uint16_t *us,
                               const uint16_t *ub, const uint32_t *dw, const uint16_t *ds,
                               const uint16_t *db, int bits, int gsz, void *workspace, uint16_t *y,
-                              float *y_partial, cudaStream_t stream) {
+                              float *y_partial, cudaStream_t stream, const MoeRowsOut *rows_out) {
     if (T == 0) return cudaSuccess;
+    const MoeRowsOut ro = rows_out ? *rows_out : MoeRowsOut{};
     const int64_t P = T * top_k;
     MoeWorkspace ws = carve(workspace, T, E, top_k, H, I, E_total);
     unsigned int *err = device_error_word();
     const int thr = 256;
     const unsigned pblocks = (unsigned)((P + thr - 1) / thr);
     // a shard always groups (pairs of other shards are skipped while grouping)
-    const bool grouped = P > E || y_partial != nullptr;
+    const bool grouped = P > E || y_partial != nullptr || ro.n > 0;
     // Tensor-core path once experts average >= 8 tokens (tc_pairs); below
     // that the grouped GEMV streams each expert's weights once.
     const bool use_tc =
@@ -377,7 +391,7 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
             d.y_ld = H;
             if ((e = launch_tc_moe(d, stream)) != cudaSuccess) return e;
             return launch_pdl(combine_kernel, cblocks, thr, stream, (const float *)ws.d, scores, idx,
-                              (int)e0, (int)E, T, H, (int)top_k, y, y_partial);
+                              (int)e0, (int)E, T, H, (int)top_k, y, y_partial, ro);
         }
         // gate/up: problem = expert, its tokens gathered from x, h rows in grouped order
         up.P = (int)E;
@@ -415,7 +429,7 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
     if ((e = launch_gemv(up, stream)) != cudaSuccess) return e;
     if ((e = launch_gemv(dn, stream)) != cudaSuccess) return e;
     return launch_pdl(combine_kernel, cblocks, thr, stream, (const float *)ws.d, scores, idx,
-                      (int)e0, (int)E, T, H, (int)top_k, y, y_partial);
+                      (int)e0, (int)E, T, H, (int)top_k, y, y_partial, ro);
 }
 
 }  // namespace nq

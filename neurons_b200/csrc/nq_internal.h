@@ -133,15 +133,28 @@ cudaError_t launch_dequantize(const uint32_t *wq, const uint16_t *s, const uint1
 size_t moe_workspace_bytes(int64_t T, int64_t E, int64_t top_k, int64_t H, int64_t I);
 size_t moe_partial_workspace_bytes(int64_t T, int64_t E, int64_t ne, int64_t top_k, int64_t H,
                                    int64_t I);
+// Where the switch step of one expert shard writes its fp32 partial sums when
+// they go straight to the tokens' owners: the call's tokens are n regions of
+// `per` rows; token q * per + i goes to row row0 + i of dst[q] (rows i >=
+// count[q] are padding and are not written).  n == 0: not used.
+struct MoeRowsOut {
+    int n = 0;
+    int64_t per = 0, row0 = 0;
+    const int32_t *count = nullptr;  // [n], device memory
+    float *dst[8] = {};
+};
+
 // The switch step for experts [e0, e0 + ne) of E_total (weights: those ne
-// experts).  y: bf16 result (all experts); y_partial: fp32 partial sums.
+// experts).  y: bf16 result (all experts); y_partial: fp32 partial sums;
+// rows_out (non-null, n > 0): fp32 partial sums into other ranks' buffers.
 cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I, int64_t E_total,
                               int64_t top_k, const int32_t *idx, const float *scores, int64_t e0,
                               int64_t ne, const uint32_t *gw, const uint16_t *gs_,
                               const uint16_t *gb, const uint32_t *uw, const uint16_t *us,
                               const uint16_t *ub, const uint32_t *dw, const uint16_t *ds,
                               const uint16_t *db, int bits, int gsz, void *workspace, uint16_t *y,
-                              float *y_partial, cudaStream_t stream);
+                              float *y_partial, cudaStream_t stream,
+                              const MoeRowsOut *rows_out = nullptr);
 
 cudaError_t launch_moe_route(const uint16_t *logits, int64_t T, int64_t E, int64_t top_k,
                              int32_t *idx, float *scores, cudaStream_t stream);

@@ -53,6 +53,10 @@ SIGNATURES = {
     "nq_tp_quantized_matmul": (I, [P, P, I64, P, P, P, I64, I64, I, I, P, P, U64, P]),
     "nq_ep_moe_switch": (I, [P, P, I64, I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, P, I,
                              I, P, U64, P, P]),
+    "nq_ep_fused_arena_size": (U64, [I64, I64, I64, I]),
+    "nq_ep_fused_workspace_size": (U64, [I64, I64, I64, I64, I64, I]),
+    "nq_ep_moe_switch_fused": (I, [P, P, I64, I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, P,
+                                   I, I, U64, P, U64, P, P]),
 }
 
 _dist_lib = None
@@ -108,6 +112,14 @@ def tp_workspace_size(M, N, nranks):
 
 def ep_workspace_size(T, E, top_k, H, I_, nranks):
     return int(dist_lib().nq_ep_workspace_size(T, E, top_k, H, I_, nranks))
+
+
+def ep_fused_arena_size(T, top_k, H, nranks):
+    return int(dist_lib().nq_ep_fused_arena_size(T, top_k, H, nranks))
+
+
+def ep_fused_workspace_size(T, E, top_k, H, I_, nranks):
+    return int(dist_lib().nq_ep_fused_workspace_size(T, E, top_k, H, I_, nranks))
 
 
 class Comm:
@@ -239,4 +251,28 @@ def ep_moe_switch(comm, x_shard, T, idx_shard, scores_shard, gate, up, down, E, 
         _ptr(gate[0]), _ptr(gate[1]), _ptr(gate[2]), _ptr(up[0]), _ptr(up[1]), _ptr(up[2]),
         _ptr(down[0]), _ptr(down[1]), _ptr(down[2]), bits, group_size, _ptr(workspace),
         workspace.numel(), _ptr(out), ops._stream()))
+    return out
+
+
+def ep_moe_switch_fused(comm, x_shard, T, idx_shard, scores_shard, gate, up, down, E,
+                        arena_offset, group_size=64, bits=4, workspace=None, out=None):
+    """ep_moe_switch with the token dispatch and the combine as an all-to-all
+    over NVLink (peer stores into the symmetric arena region at arena_offset,
+    ep_fused_arena_size bytes) instead of NCCL collectives."""
+    ops._need(x_shard, "x", (torch.bfloat16,))
+    H = int(x_shard.shape[1])
+    top_k = int(idx_shard.shape[1])
+    I_ = int(gate[0].shape[1])
+    need = ep_fused_workspace_size(T, E, top_k, H, I_, comm.size)
+    if need == 0:
+        raise NQError(1, "ep_moe_switch_fused: T and E must be multiples of the number of ranks")
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x_shard.device)
+    if out is None:
+        out = torch.empty_like(x_shard)
+    _check(dist_lib().nq_ep_moe_switch_fused(
+        comm.handle, _ptr(x_shard), T, H, I_, E, top_k, _ptr(idx_shard), _ptr(scores_shard),
+        _ptr(gate[0]), _ptr(gate[1]), _ptr(gate[2]), _ptr(up[0]), _ptr(up[1]), _ptr(up[2]),
+        _ptr(down[0]), _ptr(down[1]), _ptr(down[2]), bits, group_size, arena_offset,
+        _ptr(workspace), workspace.numel(), _ptr(out), ops._stream()))
     return out

@@ -56,14 +56,21 @@ def bits(w, s, gs):
     return lib().nq_bits_from_shapes(int(w.shape[-1]), int(s.shape[-1]), int(gs))
 
 
-def quantize(w, group_size=64, bits=4, scheme=SCHEME_MLX_AFFINE):
+def quantize(w, group_size=64, bits=4, scheme=SCHEME_MLX_AFFINE, out=None):
+    """MLX affine quantize along the last axis; out: optional (wq, scales, biases)."""
     _need(w, "w", (torch.float32, torch.bfloat16))
     K = int(w.shape[-1])
     rows = w.numel() // K if K else 0
     lead = tuple(w.shape[:-1])
-    wq = torch.empty(lead + (K * bits // 32,), dtype=torch.uint32, device=w.device)
-    s = torch.empty(lead + (K // group_size,), dtype=torch.bfloat16, device=w.device)
-    b = torch.empty_like(s)
+    if out is None:
+        wq = torch.empty(lead + (K * bits // 32,), dtype=torch.uint32, device=w.device)
+        s = torch.empty(lead + (K // group_size,), dtype=torch.bfloat16, device=w.device)
+        b = torch.empty_like(s)
+    else:
+        wq, s, b = out
+        _need(wq, "wq", _PACKED)
+        _need(s, "scales", (torch.bfloat16,))
+        _need(b, "biases", (torch.bfloat16,))
     dt = 0 if w.dtype == torch.float32 else 1
     check(lib().nq_quantize(_ptr(w), dt, rows, K, bits, group_size, scheme, _ptr(wq), _ptr(s),
                             _ptr(b), _stream()))
@@ -143,9 +150,13 @@ def lin(x, key, wm, gs, out=None):
     w = wm[key + ".weight"]
     s = wm.get(key + ".scales")
     if s is None:
-        # the C++ cuda_ops::lin serves unquantized layers through cuBLAS; this
-        # mirror covers the quantized entry points only
-        raise NQError(2, f"{key}: unquantized weights: use cuda_ops::lin (C++) for them")
+        # unquantized layer: matmul(x, w^T) as mlx_ops.h:41 does (a library GEMM,
+        # as in the C++ cuda_ops::lin)
+        _need(x, "x", (torch.bfloat16,))
+        _need(w, "w", (torch.bfloat16,))
+        if out is None:
+            return torch.matmul(x, w.t())
+        return torch.matmul(x, w.t(), out=out)
     b = wm.get(key + ".biases")
     return quantized_matmul(x, w, s, b, True, gs, bits(w, s, gs), out=out)
 

@@ -192,3 +192,79 @@ def test_expert_parallel_plan_two_gloo_ranks(dlib):
     for r, err in out.items():
         assert isinstance(err, float), err
         assert err < 1e-2, (r, err)
+
+
+def _ep_a2a_rank(rank, world, T, E, k, H, I):
+    """The data flow of nq_ep_moe_switch_fused with the oracle doing the
+    arithmetic: each token goes once to every rank holding one of its experts
+    (rows of region `rank` of that rank's receive buffer, padding rows routed
+    to an expert of another rank with score 0), each rank computes its
+    experts' partial sums over the rows it received and returns them to the
+    owners, and each owner sums them in rank order."""
+    import torch
+    import torch.distributed as tdist
+    from oracle import oracle as O
+    from neurons_b200 import dist
+    rng = np.random.default_rng(23)
+
+    def experts(rows, cols):
+        wq, s, b = O.quantize((rng.standard_normal((E * rows, cols)) * 0.02).astype(np.float32),
+                              4, 32, 0)
+        return wq.reshape(E, rows, -1), s.reshape(E, rows, -1), b.reshape(E, rows, -1)
+
+    gate, up, down = experts(I, H), experts(I, H), experts(H, I)
+    x = O.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
+    idx, sc = O.moe_route(O.f32_to_bf16(rng.standard_normal((T, E)).astype(np.float32)), k)
+    t0, cap = dist.ep_token_shard(T, world, rank)
+    e0, ne = dist.ep_shard(E, world, rank)
+    # dispatch plan: pos[t][d] = row of token t in rank d's region for this rank
+    pos = -np.ones((cap, world), np.int64)
+    cnt = np.zeros(world, np.int64)
+    send_x = np.zeros((world, cap, H), np.int32)
+    send_idx = np.zeros((world, cap, k), np.int32)
+    send_sc = np.zeros((world, cap, k), np.float32)
+    for t in range(cap):
+        for d in sorted({int(e) // ne for e in idx[t0 + t]}):
+            pos[t, d] = cnt[d]
+            send_x[d, cnt[d]] = x[t0 + t]
+            send_idx[d, cnt[d]] = idx[t0 + t]
+            send_sc[d, cnt[d]] = sc[t0 + t]
+            cnt[d] += 1
+
+    def exchange(a, dtype):
+        """a [P][...] on every rank -> b [P][...] with b[q] = rank q's a[rank]."""
+        parts = [torch.empty(a.shape, dtype=dtype) for _ in range(world)]
+        tdist.all_gather(parts, torch.from_numpy(np.ascontiguousarray(a)))
+        return np.stack([p.numpy()[rank] for p in parts])
+
+    recv_x = exchange(send_x, torch.int32).astype(np.uint16).reshape(world * cap, H)
+    recv_idx = exchange(send_idx, torch.int32).reshape(world * cap, k)
+    recv_sc = exchange(send_sc, torch.float32).reshape(world * cap, k)
+    recv_cnt = exchange(cnt[:, None].astype(np.int32), torch.int32)[:, 0]
+    e_pad = (e0 + ne) % E
+    for q in range(world):
+        recv_idx[q * cap + recv_cnt[q]:(q + 1) * cap] = e_pad
+        recv_sc[q * cap + recv_cnt[q]:(q + 1) * cap] = 0
+    # this rank's experts over the received rows
+    local = (recv_idx >= e0) & (recv_idx < e0 + ne)
+    h = O.moe_hidden(recv_x, recv_idx, gate, up, 4, 32, rounding=1)
+    part = O.bf16_to_f32(O.moe_combine(h, recv_idx, np.where(local, recv_sc, 0).astype(np.float32),
+                                       down, 4, 32, rounding=1)).astype(np.float32)
+    # combine: region q of the partials goes back to rank q; sum in rank order
+    back = exchange(part.reshape(world, cap, H), torch.float32)  # back[d] = rank d's rows for us
+    y = np.zeros((cap, H), np.float32)
+    for d in range(world):
+        for t in range(cap):
+            if pos[t, d] >= 0:
+                y[t] += back[d, pos[t, d]]
+    ref = O.bf16_to_f32(O.moe_switch(x, idx, sc, gate, up, down, 4, 32, rounding=1))[t0:t0 + cap]
+    size_ok = dist.ep_fused_arena_size(T, k, H, world) >= world * cap * H * 6
+    return float(np.linalg.norm(y - ref) / np.linalg.norm(ref)) if size_ok else "arena size"
+
+
+def test_expert_parallel_all_to_all_plan_two_gloo_ranks(dlib):
+    out = _run_ranks("_ep_a2a_rank", 6, 8, 2, 64, 32)
+    assert set(out) == {0, 1}
+    for r, err in out.items():
+        assert isinstance(err, float), err
+        assert err < 1e-2, (r, err)

@@ -1,6 +1,7 @@
 """Two ranks over NCCL (one process per GPU): the tensor-parallel linear and
-the expert-parallel switch step through libnq_dist.so's C ABI, against the
-single-GPU calls on the same seeded inputs.  Needs two GPUs; skipped with one."""
+the expert-parallel switch step (NCCL collectives, and the all-to-all over
+peer memory) through libnq_dist.so's C ABI, against the single-GPU calls on
+the same seeded inputs.  Needs two GPUs; skipped with one."""
 import os
 import socket
 
@@ -69,6 +70,16 @@ def _worker(rank, world, port, q):
                                    loc(gate), loc(up), loc(down), E)
             torch.cuda.synchronize()
             out[f"ep{T}"] = (_rel(y, ref[t0:t0 + nt]), True)
+            # the all-to-all over NVLink; three calls on the same arena region
+            off = 4 << 20
+            assert off + dist.ep_fused_arena_size(T, k, H, world) <= 8 << 20
+            for _ in range(3):
+                yf = dist.ep_moe_switch_fused(comm, x[t0:t0 + nt].contiguous(), T,
+                                              idx[t0:t0 + nt].contiguous(),
+                                              sc[t0:t0 + nt].contiguous(), loc(gate), loc(up),
+                                              loc(down), E, off)
+            torch.cuda.synchronize()
+            out[f"epf{T}"] = (_rel(yf, ref[t0:t0 + nt]), float((yf.float() - y.float()).abs().max()))
         out["device_error"] = (float(nb.take_device_error()), True)
         out["comm_error"] = (float(comm.take_error()), True)
         comm.close()
@@ -101,5 +112,5 @@ def test_two_rank_tensor_and_expert_parallel():
         for key in ("tp1", "tp7", "tp300"):
             rel, same_cols = out[key]
             assert rel < 1e-2 and same_cols, (r, key, out[key])
-        for key in ("ep64", "ep512"):
+        for key in ("ep64", "ep512", "epf64", "epf512"):
             assert out[key][0] < 1e-2, (r, key, out[key])

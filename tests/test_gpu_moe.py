@@ -8,7 +8,7 @@ import pytest
 import torch
 
 from _util import (acts, assert_close, dev_bf16, dev_f32, dev_i32, dev_u32, host_u16,
-                   weights)
+                   weights, workspace_hidden)
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
@@ -96,29 +96,6 @@ def test_route_ties(oracle, nqlib):
     idx, sc = nb.moe_route(dev_bf16(logits), 4)
     ridx, rsc = oracle.moe_route(logits, 4)
     np.testing.assert_array_equal(idx.cpu().numpy(), ridx)
-
-
-def workspace_hidden(ws, T, E, k, H, I):
-    """The SwiGLU activations h the GPU wrote into the caller-owned workspace,
-    returned in pair order (t*k + j).  Follows the workspace layout of
-    neurons_b200/csrc/moe.cu: counts[E], offsets[E], cursor[E], pos_token[P],
-    pos_pair[P] (int32), tiles[ceil(P/256) + min(E, P)] (int4), n_tiles (int32),
-    h[P, I] (bf16), d[P, H] (fp32), each region aligned to 256 bytes; h is in
-    pair order when P <= E, else grouped by expert with pos_pair giving each
-    row's pair."""
-    P = T * k
-    a = lambda n: (n + 255) // 256 * 256
-    raw = ws.cpu().numpy()
-    off = 3 * a(4 * E)
-    pos_pair = raw[off + a(4 * P): off + a(4 * P) + 4 * P].view(np.int32)
-    max_tiles = (P + 255) // 256 + min(E, P)
-    hoff = off + 2 * a(4 * P) + a(16 * max_tiles) + a(4)
-    h = raw[hoff: hoff + 2 * P * I].view(np.uint16).reshape(P, I)
-    if P <= E:
-        return h.copy()
-    out = np.zeros_like(h)
-    out[pos_pair] = h
-    return out
 
 
 def staged_switch_check(oracle, x, idx, sc, gate, up, down, bits, gs, what):

@@ -189,7 +189,8 @@ def test_square_prefill_and_8bit(oracle, nqlib):
 
 
 def test_lin_mirrors_mlx_ops(oracle, nqlib):
-    """lin() infers bits from the shapes exactly as mlx_ops::lin does."""
+    """lin() infers bits from the shapes exactly as mlx_ops::lin does, and
+    serves a layer stored without scales as matmul(x, W^T)."""
     import neurons_b200 as nb
     rng = np.random.default_rng(3)
     for bits in (4, 8):
@@ -199,9 +200,12 @@ def test_lin_mirrors_mlx_ops(oracle, nqlib):
         x = acts(rng, 3, 512)
         y = nb.lin(dev_bf16(x), "q_proj", wm, 64)
         assert_close(host_u16(y), oracle.qmm(x, wq, s, b, bits, 64), f"lin bits={bits}")
-    with pytest.raises(nb.NQError) as ei:
-        nb.lin(dev_bf16(x), "dense", {"dense.weight": dev_bf16(x)}, 64)
-    assert ei.value.code == "InvalidModel"
+    # a layer without scales is a plain matmul, as in mlx_ops::lin and the C++
+    # cuda_ops::lin (same reference and tolerance as the C++ dense test)
+    w = oracle.f32_to_bf16(weights(rng, 96, 512))
+    y = nb.lin(dev_bf16(x), "dense", {"dense.weight": dev_bf16(w)}, 64)
+    ref = oracle.bf16_to_f32(x).astype(np.float64) @ oracle.bf16_to_f32(w).astype(np.float64).T
+    assert_close(host_u16(y), oracle.f32_to_bf16(ref.astype(np.float32)), "dense lin")
 
 
 def test_back_to_back_launches_are_ordered(oracle, nqlib):

@@ -16,15 +16,17 @@ import numpy as np
 import pytest
 import torch
 
-from _util import acts, assert_close, dev_bf16, dev_f32, dev_i32, dev_u32, host_u16, weights
+from _util import (acts, assert_close, dev_bf16, dev_f32, dev_i32, dev_u32, host_u16, weights,
+                   workspace_hidden)
 
 pytestmark = pytest.mark.gpu
 
 
 def _experts(oracle, rng, E, rows, cols):
+    """(host, device) copies of E stacked quantized experts."""
     wq, s, b = oracle.quantize(weights(rng, E * rows, cols), 4, 64, 0)
-    return (dev_u32(wq.reshape(E, rows, -1)), dev_bf16(s.reshape(E, rows, -1)),
-            dev_bf16(b.reshape(E, rows, -1)))
+    host = (wq.reshape(E, rows, -1), s.reshape(E, rows, -1), b.reshape(E, rows, -1))
+    return host, (dev_u32(host[0]), dev_bf16(host[1]), dev_bf16(host[2]))
 
 
 def _p(t):
@@ -50,11 +52,12 @@ def _call_workspace(lib, x, idx, sc, gate, up, down, y):
     need = lib.nq_moe_workspace_size(T, E, k, H, I)
     ws = torch.empty(need, dtype=torch.uint8, device="cuda")
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    return lib.nq_moe_switch(_p(x), T, H, I, E, k, _p(idx), _p(sc),
-                             _p(gate[0]), _p(gate[1]), _p(gate[2]),
-                             _p(up[0]), _p(up[1]), _p(up[2]),
-                             _p(down[0]), _p(down[1]), _p(down[2]),
-                             4, 64, _p(ws), need, _p(y), stream)
+    rc = lib.nq_moe_switch(_p(x), T, H, I, E, k, _p(idx), _p(sc),
+                           _p(gate[0]), _p(gate[1]), _p(gate[2]),
+                           _p(up[0]), _p(up[1]), _p(up[2]),
+                           _p(down[0]), _p(down[1]), _p(down[2]),
+                           4, 64, _p(ws), need, _p(y), stream)
+    return rc, ws
 
 
 @pytest.mark.parametrize("T", [1, 20])
@@ -62,11 +65,16 @@ def test_static_scratch_matches_workspace_entry_point(oracle, nqlib, T):
     """Two calls in a row on different token batches (T=1: one problem per pair;
     T=20: pairs grouped by expert, which needs zeroed counters), each checked
     against nq_moe_switch with a caller-provided workspace, at the Qwen3-30B-A3B
-    layer dims (E=128, top-8, hidden 2048, intermediate 768, 4-bit g64)."""
+    layer dims (E=128, top-8, hidden 2048, intermediate 768, 4-bit g64).  The
+    first call is also held to the oracle stage by stage: the SwiGLU activations
+    h (read from the workspace call, which runs the same kernels on the same
+    inputs) against the oracle's first stage, and the static call's y against
+    the oracle's second stage applied to that h."""
     E, k, H, I = 128, 8, 2048, 768
     rng = np.random.default_rng(100 + T)
-    gate, up, down = (_experts(oracle, rng, E, I, H), _experts(oracle, rng, E, I, H),
-                      _experts(oracle, rng, E, H, I))
+    (gate_h, gate), (up_h, up), (down_h, down) = (
+        _experts(oracle, rng, E, I, H), _experts(oracle, rng, E, I, H),
+        _experts(oracle, rng, E, H, I))
     for call in range(2):
         x = acts(rng, T, H)
         idx, sc = oracle.moe_route(acts(rng, T, E), k)
@@ -75,12 +83,19 @@ def test_static_scratch_matches_workspace_entry_point(oracle, nqlib, T):
         y_ws = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
         assert _call_static(nqlib, xd, idxd, scd, gate, up, down, y_static) == 0, \
             nqlib.nq_last_error()
-        assert _call_workspace(nqlib, xd, idxd, scd, gate, up, down, y_ws) == 0, \
-            nqlib.nq_last_error()
+        rc, ws = _call_workspace(nqlib, xd, idxd, scd, gate, up, down, y_ws)
+        assert rc == 0, nqlib.nq_last_error()
         torch.cuda.synchronize()
         err = ctypes.c_uint(0)
         assert nqlib.nq_take_device_error(ctypes.byref(err)) == 0 and err.value == 0
         assert_close(host_u16(y_static), host_u16(y_ws), f"static vs workspace, call {call}")
+        if call == 0:
+            h = workspace_hidden(ws, T, E, k, H, I)
+            assert_close(h, oracle.moe_hidden(x, idx, gate_h, up_h, 4, 64, rounding=1),
+                         f"T={T} h vs oracle")
+            assert_close(host_u16(y_static),
+                         oracle.moe_combine(h, idx, sc, down_h, 4, 64, rounding=1),
+                         f"T={T} static y vs oracle")
 
 
 def test_static_scratch_rejects_oversize(nqlib):
