@@ -347,6 +347,88 @@ def time_replay(tokens, warmup, world, seed, clocks=None):
     return max_over_ranks(total, world), rp, clk
 
 
+def time_llama_step(prompt, tokens, world, seed, pk):
+    """The Llama decode step (nq_llama_*) at the Llama-3.2-3B dims, random
+    4-bit g64 weights, tied 4-bit LM head: a prompt of `prompt` tokens, then
+    `tokens` greedy tokens generated back to back on the device (each step
+    reads the previous argmax; no host round trip), timed with CUDA events.
+    Per token: the weights once (the algorithmic bytes of the replay) plus the
+    KV cache read by attention (positions so far x layers x 2 x n_kv x
+    head_dim bf16)."""
+    import torch
+    import neurons_b200 as nb
+    from neurons_b200.llama import LlamaDecoder
+    c = LLAMA3B
+    cfg = dict(n_layers=c["layers"], hidden=c["hidden"], n_heads=c["n_heads"],
+               n_kv_heads=c["n_kv"], head_dim=c["head_dim"], intermediate=c["inter"],
+               vocab=c["vocab"], bits=BITS, group_size=GS, max_context=prompt + tokens + 32,
+               rms_eps=1e-5, rope_theta=500000.0)
+    g = torch.Generator(device="cuda").manual_seed(6000 + seed)
+
+    def qw(n, k, std=0.02):
+        w = torch.randn(n, k, device="cuda", generator=g) * std
+        q = nb.quantize(w, GS, BITS, nb.SCHEME_MINMAX)
+        del w
+        return q
+
+    H, I, V = c["hidden"], c["inter"], c["vocab"]
+    nq_, nkv = c["n_heads"] * c["head_dim"], c["n_kv"] * c["head_dim"]
+    ones = lambda: (1 + 0.1 * torch.randn(H, device="cuda", generator=g)).to(torch.bfloat16)
+    weights = {"embed": qw(V, H, 1.0), "final_norm": ones(), "layers": []}
+    for _ in range(c["layers"]):
+        weights["layers"].append({"q": qw(nq_, H), "k": qw(nkv, H), "v": qw(nkv, H),
+                                  "o": qw(H, nq_), "gate": qw(I, H), "up": qw(I, H),
+                                  "down": qw(H, I), "input_norm": ones(), "post_norm": ones()})
+    dec = LlamaDecoder(cfg, weights)
+    ptoks = torch.randint(0, V, (prompt,), device="cuda", generator=g, dtype=torch.int32)
+    out = torch.empty(tokens, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def timed(fn):
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        fn()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1) / 1e3
+
+    # steps launched from the host one after another (warm-up pass first)
+    dec.prefill(ptoks, logits=False)
+    dec.generate(8, out=out[:8])
+    dec.reset()
+    dec.prefill(ptoks, logits=False)
+    sec_stream = timed(lambda: dec.generate(tokens, out=out))
+    # the same steps replayed from a CUDA graph of 16 steps
+    per_graph = 16
+    dec.reset()
+    dec.prefill(ptoks, logits=False)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        dec.generate(per_graph, out=out[:per_graph])
+    torch.cuda.synchronize()
+    sec = timed(lambda: [graph.replay() for _ in range(tokens // per_graph)])
+    tokens_g = tokens // per_graph * per_graph
+    del graph
+    assert nb.take_device_error() == 0
+    dec.close()
+    layer_w = (nq_ + 2 * nkv) * H + nq_ * H + 3 * I * H
+    wbytes = c["layers"] * (layer_w * BITS // 8 + layer_w // GS * 4) + V * H * BITS // 8 + \
+        V * (H // GS) * 4
+    kv_avg = c["layers"] * 2 * nkv * 2 * (prompt + tokens / 2)
+    byts = wbytes + kv_avg
+    return {"workload": f"Llama-3.2-3B decode step (28 layers, RMSNorm, RoPE, GQA attention over "
+                        f"the KV cache, SwiGLU, tied 4-bit LM head, argmax), prompt {prompt}, "
+                        f"{tokens} tokens generated on the device",
+            "tokens_per_s": tokens_g / sec, "us_per_token": sec / tokens_g * 1e6,
+            "algorithmic_bytes_per_token": byts,
+            "gbs": byts * tokens_g / sec / 1e9,
+            "frac": byts * tokens_g / sec / 1e9 / pk["hbm_gbs"],
+            "note": f"steps replayed from a CUDA graph of {per_graph} steps; launched from the "
+                    f"host one by one: {sec_stream / tokens * 1e6:.0f} us/token",
+            "launches_per_token": 5 * c["layers"] + 3}
+
+
 def replay_summary(t, tokens, rp, world, pk):
     byts = rp.algorithmic_bytes()
     gbs = world * byts * tokens / t / 1e9
@@ -862,6 +944,12 @@ def ours(args):
     pk = peaks()
     if args.workload == "llama3b-decode":
         return ours_replay(args, world, rank, local, pk)
+    if args.workload == "llama3b-step":
+        # the decode step alone (--steps tokens after a 128-token prompt)
+        ls = time_llama_step(128, args.steps, world, rank, pk)
+        if rank == 0:
+            print(json.dumps({"workload": "llama3b-step", **ls}), flush=True)
+        return
     if args.workload.startswith("moe-"):
         return ours_moe(args, world, rank, local, pk)
     wl = WORKLOADS[args.workload]
@@ -970,6 +1058,9 @@ def ours(args):
         line["llama3b_decode"] = replay_summary(t_r, 50, rp, world, pk)
         line["gpu_launches"] += 50 * rp.launches_per_token()
         del rp
+        ls = time_llama_step(128, 128, world, rank, pk)
+        line["llama3b_decode_step"] = ls
+        line["gpu_launches"] += (3 * 128 + 8 + 2 * 128) * ls["launches_per_token"]
     if tp_e2e is not None:
         t_e, n_e, h2d, d2h = tp_e2e
         line["e2e"] = {"value": flops * n_e / t_e / 1e12, "unit": unit, "h2d_bytes_per_step": h2d,
@@ -1121,8 +1212,8 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="prefill", choices=sorted(WORKLOADS) + ["llama3b-decode", "moe-1", "moe-64",
-                                                             "moe-2048"])
+    ap.add_argument("--workload", default="prefill", choices=sorted(WORKLOADS) + ["llama3b-decode", "llama3b-step",
+                                                             "moe-1", "moe-64", "moe-2048"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-lines")
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE sub-line")

@@ -244,6 +244,66 @@ int nq_moe_switch_partial_push(const uint16_t *x, int64_t T, int64_t H, int64_t 
                                void *workspace, size_t workspace_bytes,
                                const nq_rows_push_t *push, void *stream);
 
+/* ---- Llama decode step ----
+ * A Llama decode step on the GPU around the quantized matmuls, restating the
+ * reference's compiled decode function
+ * (compute/src/compute/model/llama_model.cpp:355-509): embedding row,
+ * per layer RMSNorm -> q/k/v -> RoPE -> GQA attention over the growing KV
+ * cache -> o (+ residual) -> RMSNorm -> gate/up -> SwiGLU -> down
+ * (+ residual), final RMSNorm, LM head (lm_head, else the tied quantized
+ * embedding) and a greedy argmax, whose token feeds the next step from
+ * device memory as in mlx_generate_pipelined (:713-812).  Every call only
+ * enqueues work on `stream` (no host synchronisation, no allocation): steps
+ * may be captured in a CUDA graph and replayed.  Serves 4-bit codes with
+ * hidden, intermediate and n_heads*head_dim multiples of 128, head_dim <= 256
+ * and at most 8 query heads per KV head.  Weights are borrowed (they must
+ * outlive the decoder) except q/k/v and gate/up, which are copied into
+ * row-concatenated buffers at creation. */
+typedef struct nq_qweight {
+    const uint32_t *w;        /* packed codes [N, K*bits/32] (dense bf16 [N, K] for an
+                                 unquantized embedding, with scales == NULL) */
+    const uint16_t *scales;   /* bf16 [N, K/gs] */
+    const uint16_t *biases;   /* bf16 [N, K/gs] */
+} nq_qweight_t;
+
+typedef struct nq_llama_config {
+    int n_layers, hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab;
+    int bits, group_size, max_context;
+    float rms_eps, rope_theta;
+} nq_llama_config_t;
+
+typedef struct nq_llama_layer {
+    const uint16_t *input_norm;  /* bf16 [hidden], 16-byte aligned */
+    const uint16_t *post_norm;   /* bf16 [hidden], 16-byte aligned */
+    nq_qweight_t q, k, v, o, gate, up, down;
+} nq_llama_layer_t;
+
+typedef struct nq_llama_s *nq_llama_t;
+
+/* lm_head NULL (or lm_head->w NULL): the tied embedding is the LM head. */
+int nq_llama_create(nq_llama_t *out, const nq_llama_config_t *cfg,
+                    const nq_llama_layer_t *layers, const uint16_t *final_norm,
+                    const nq_qweight_t *embed, const nq_qweight_t *lm_head);
+int nq_llama_destroy(nq_llama_t dec);
+/* Steps enqueued since the last reset (the next step's position). */
+int64_t nq_llama_position(nq_llama_t dec);
+/* Empties the KV cache (position 0). */
+int nq_llama_reset(nq_llama_t dec, void *stream);
+/* One step on token[0] (device int32; NULL: the previous step's argmax).
+ * logits (fp32 [vocab], optional) and next_token (int32, optional) receive
+ * the step's logits and argmax. */
+int nq_llama_step(nq_llama_t dec, const int32_t *token, float *logits,
+                  int32_t *next_token, void *stream);
+/* n steps over the prompt tokens[0..n) (device); logits (optional) gets the
+ * last position's.  Afterwards the decoder's next input is the argmax of the
+ * last position (the first generated token). */
+int nq_llama_prefill(nq_llama_t dec, const int32_t *tokens, int64_t n,
+                     float *logits, void *stream);
+/* n greedy steps, each fed the previous step's argmax (the first one token[0]
+ * when token != NULL); tokens[i] (device int32 [n]) receives step i's argmax. */
+int nq_llama_generate(nq_llama_t dec, const int32_t *token, int64_t n,
+                      int32_t *tokens, void *stream);
+
 /* nq_moe_switch without a workspace argument, for callers that cannot
  * allocate device memory themselves (an FFI host or a runtime that only
  * hands over the tensors it owns and exposes no allocator).  No counterpart

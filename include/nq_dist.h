@@ -53,6 +53,22 @@ int nq_comm_abort(nq_comm_t comm);
 int nq_comm_rank(nq_comm_t comm);
 int nq_comm_size(nq_comm_t comm);
 
+/* Failure detection.  nq_comm_wait waits until the work enqueued on `stream`
+ * so far has completed, polling the stream, NCCL's asynchronous error state
+ * (ncclCommGetAsyncError) and a host deadline of timeout_ms milliseconds
+ * (> 0).  A NCCL error, or the deadline passing first (a rank that left or
+ * stopped making calls), aborts the NCCL communicator (ncclCommAbort, which
+ * ends its collectives still waiting), waits a bounded time for the stream
+ * to drain and returns NQ_COMPUTE_ERROR; every later call on the
+ * communicator then fails at once, and nq_comm_destroy only releases it.
+ * The fused calls' own waits on peer flags are bounded on the device (2 s,
+ * bit 0 of the error word).
+ * nq_comm_set_timeout(comm, ms) with ms > 0 makes every sharded call end with
+ * nq_comm_wait(comm, stream, ms) (synchronous calls with a bounded wait);
+ * 0, the default, leaves the calls asynchronous. */
+int nq_comm_wait(nq_comm_t comm, void *stream, int64_t timeout_ms);
+int nq_comm_set_timeout(nq_comm_t comm, int64_t timeout_ms);
+
 /* Allocates this rank's share of a symmetric arena of `bytes` (collective:
  * every rank calls with the same size) and maps every other rank's share into
  * this process (CUDA IPC).  Outputs of nq_tp_quantized_matmul_fused live

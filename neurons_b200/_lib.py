@@ -44,6 +44,13 @@ SIGNATURES = {
                                   P, P, I, I, P, U64, P, P]),
     "nq_moe_switch_partial_push": (I, [P, I64, I64, I64, I64, I64, P, P, I64, I64, P, P, P, P, P, P,
                                        P, P, P, I, I, P, U64, P, P]),
+    "nq_llama_create": (I, [P, P, P, P, P, P]),
+    "nq_llama_destroy": (I, [P]),
+    "nq_llama_position": (I64, [P]),
+    "nq_llama_reset": (I, [P, P]),
+    "nq_llama_step": (I, [P, P, P, P, P]),
+    "nq_llama_prefill": (I, [P, P, I64, P, P]),
+    "nq_llama_generate": (I, [P, P, I64, P, P]),
 }
 
 

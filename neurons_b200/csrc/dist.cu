@@ -7,8 +7,10 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 #include <string>
+#include <thread>
 
 #include "nq.h"
 #include "nq_dist.h"
@@ -37,6 +39,8 @@ struct nq_comm_s {
     char *arena = nullptr;                 // this rank's arena (header + data)
     size_t arena_bytes = 0;                // data bytes
     char *peer[NQ_MAX_RANKS] = {};         // every rank's arena in this process (self included)
+    int64_t timeout_ms = 0;                // > 0: every sharded call ends with nq_comm_wait
+    bool aborted = false;                  // the NCCL communicator was aborted
 };
 
 namespace {
@@ -426,6 +430,17 @@ unsigned grid_for(int64_t n) {
 
 }  // namespace
 
+extern "C" int nq_comm_wait(nq_comm_t comm, void *stream, int64_t timeout_ms);
+
+namespace {
+// A sharded call that succeeded ends with the communicator's bounded wait
+// when one is set (nq_comm_set_timeout).
+int settle(nq_comm_t comm, void *stream, int rc) {
+    if (rc != NQ_SUCCESS || !comm || comm->timeout_ms <= 0) return rc;
+    return nq_comm_wait(comm, stream, comm->timeout_ms);
+}
+}  // namespace
+
 extern "C" {
 
 const char *nq_dist_last_error(void) { return g_err.c_str(); }
@@ -470,7 +485,8 @@ static void release_arena(nq_comm_t comm) {
 int nq_comm_destroy(nq_comm_t comm) {
     if (!comm) return NQ_SUCCESS;
     release_arena(comm);
-    const int rc = from_nccl(ncclCommDestroy(comm->nccl), "nq_comm_destroy");
+    const int rc =
+        comm->aborted ? NQ_SUCCESS : from_nccl(ncclCommDestroy(comm->nccl), "nq_comm_destroy");
     delete comm;
     return rc;
 }
@@ -478,9 +494,58 @@ int nq_comm_destroy(nq_comm_t comm) {
 int nq_comm_abort(nq_comm_t comm) {
     if (!comm) return NQ_SUCCESS;
     release_arena(comm);
-    const int rc = from_nccl(ncclCommAbort(comm->nccl), "nq_comm_abort");
+    const int rc =
+        comm->aborted ? NQ_SUCCESS : from_nccl(ncclCommAbort(comm->nccl), "nq_comm_abort");
     delete comm;
     return rc;
+}
+
+int nq_comm_set_timeout(nq_comm_t comm, int64_t timeout_ms) {
+    if (!comm || timeout_ms < 0)
+        return fail(NQ_INVALID_INPUT, "nq_comm_set_timeout: NULL communicator or negative timeout");
+    comm->timeout_ms = timeout_ms;
+    return NQ_SUCCESS;
+}
+
+int nq_comm_wait(nq_comm_t comm, void *stream, int64_t timeout_ms) {
+    const char *what = "nq_comm_wait";
+    if (!comm || timeout_ms <= 0)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": NULL communicator or timeout <= 0");
+    if (comm->aborted)
+        return fail(NQ_COMPUTE_ERROR, std::string(what) + ": the communicator was aborted");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    using clock = std::chrono::steady_clock;
+    const auto deadline = clock::now() + std::chrono::milliseconds(timeout_ms);
+    std::string why;
+    while (true) {
+        const cudaError_t q = cudaStreamQuery(st);
+        if (q == cudaSuccess) return NQ_SUCCESS;
+        if (q != cudaErrorNotReady) return from_cuda(q, what);
+        ncclResult_t async = ncclSuccess;
+        const ncclResult_t r = ncclCommGetAsyncError(comm->nccl, &async);
+        if (r != ncclSuccess || (async != ncclSuccess && async != ncclInProgress)) {
+            why = std::string("NCCL reported an error: ") +
+                  ncclGetErrorString(r != ncclSuccess ? r : async);
+            break;
+        }
+        if (clock::now() > deadline) {
+            why = "timed out after " + std::to_string(timeout_ms) +
+                  " ms (a rank left or stopped calling)";
+            break;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+    // end the collectives still waiting, then let the stream drain (bounded)
+    ncclCommAbort(comm->nccl);
+    comm->aborted = true;
+    const auto drain = clock::now() + std::chrono::seconds(10);
+    while (cudaStreamQuery(st) == cudaErrorNotReady && clock::now() < drain)
+        std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    const bool drained = cudaStreamQuery(st) != cudaErrorNotReady;
+    cudaGetLastError();
+    return fail(NQ_COMPUTE_ERROR, std::string(what) + ": " + why +
+                                      "; communicator aborted" +
+                                      (drained ? "" : ", stream still busy after 10 s"));
 }
 
 int nq_comm_rank(nq_comm_t comm) { return comm ? comm->rank : -1; }
@@ -576,7 +641,7 @@ int nq_comm_take_error(nq_comm_t comm, unsigned int *value) {
                      "nq_comm_take_error");
 }
 
-int nq_tp_quantized_matmul_fused(nq_comm_t comm, const uint16_t *x, int64_t M,
+static int tp_quantized_matmul_fused_impl(nq_comm_t comm, const uint16_t *x, int64_t M,
                                  const uint32_t *w_shard, const uint16_t *s_shard,
                                  const uint16_t *b_shard, int64_t N, int64_t K, int bits,
                                  int group_size, uint16_t *y, void *stream) {
@@ -641,6 +706,17 @@ int nq_tp_quantized_matmul_fused(nq_comm_t comm, const uint16_t *x, int64_t M,
         what);
 }
 
+int nq_tp_quantized_matmul_fused(nq_comm_t comm, const uint16_t *x, int64_t M,
+                                 const uint32_t *w_shard, const uint16_t *s_shard,
+                                 const uint16_t *b_shard, int64_t N, int64_t K, int bits,
+                                 int group_size, uint16_t *y, void *stream) {
+    if (comm && comm->aborted)
+        return fail(NQ_COMPUTE_ERROR, "nq_tp_quantized_matmul_fused: the communicator was aborted");
+    const int rc = tp_quantized_matmul_fused_impl(comm, x, M, w_shard, s_shard, b_shard, N, K, bits,
+                                                  group_size, y, stream);
+    return settle(comm, stream, rc);
+}
+
 int nq_tp_shard(int64_t N, int nranks, int rank, int64_t *row0, int64_t *rows) {
     return split(N, nranks, rank, row0, rows, "nq_tp_shard");
 }
@@ -665,7 +741,7 @@ size_t nq_ep_workspace_size(int64_t T, int64_t E, int64_t top_k, int64_t H, int6
     return ep_carve(nullptr, T, E, top_k, H, I, nranks).bytes;
 }
 
-int nq_tp_quantized_matmul(nq_comm_t comm, const uint16_t *x, int64_t M, const uint32_t *w_shard,
+static int tp_quantized_matmul_impl(nq_comm_t comm, const uint16_t *x, int64_t M, const uint32_t *w_shard,
                            const uint16_t *s_shard, const uint16_t *b_shard, int64_t N, int64_t K,
                            int bits, int group_size, uint16_t *y, void *workspace,
                            size_t workspace_bytes, void *stream) {
@@ -707,7 +783,18 @@ int nq_tp_quantized_matmul(nq_comm_t comm, const uint16_t *x, int64_t M, const u
     return from_cuda(cudaGetLastError(), what);
 }
 
-int nq_ep_moe_switch(nq_comm_t comm, const uint16_t *x_shard, int64_t T, int64_t H, int64_t I,
+int nq_tp_quantized_matmul(nq_comm_t comm, const uint16_t *x, int64_t M, const uint32_t *w_shard,
+                           const uint16_t *s_shard, const uint16_t *b_shard, int64_t N, int64_t K,
+                           int bits, int group_size, uint16_t *y, void *workspace,
+                           size_t workspace_bytes, void *stream) {
+    if (comm && comm->aborted)
+        return fail(NQ_COMPUTE_ERROR, "nq_tp_quantized_matmul: the communicator was aborted");
+    const int rc = tp_quantized_matmul_impl(comm, x, M, w_shard, s_shard, b_shard, N, K, bits,
+                                            group_size, y, workspace, workspace_bytes, stream);
+    return settle(comm, stream, rc);
+}
+
+static int ep_moe_switch_impl(nq_comm_t comm, const uint16_t *x_shard, int64_t T, int64_t H, int64_t I,
                      int64_t E, int64_t top_k, const int32_t *topk_idx_shard,
                      const float *topk_scores_shard, const uint32_t *gate_w,
                      const uint16_t *gate_s, const uint16_t *gate_b, const uint32_t *up_w,
@@ -751,6 +838,22 @@ int nq_ep_moe_switch(nq_comm_t comm, const uint16_t *x_shard, int64_t T, int64_t
     return from_cuda(cudaGetLastError(), what);
 }
 
+int nq_ep_moe_switch(nq_comm_t comm, const uint16_t *x_shard, int64_t T, int64_t H, int64_t I,
+                     int64_t E, int64_t top_k, const int32_t *topk_idx_shard,
+                     const float *topk_scores_shard, const uint32_t *gate_w,
+                     const uint16_t *gate_s, const uint16_t *gate_b, const uint32_t *up_w,
+                     const uint16_t *up_s, const uint16_t *up_b, const uint32_t *down_w,
+                     const uint16_t *down_s, const uint16_t *down_b, int bits, int group_size,
+                     void *workspace, size_t workspace_bytes, uint16_t *y_shard, void *stream) {
+    if (comm && comm->aborted)
+        return fail(NQ_COMPUTE_ERROR, "nq_ep_moe_switch: the communicator was aborted");
+    const int rc = ep_moe_switch_impl(comm, x_shard, T, H, I, E, top_k, topk_idx_shard,
+                                      topk_scores_shard, gate_w, gate_s, gate_b, up_w, up_s, up_b,
+                                      down_w, down_s, down_b, bits, group_size, workspace,
+                                      workspace_bytes, y_shard, stream);
+    return settle(comm, stream, rc);
+}
+
 size_t nq_ep_fused_arena_size(int64_t T, int64_t top_k, int64_t H, int nranks) {
     if (T <= 0 || top_k <= 0 || H <= 0 || nranks <= 0 || nranks > NQ_MAX_RANKS || T % nranks)
         return 0;
@@ -765,7 +868,7 @@ size_t nq_ep_fused_workspace_size(int64_t T, int64_t E, int64_t top_k, int64_t H
     return ep_local(nullptr, T, E, top_k, H, I, nranks).bytes;
 }
 
-int nq_ep_moe_switch_fused(nq_comm_t comm, const uint16_t *x_shard, int64_t T, int64_t H,
+static int ep_moe_switch_fused_impl(nq_comm_t comm, const uint16_t *x_shard, int64_t T, int64_t H,
                            int64_t I, int64_t E, int64_t top_k, const int32_t *topk_idx_shard,
                            const float *topk_scores_shard, const uint32_t *gate_w,
                            const uint16_t *gate_s, const uint16_t *gate_b, const uint32_t *up_w,
@@ -876,6 +979,24 @@ int nq_ep_moe_switch_fused(nq_comm_t comm, const uint16_t *x_shard, int64_t T, i
                                   reinterpret_cast<const float *>(mine + rg.back),
                                   (const int32_t *)loc.pos, cap, H, P, y_shard),
                      what);
+}
+
+int nq_ep_moe_switch_fused(nq_comm_t comm, const uint16_t *x_shard, int64_t T, int64_t H,
+                           int64_t I, int64_t E, int64_t top_k, const int32_t *topk_idx_shard,
+                           const float *topk_scores_shard, const uint32_t *gate_w,
+                           const uint16_t *gate_s, const uint16_t *gate_b, const uint32_t *up_w,
+                           const uint16_t *up_s, const uint16_t *up_b, const uint32_t *down_w,
+                           const uint16_t *down_s, const uint16_t *down_b, int bits,
+                           int group_size, size_t arena_offset, void *workspace,
+                           size_t workspace_bytes, uint16_t *y_shard, void *stream) {
+    if (comm && comm->aborted)
+        return fail(NQ_COMPUTE_ERROR, "nq_ep_moe_switch_fused: the communicator was aborted");
+    const int rc = ep_moe_switch_fused_impl(comm, x_shard, T, H, I, E, top_k, topk_idx_shard,
+                                            topk_scores_shard, gate_w, gate_s, gate_b, up_w, up_s,
+                                            up_b, down_w, down_s, down_b, bits, group_size,
+                                            arena_offset, workspace, workspace_bytes, y_shard,
+                                            stream);
+    return settle(comm, stream, rc);
 }
 
 }  // extern "C"

@@ -1039,13 +1039,60 @@ cudaError_t dispatch_tma(const CUtensorMap &m1, const CUtensorMap &m2, const Gem
 // Measured (B200, CUDA graph of back-to-back calls): 4096x4096 at M=1 5.0 us
 // against 7.9 us for the TMA-fed kernel, 3072x3072 3.7 against 8.5 us.
 // ----------------------------------------------------------------------------
+constexpr int kRowsPlain = 0, kRowsNorm = 1, kRowsSwiglu = 2;
+
 struct RowsParams {
     const uint32_t *w;
     const uint16_t *s, *b, *x;
     uint16_t *y;
     int64_t N, K, Kw, G, x_ld, y_ld;
     int gs_shift, M;
+    // prologue applied to each x row as it is staged (kRowsPlain for none)
+    int pro;
+    const uint16_t *nw;  // kRowsNorm: the RMSNorm weight [K]
+    float eps;
+    // epilogue: y = bf16(res + bf16(acc)) when res != nullptr (rows res_ld apart)
+    const uint16_t *res;
+    int64_t res_ld;
 };
+
+// x = bf16(bf16(bf16(sigmoid(g)) * g) * u) for one bf16 pair each of g, u:
+// the SwiGLU op chain of mlx_ops' callers (sigmoid(gate) * gate * up, each
+// op rounded to bf16)
+__device__ __forceinline__ uint32_t swiglu_pair(uint32_t g2, uint32_t u2) {
+    uint32_t out = 0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const float g = bf16_to_f32((uint16_t)(g2 >> (16 * h)));
+        const float u = bf16_to_f32((uint16_t)(u2 >> (16 * h)));
+        const float sg = bf16_to_f32(f32_to_bf16(1.0f / (1.0f + expf(-g))));
+        const float a = bf16_to_f32(f32_to_bf16(sg * g));
+        out |= (uint32_t)f32_to_bf16(a * u) << (16 * h);
+    }
+    return out;
+}
+
+// y = bf16(w * bf16(x * inv)) for one bf16 pair each of x, w (MLX's rms_norm
+// output rounding)
+__device__ __forceinline__ uint32_t norm_pair(uint32_t x2, uint32_t w2, float inv) {
+    uint32_t out = 0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const float x = bf16_to_f32((uint16_t)(x2 >> (16 * h)));
+        const float w = bf16_to_f32((uint16_t)(w2 >> (16 * h)));
+        out |= (uint32_t)f32_to_bf16(w * bf16_to_f32(f32_to_bf16(x * inv))) << (16 * h);
+    }
+    return out;
+}
+
+__device__ __forceinline__ uint4 pair_permute(uint4 v) {
+    uint4 o;
+    o.x = prmt(v.x, v.z, 0x5410u);
+    o.y = prmt(v.x, v.z, 0x7632u);
+    o.z = prmt(v.y, v.w, 0x5410u);
+    o.w = prmt(v.y, v.w, 0x7632u);
+    return o;
+}
 
 template <int KBW>
 __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
@@ -1081,16 +1128,49 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
         }
     }
     pdl_wait();  // x may be the previous kernel's output
+    float ss = 0.f;  // kRowsNorm (M == 1): this lane's share of sum(x^2)
     for (int q = lane; q < M * XCH; q += 32) {
         const int m = q / XCH, ck = q % XCH;  // chunk ck of the slice covers codes kb0*128 + 8*ck ...
-        const uint4 v = ldg16(p.x + (int64_t)m * p.x_ld + kb0 * 128 + ck * 8);
+        const uint16_t *xr = p.x + (int64_t)m * p.x_ld + kb0 * 128 + ck * 8;
+        uint4 v = ldg16(xr);
+        if (p.pro == kRowsSwiglu) {
+            const uint4 u = ldg16(xr + p.K);  // x row = [gate (K) | up (K)]
+            v.x = swiglu_pair(v.x, u.x);
+            v.y = swiglu_pair(v.y, u.y);
+            v.z = swiglu_pair(v.z, u.z);
+            v.w = swiglu_pair(v.w, u.w);
+        } else if (p.pro == kRowsNorm) {
+            const uint32_t e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float lo = bf16_to_f32((uint16_t)e[j]), hi = bf16_to_f32((uint16_t)(e[j] >> 16));
+                ss = fmaf(lo, lo, ss);
+                ss = fmaf(hi, hi, ss);
+            }
+        }
         const int kbi = ck >> 4, cc = (ck >> 2) & 3, i = ck & 3;
-        uint4 o;
-        o.x = prmt(v.x, v.z, 0x5410u);
-        o.y = prmt(v.x, v.z, 0x7632u);
-        o.z = prmt(v.y, v.w, 0x5410u);
-        o.w = prmt(v.y, v.w, 0x7632u);
-        xs[m * XCH + kbi * 16 + i * 4 + cc] = o;
+        xs[m * XCH + kbi * 16 + i * 4 + cc] = pair_permute(v);
+    }
+    if (p.pro == kRowsNorm) {
+        // mean of x^2 over the whole row: every warp's slice, through shared
+        // memory; then each lane normalises the chunks it staged
+        __shared__ float ss_warp[16];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) ss_warp[warp] = ss;
+        __syncthreads();
+        float tot = 0.f;
+        for (int w = 0; w < W; ++w) tot += ss_warp[w];
+        const float inv = 1.0f / sqrtf(tot / (float)p.K + p.eps);
+        for (int ck = lane; ck < XCH; ck += 32) {
+            const int kbi = ck >> 4, cc = (ck >> 2) & 3, i = ck & 3;
+            uint4 &o = xs[kbi * 16 + i * 4 + cc];
+            const uint4 wn = pair_permute(ldg16(p.nw + kb0 * 128 + ck * 8));
+            o.x = norm_pair(o.x, wn.x, inv);
+            o.y = norm_pair(o.y, wn.y, inv);
+            o.z = norm_pair(o.z, wn.z, inv);
+            o.w = norm_pair(o.w, wn.w, inv);
+        }
     }
     __syncwarp();
     const uint4 *xr = xs + min(g, M - 1) * XCH + c;
@@ -1134,7 +1214,12 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
         for (int w = 0; w < W; ++w) v += red[(w * 4 + j) * 32 + lane];
         const int m = 2 * c + (j & 1);
         const int64_t n = r0 + g + 8 * (j >> 1);
-        if (m < M && n < p.N) p.y[(int64_t)m * p.y_ld + n] = f32_to_bf16(v);
+        if (m < M && n < p.N) {
+            uint16_t out = f32_to_bf16(v);
+            if (p.res)
+                out = f32_to_bf16(bf16_to_f32(p.res[(int64_t)m * p.res_ld + n]) + bf16_to_f32(out));
+            p.y[(int64_t)m * p.y_ld + n] = out;
+        }
     }
 }
 
@@ -1184,37 +1269,18 @@ cudaError_t launch_rows(const RowsParams &p, int W, cudaStream_t stream) {
     return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-// The row-group kernel serves q when q is one plain problem of at most 8
-// tokens with 4-bit codes, K a multiple of 128 that splits into 4..16 warps,
-// and x rows 16-byte aligned; returns cudaErrorNotSupported otherwise.
-cudaError_t try_launch_rows(const GemvProblems &q, cudaStream_t stream) {
-    const bool plain = q.P == 1 && !q.expert && !q.expert_is_p && !q.m_count && !q.m_offset &&
-                       !q.x_rows && !q.lhs && !q.y_rows && q.x_div == 0 && !q.w2 && !q.push &&
-                       !q.out_f32 && !q.swiglu;
-    if (!plain || q.bits != 4 || q.M < 1 || q.M > 8 || q.K % 128 || q.N < 1) return cudaErrorNotSupported;
-    if ((reinterpret_cast<uintptr_t>(q.x) & 15) || q.x_ld % 8 || q.N > ((int64_t)1 << 31) * 16)
+// Checks shared by both entry points, then the kernel choice and launch.
+cudaError_t launch_rows_checked(RowsParams p, const void *x, cudaStream_t stream) {
+    if (p.M < 1 || p.M > 8 || p.K % 128 || p.N < 1) return cudaErrorNotSupported;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || p.x_ld % 8 || p.N > ((int64_t)1 << 31) * 16)
         return cudaErrorNotSupported;
     // x staged per warp: M x K bf16 per CTA in all (at most 96 KB, so that two
     // CTAs of consecutive calls still fit an SM side by side)
-    if ((int64_t)q.M * q.K * 2 > 96 * 1024) return cudaErrorNotSupported;
-    const int64_t kb_total = q.K / 128;
-    const int kbw = rows_kbw(kb_total, (q.N + 15) / 16);
+    if ((int64_t)p.M * p.K * 2 > 96 * 1024) return cudaErrorNotSupported;
+    const int64_t kb_total = p.K / 128;
+    const int kbw = rows_kbw(kb_total, (p.N + 15) / 16);
     if (!kbw) return cudaErrorNotSupported;
     const int W = (int)(kb_total / kbw);
-    RowsParams p;
-    p.w = q.w;
-    p.s = q.s;
-    p.b = q.b;
-    p.x = q.x;
-    p.y = static_cast<uint16_t *>(q.y);
-    p.N = q.N;
-    p.K = q.K;
-    p.Kw = q.K / 8;
-    p.G = q.K / q.gs;
-    p.x_ld = q.x_ld;
-    p.y_ld = q.y_ld;
-    p.gs_shift = q.gs == 32 ? 5 : (q.gs == 64 ? 6 : 7);
-    p.M = q.M;
     switch (kbw) {
         case 2: return launch_rows<2>(p, W, stream);
         case 3: return launch_rows<3>(p, W, stream);
@@ -1224,7 +1290,65 @@ cudaError_t try_launch_rows(const GemvProblems &q, cudaStream_t stream) {
     }
 }
 
+RowsParams rows_params(const uint32_t *w, const uint16_t *s, const uint16_t *b, int64_t N,
+                       int64_t K, int gs, const uint16_t *x, int64_t x_ld, int M, uint16_t *y,
+                       int64_t y_ld) {
+    RowsParams p;
+    p.w = w;
+    p.s = s;
+    p.b = b;
+    p.x = x;
+    p.y = y;
+    p.N = N;
+    p.K = K;
+    p.Kw = K / 8;
+    p.G = K / gs;
+    p.x_ld = x_ld;
+    p.y_ld = y_ld;
+    p.gs_shift = gs == 32 ? 5 : (gs == 64 ? 6 : 7);
+    p.M = M;
+    p.pro = kRowsPlain;
+    p.nw = nullptr;
+    p.eps = 0.f;
+    p.res = nullptr;
+    p.res_ld = 0;
+    return p;
+}
+
+// The row-group kernel serves q when q is one plain problem of at most 8
+// tokens with 4-bit codes, K a multiple of 128 that splits into 4..16 warps,
+// and x rows 16-byte aligned; returns cudaErrorNotSupported otherwise.
+cudaError_t try_launch_rows(const GemvProblems &q, cudaStream_t stream) {
+    const bool plain = q.P == 1 && !q.expert && !q.expert_is_p && !q.m_count && !q.m_offset &&
+                       !q.x_rows && !q.lhs && !q.y_rows && q.x_div == 0 && !q.w2 && !q.push &&
+                       !q.out_f32 && !q.swiglu;
+    if (!plain || q.bits != 4) return cudaErrorNotSupported;
+    return launch_rows_checked(rows_params(q.w, q.s, q.b, q.N, q.K, q.gs, q.x, q.x_ld, q.M,
+                                           static_cast<uint16_t *>(q.y), q.y_ld),
+                               q.x, stream);
+}
+
 }  // namespace
+
+bool rows_fused_supported(int64_t N, int64_t K, int bits) {
+    return bits == 4 && N >= 1 && K % 128 == 0 && K * 2 <= 96 * 1024 &&
+           N <= ((int64_t)1 << 31) * 16 && rows_kbw(K / 128, (N + 15) / 16) != 0;
+}
+
+cudaError_t launch_rows_fused(const RowsFusedArgs &a, cudaStream_t stream) {
+    if (a.bits != 4) return cudaErrorNotSupported;
+    if (a.prologue != kRowsPlain && a.M != 1) return cudaErrorNotSupported;
+    if (a.prologue == kRowsSwiglu && (a.x_ld < 2 * a.K)) return cudaErrorNotSupported;
+    if (a.prologue == kRowsNorm && (!a.norm_w || (reinterpret_cast<uintptr_t>(a.norm_w) & 15)))
+        return cudaErrorNotSupported;
+    RowsParams p = rows_params(a.w, a.s, a.b, a.N, a.K, a.gs, a.x, a.x_ld, a.M, a.y, a.y_ld);
+    p.pro = a.prologue;
+    p.nw = a.norm_w;
+    p.eps = a.eps;
+    p.res = a.res;
+    p.res_ld = a.res_ld;
+    return launch_rows_checked(p, a.x, stream);
+}
 
 const char *gemv_push_unsupported(const GemvProblems &q) {
     // the output fan-out lives in the TMA-fed kernel: its conditions, below

@@ -62,6 +62,33 @@ struct GemvProblems {
 
 cudaError_t launch_gemv(const GemvProblems &p, cudaStream_t stream);
 
+// Decode-step GEMV of the row-group kernel (4-bit codes, K % 128 == 0) with a
+// prologue fused into the staging of x and a residual epilogue:
+//   prologue 0: x as is; 1: x = bf16(norm_w * bf16(x * rsqrt(mean(x^2) + eps)))
+//   (MLX rms_norm); 2: x = swiglu(g, u) for the row [g (K) | u (K)];
+//   res != nullptr: y = bf16(res + bf16(x . W^T)).
+// Prologues 1 and 2 need M == 1.  cudaErrorNotSupported when the kernel does
+// not serve the shape.
+struct RowsFusedArgs {
+    const uint16_t *x = nullptr;
+    int64_t x_ld = 0;
+    int M = 1;
+    const uint32_t *w = nullptr;
+    const uint16_t *s = nullptr, *b = nullptr;
+    int64_t N = 0, K = 0;
+    int bits = 4, gs = 64;
+    uint16_t *y = nullptr;
+    int64_t y_ld = 0;
+    int prologue = 0;
+    const uint16_t *norm_w = nullptr;
+    float eps = 0.f;
+    const uint16_t *res = nullptr;
+    int64_t res_ld = 0;
+};
+cudaError_t launch_rows_fused(const RowsFusedArgs &a, cudaStream_t stream);
+// Whether launch_rows_fused serves an N x K weight at M == 1 (host only).
+bool rows_fused_supported(int64_t N, int64_t K, int bits);
+
 // Why launch_gemv cannot serve p with an output fan-out (p.push), or nullptr
 // when its arguments allow it (the fan-out also needs tensor maps from the
 // driver: tensor_maps_available()).  Host-side only: no device work.

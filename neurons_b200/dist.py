@@ -44,6 +44,8 @@ SIGNATURES = {
     "nq_comm_symmetric_alloc": (I, [P, U64]),
     "nq_comm_symmetric_ptr": (P, [P, U64]),
     "nq_comm_take_error": (I, [P, ctypes.POINTER(ctypes.c_uint)]),
+    "nq_comm_wait": (I, [P, P, I64]),
+    "nq_comm_set_timeout": (I, [P, I64]),
     "nq_tp_quantized_matmul_fused": (I, [P, P, I64, P, P, P, I64, I64, I, I, P, P]),
     "nq_tp_shard": (I, [I64, I, I, PI64, PI64]),
     "nq_ep_shard": (I, [I64, I, I, PI64, PI64]),
@@ -167,6 +169,17 @@ class Comm:
         v = ctypes.c_uint(0)
         _check(dist_lib().nq_comm_take_error(self.handle, ctypes.byref(v)))
         return v.value
+
+    def wait(self, timeout_ms, stream=None):
+        """Bounded wait for the work enqueued on the stream (default: the
+        current one): raises NQError (ComputeError) and aborts the
+        communicator when NCCL reports an error or the deadline passes."""
+        st = P(stream.cuda_stream) if stream is not None else ops._stream()
+        _check(dist_lib().nq_comm_wait(self.handle, st, timeout_ms))
+
+    def set_timeout(self, timeout_ms):
+        """timeout_ms > 0: every sharded call ends with wait(timeout_ms)."""
+        _check(dist_lib().nq_comm_set_timeout(self.handle, timeout_ms))
 
     def close(self):
         if self.handle:

@@ -144,3 +144,30 @@ def test_push_check_names_misaligned_scales(nqlib):
     args[10] = 100  # columns [100, 164) outside N_total = 128
     assert nqlib.nq_quantized_matmul_push_check(*args) == 1
     assert b"columns outside" in nqlib.nq_last_error()
+
+
+def test_llama_create_validates_on_the_host(nqlib):
+    """nq_llama_create rejects NULL arguments and configurations the decode
+    step does not serve before it touches a device."""
+    import ctypes
+    from neurons_b200.llama import LlamaConfig, LlamaLayer, QWeight
+    out = ctypes.c_void_p()
+    assert nqlib.nq_llama_create(ctypes.byref(out), None, None, None, None, None) == 1
+    cfg = LlamaConfig(n_layers=1, hidden=3072, n_heads=24, n_kv_heads=8, head_dim=128,
+                      intermediate=8192, vocab=1000, bits=8, group_size=64, max_context=16,
+                      rms_eps=1e-5, rope_theta=1e4)
+    layers = (LlamaLayer * 1)()
+    dummy = ctypes.c_void_p(256)
+    emb = QWeight(dummy, dummy, dummy)
+    rc = nqlib.nq_llama_create(ctypes.byref(out), ctypes.byref(cfg), layers, dummy,
+                               ctypes.byref(emb), None)
+    assert rc == 1 and b"4-bit" in nqlib.nq_last_error()
+    cfg.bits, cfg.n_kv_heads = 4, 5  # 24 heads do not split over 5 KV heads
+    rc = nqlib.nq_llama_create(ctypes.byref(out), ctypes.byref(cfg), layers, dummy,
+                               ctypes.byref(emb), None)
+    assert rc == 1 and b"n_kv_heads" in nqlib.nq_last_error()
+    cfg.n_kv_heads, cfg.hidden = 8, 320  # K = 320 is not served by the decode GEMV
+    rc = nqlib.nq_llama_create(ctypes.byref(out), ctypes.byref(cfg), layers, dummy,
+                               ctypes.byref(emb), None)
+    assert rc == 1
+    assert not out.value

@@ -70,6 +70,14 @@ def test_workspace_sizes(dlib):
     assert dist.ep_workspace_size(2047, 128, 8, 2048, 768, 8) == 0  # T not divisible
 
 
+def test_failure_detection_arguments(dlib):
+    """nq_comm_wait needs a communicator and a positive deadline;
+    nq_comm_set_timeout rejects a negative one (no device is touched)."""
+    assert dlib.nq_comm_wait(None, None, 1000) == 1
+    assert b"nq_comm_wait" in dlib.nq_dist_last_error()
+    assert dlib.nq_comm_set_timeout(None, 10) == 1
+
+
 def test_sharded_calls_validate_before_touching_a_device(dlib):
     dummy = ctypes.c_void_p(16)
     rc = dlib.nq_tp_quantized_matmul(None, dummy, 1, dummy, dummy, dummy, 64, 64, 4, 64, dummy,
