@@ -66,6 +66,7 @@ typedef enum nq_status {
 /* Input dtypes for nq_quantize. */
 #define NQ_DTYPE_F32 0
 #define NQ_DTYPE_BF16 1
+#define NQ_DTYPE_F16 2
 
 /* Library identity / diagnostics (no reference counterpart: FFI plumbing). */
 int nq_version(void);
@@ -80,8 +81,9 @@ int nq_take_device_error(unsigned int *err_out);
 /* mlx_ops::bits: round(32 * (w_cols / s_cols) / group_size), 4 if not positive. */
 int nq_bits_from_shapes(int64_t w_cols, int64_t s_cols, int group_size);
 
-/* mx::quantize.  w: [rows, K] fp32 or bf16 (w_dtype).  Outputs: wq [rows,
- * K*bits/32] uint32, scales/biases [rows, K/group_size] bf16. */
+/* mx::quantize.  w: [rows, K] fp32, bf16 or fp16 (w_dtype).  Outputs: wq
+ * [rows, K*bits/32] uint32, scales/biases [rows, K/group_size] bf16 (fp16 for
+ * fp16 weights: MLX keeps the weights' dtype). */
 int nq_quantize(const void *w, int w_dtype, int64_t rows, int64_t K, int bits,
                 int group_size, int scheme, uint32_t *wq, uint16_t *scales,
                 uint16_t *biases, void *stream);
@@ -90,6 +92,22 @@ int nq_quantize(const void *w, int w_dtype, int64_t rows, int64_t K, int bits,
 int nq_dequantize(const uint32_t *wq, const uint16_t *scales,
                   const uint16_t *biases, int64_t rows, int64_t K, int bits,
                   int group_size, uint16_t *out, void *stream);
+
+/* mx::dequantize with fp16 scales and biases (an fp16 checkpoint): out
+ * [rows, K] fp16, bit-exact fp16(fp16(s*q) + b). */
+int nq_dequantize_f16(const uint32_t *wq, const uint16_t *scales,
+                      const uint16_t *biases, int64_t rows, int64_t K, int bits,
+                      int group_size, uint16_t *out, void *stream);
+
+/* mx::quantized_matmul with fp16 x, scales, biases and y (what mlx_ops::lin,
+ * compute/src/compute/model/mlx_ops.h:33-39, runs for an fp16 checkpoint):
+ * fp32 accumulation, fp16 out.  M <= 8 with 4-bit codes takes the decode
+ * GEMV (K % 128 == 0, at most 96 KB of x); every other shape the tcgen05
+ * GEMM (16-byte aligned x and packed rows). */
+int nq_quantized_matmul_f16(const uint16_t *x, int64_t M, const uint32_t *wq,
+                            const uint16_t *scales, const uint16_t *biases,
+                            int64_t N, int64_t K, int bits, int group_size,
+                            uint16_t *y, void *stream);
 
 /* mx::quantized_matmul(x, w, scales, biases, transpose=true, gs, bits).
  * x: [M, K] bf16; y: [M, N] bf16.  fp32 accumulation.  biases must be

@@ -28,6 +28,8 @@ SIGNATURES = {
     "nq_bits_from_shapes": (I, [I64, I64, I]),
     "nq_quantize": (I, [P, I, I64, I64, I, I, I, P, P, P, P]),
     "nq_dequantize": (I, [P, P, P, I64, I64, I, I, P, P]),
+    "nq_dequantize_f16": (I, [P, P, P, I64, I64, I, I, P, P]),
+    "nq_quantized_matmul_f16": (I, [P, I64, P, P, P, I64, I64, I, I, P, P]),
     "nq_quantized_matmul": (I, [P, I64, P, P, P, I64, I64, I, I, P, P]),
     "nq_quantized_matmul_launches": (I, [I64, I64, I64, I, I]),
     "nq_gather_qmm": (I, [P, I64, I64, P, P, I64, P, P, P, I64, I64, I64, I, I, P, P]),

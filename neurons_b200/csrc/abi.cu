@@ -145,8 +145,9 @@ int nq_bits_from_shapes(int64_t w_cols, int64_t s_cols, int group_size) {
 int nq_quantize(const void *w, int w_dtype, int64_t rows, int64_t K, int bits, int group_size,
                 int scheme, uint32_t *wq, uint16_t *scales, uint16_t *biases, void *stream) {
     if (int rc = check_quant(rows, K, bits, group_size, "nq_quantize")) return rc;
-    if (w_dtype != NQ_DTYPE_F32 && w_dtype != NQ_DTYPE_BF16)
-        return fail(NQ_INVALID_INPUT, "nq_quantize: w_dtype must be NQ_DTYPE_F32 or NQ_DTYPE_BF16");
+    if (w_dtype != NQ_DTYPE_F32 && w_dtype != NQ_DTYPE_BF16 && w_dtype != NQ_DTYPE_F16)
+        return fail(NQ_INVALID_INPUT,
+                    "nq_quantize: w_dtype must be NQ_DTYPE_F32, NQ_DTYPE_BF16 or NQ_DTYPE_F16");
     if (scheme != NQ_SCHEME_MLX_AFFINE && scheme != NQ_SCHEME_MINMAX)
         return fail(NQ_INVALID_INPUT, "nq_quantize: unknown scheme");
     if (rows == 0) return NQ_SUCCESS;
@@ -174,6 +175,55 @@ int nq_dequantize(const uint32_t *wq, const uint16_t *scales, const uint16_t *bi
     return from_cuda(nq::launch_dequantize(wq, scales, biases, rows, K, bits, group_size, out,
                                            static_cast<cudaStream_t>(stream)),
                      "nq_dequantize");
+}
+
+int nq_dequantize_f16(const uint32_t *wq, const uint16_t *scales, const uint16_t *biases,
+                      int64_t rows, int64_t K, int bits, int group_size, uint16_t *out,
+                      void *stream) {
+    const char *what = "nq_dequantize_f16";
+    if (int rc = check_quant(rows, K, bits, group_size, what)) return rc;
+    if (rows == 0) return NQ_SUCCESS;
+    if (!wq || !scales || !biases || !out)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": NULL tensor pointer");
+    if (!aligned16(wq) || !aligned16(out))
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": wq and out must be 16-byte aligned");
+    if (int rc = need_device(what)) return rc;
+    return from_cuda(nq::launch_dequantize(wq, scales, biases, rows, K, bits, group_size, out,
+                                           static_cast<cudaStream_t>(stream), true),
+                     what);
+}
+
+int nq_quantized_matmul_f16(const uint16_t *x, int64_t M, const uint32_t *wq,
+                            const uint16_t *scales, const uint16_t *biases, int64_t N, int64_t K,
+                            int bits, int group_size, uint16_t *y, void *stream) {
+    const char *what = "nq_quantized_matmul_f16";
+    if (int rc = check_quant(N, K, bits, group_size, what)) return rc;
+    if (M < 0) return fail(NQ_INVALID_INPUT, std::string(what) + ": M must be >= 0");
+    if (M == 0 || N == 0) return NQ_SUCCESS;
+    if (!x || !wq || !scales || !biases || !y)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": NULL tensor pointer");
+    if (!aligned16(x) || !aligned16(wq))
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": x and wq must be 16-byte aligned");
+    if (N > (1LL << 31) - 1 || M > (1LL << 31) - 1)
+        return fail(NQ_INVALID_INPUT, std::string(what) + ": shape too large");
+    if (int rc = need_device(what)) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (M <= 8 && bits == 4) {
+        const cudaError_t e = nq::launch_rows_f16(x, (int)M, wq, scales, biases, N, K, bits,
+                                                  group_size, y, st);
+        if (e != cudaErrorNotSupported) return from_cuda(e, what);
+    }
+    nq::TcGemmArgs a;
+    a.x = x; a.x_ld = K; a.M = M;
+    a.w = wq; a.s = scales; a.b = biases;
+    a.N = N; a.K = K; a.bits = bits; a.gs = group_size;
+    a.y = y; a.y_ld = N;
+    a.f16 = true;
+    if (!nq::tc_gemm_supported(a))
+        return fail(NQ_BACKEND_NOT_AVAILABLE,
+                    std::string(what) + ": shape not served (K*bits/8 and x rows must be "
+                                        "multiples of 16 bytes, and tensor maps available)");
+    return from_cuda(nq::launch_tc_gemm(a, st), what);
 }
 
 // M at or above which the tcgen05 GEMM replaces the mma.sync GEMV.

@@ -187,10 +187,15 @@ Result<void> lin(const DeviceTensor &x, const std::string &key, const WeightMap 
     const DeviceTensor *b = bit == wm.end() ? nullptr : &bit->second;
     if (w.dtype != DType::U32 && w.dtype != DType::I32)
         return std::unexpected(Error{ErrorCode::InvalidModel, key + ".weight: packed codes must be uint32"});
-    if (s.dtype != DType::BF16 || (b && b->dtype != DType::BF16))
+    // bf16 or fp16 scales (mlx_ops.h:33-39 passes whatever the checkpoint
+    // holds); the activations and the output take the scales' dtype
+    const bool f16 = s.dtype == DType::F16;
+    if ((s.dtype != DType::BF16 && !f16) || (b && b->dtype != s.dtype))
         return std::unexpected(Error{ErrorCode::InvalidModel,
-                                     key + ": scales and biases must be bf16 (the dequantized "
-                                           "values are bf16(bf16(s*q) + b))"});
+                                     key + ": scales and biases must both be bf16 or both fp16"});
+    if (x.dtype != s.dtype || y.dtype != s.dtype)
+        return std::unexpected(Error{ErrorCode::InvalidInput,
+                                     key + ": x and the output must have the scales' dtype"});
     const int nb = bits(w, s, gs);
     const int64_t K = x.dim(-1);
     if (K <= 0)
@@ -201,8 +206,11 @@ Result<void> lin(const DeviceTensor &x, const std::string &key, const WeightMap 
         return std::unexpected(Error{ErrorCode::InvalidInput, key + ": x/W inner dimension mismatch"});
     if (y.numel() != M * N)
         return std::unexpected(Error{ErrorCode::InvalidInput, key + ": output has the wrong size"});
-    const int st = nq_quantized_matmul(bf16p(x), M, u32p(w), bf16p(s), b ? bf16p(*b) : nullptr, N,
-                                       K, nb, gs, bf16p(y), stream);
+    const int st =
+        f16 ? nq_quantized_matmul_f16(bf16p(x), M, u32p(w), bf16p(s), b ? bf16p(*b) : nullptr, N,
+                                      K, nb, gs, bf16p(y), stream)
+            : nq_quantized_matmul(bf16p(x), M, u32p(w), bf16p(s), b ? bf16p(*b) : nullptr, N, K,
+                                  nb, gs, bf16p(y), stream);
     if (st != NQ_SUCCESS) return std::unexpected(nq_error(st, "lin(" + key + ")"));
     return {};
 }
@@ -214,8 +222,11 @@ Result<void> dequantize(const DeviceTensor &w, const DeviceTensor &scales,
     const int64_t K = w.dim(-1) * 32 / bits;
     if (out.numel() != rows * K)
         return std::unexpected(Error{ErrorCode::InvalidInput, "dequantize: wrong output size"});
-    const int st = nq_dequantize(u32p(w), bf16p(scales), bf16p(biases), rows, K, bits, gs,
-                                 bf16p(out), stream);
+    const int st = scales.dtype == DType::F16
+                       ? nq_dequantize_f16(u32p(w), bf16p(scales), bf16p(biases), rows, K, bits,
+                                           gs, bf16p(out), stream)
+                       : nq_dequantize(u32p(w), bf16p(scales), bf16p(biases), rows, K, bits, gs,
+                                       bf16p(out), stream);
     if (st != NQ_SUCCESS) return std::unexpected(nq_error(st, "dequantize"));
     return {};
 }

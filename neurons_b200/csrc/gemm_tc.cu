@@ -121,7 +121,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
 // SPLIT = false: one CTA per tile on the (weight tile, token tile) grid.
 // SPLIT = true: the tail -- a 1-D grid of prm.split CTAs per tile, for the
 // tiles from prm.main_tiles on.
-template <int BITS, int BM, bool SPLIT>
+template <int BITS, int BM, bool SPLIT, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_qgemm_kernel(const __grid_constant__ CUtensorMap tmap_x,
                     const __grid_constant__ CUtensorMap tmap_w,
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16_f32(kBlockW, BM);
+            constexpr uint32_t idesc = F16 ? idesc_f16_f32(kBlockW, BM) : idesc_bf16_f32(kBlockW, BM);
             for (int i = 0; i < num_kb; ++i) {
                 const int s = i % S;
                 const uint32_t ph = (uint32_t)(i / S) & 1u;
@@ -265,14 +265,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     wst + r * 32 + 16 * (h ^ ((r >> 2) & 1)));
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
-                const Dq4 d = make_dq4(sq[0], bq[0]);
+                const Dq4 d = F16 ? Dq4{} : make_dq4(sq[0], bq[0]);
+                const Dq4h dh = make_dq4h(sq[0], bq[0]);
                 const uint32_t words[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const uint32_t d0 = dq4_pair(q4_pair_biased(words[i], 0), d);  // (w0, w4)
-                    const uint32_t d1 = dq4_pair(q4_pair_biased(words[i], 1), d);  // (w1, w5)
-                    const uint32_t d2 = dq4_pair(q4_pair_biased(words[i], 2), d);  // (w2, w6)
-                    const uint32_t d3 = dq4_pair(q4_pair_biased(words[i], 3), d);  // (w3, w7)
+                    uint32_t d0, d1, d2, d3;
+                    if constexpr (F16) {
+                        d0 = dqh_pair(q4_pair_biased_h(words[i], 0), dh);
+                        d1 = dqh_pair(q4_pair_biased_h(words[i], 1), dh);
+                        d2 = dqh_pair(q4_pair_biased_h(words[i], 2), dh);
+                        d3 = dqh_pair(q4_pair_biased_h(words[i], 3), dh);
+                    } else {
+                        d0 = dq4_pair(q4_pair_biased(words[i], 0), d);  // (w0, w4)
+                        d1 = dq4_pair(q4_pair_biased(words[i], 1), d);  // (w1, w5)
+                        d2 = dq4_pair(q4_pair_biased(words[i], 2), d);  // (w2, w6)
+                        d3 = dq4_pair(q4_pair_biased(words[i], 3), d);  // (w3, w7)
+                    }
                     out[4 * i + 0] = prmt(d0, d1, 0x5410u);  // (w0, w1)
                     out[4 * i + 1] = prmt(d2, d3, 0x5410u);  // (w2, w3)
                     out[4 * i + 2] = prmt(d0, d1, 0x7632u);  // (w4, w5)
@@ -286,12 +295,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *reinterpret_cast<const uint4 *>(wst + r * 64 + 16 * ((2 * h + 1) ^ x));
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
-                const Dq8 d = make_dq8(sq[0], bq[0]);
                 const uint32_t words[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                if constexpr (F16) {
+                    const Dq4h dh = make_dq4h(sq[0], bq[0]);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    out[2 * i + 0] = dq8_pair(words[i], 0, 1, d);
-                    out[2 * i + 1] = dq8_pair(words[i], 2, 3, d);
+                    for (int i = 0; i < 8; ++i) {
+                        out[2 * i + 0] = dqh_pair(q8_pair_biased_h(words[i], 0, 1), dh);
+                        out[2 * i + 1] = dqh_pair(q8_pair_biased_h(words[i], 2, 3), dh);
+                    }
+                } else {
+                    const Dq8 d = make_dq8(sq[0], bq[0]);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        out[2 * i + 0] = dq8_pair(words[i], 0, 1, d);
+                        out[2 * i + 1] = dq8_pair(words[i], 2, 3, d);
+                    }
                 }
             }
             tmem_st_32x32b_x16(tmem_base + t_lane + (uint32_t)(Cfg::kACol0 + s * 32 + 16 * h), out);
@@ -337,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
                         *reinterpret_cast<uint16_t *>(stage + ((c0 + j) * kBlockW + r) * 2) =
-                            f32_to_bf16(__uint_as_float(acc[j]));
+                            f32_to_t16<F16>(__uint_as_float(acc[j]));
                 }
             }
             fence_proxy_async_smem();
@@ -363,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
                         *reinterpret_cast<uint16_t *>(stage + ((c0 + j) * kBlockW + r) * 2) =
-                            f32_to_bf16(__uint_as_float(acc[j]));
+                            f32_to_t16<F16>(__uint_as_float(acc[j]));
                 }
             }
             bar_sync(1, 16 * 32);
@@ -401,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int64_t m = m0 + c0 + j;
                         if (m < prm.M)
                             push_store(prm.push, prm.y + m * prm.y_ld + nrow,
-                                       f32_to_bf16(__uint_as_float(acc[j])));
+                                       f32_to_t16<F16>(__uint_as_float(acc[j])));
                     }
                 }
             }
@@ -436,12 +454,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!store_ok || m >= prm.M) continue;
             uint16_t *dst = prm.y + m * prm.y_ld + nr;
             if (nr + 4 <= prm.N && (reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
-                const uint2 pk = make_uint2(pack_bf2(v.x, v.y), pack_bf2(v.z, v.w));
+                const uint2 pk = make_uint2(pack_t2<F16>(v.x, v.y), pack_t2<F16>(v.z, v.w));
                 push_store(prm.push, reinterpret_cast<uint2 *>(dst), pk);
             } else {
                 const float e[4] = {v.x, v.y, v.z, v.w};
                 for (int i = 0; i < 4; ++i)
-                    if (nr + i < prm.N) push_store(prm.push, dst + i, f32_to_bf16(e[i]));
+                    if (nr + i < prm.N) push_store(prm.push, dst + i, f32_to_t16<F16>(e[i]));
             }
         }
         cluster_sync_all();  // the peers' reads of this CTA's partial are done
@@ -778,7 +796,7 @@ int max_clusters(int S) {
     }
     std::lock_guard<std::mutex> lk(mu);
     if (cache[d][S] == 0) {
-        auto kern = tc_qgemm_kernel<BITS, BM, true>;
+        auto kern = tc_qgemm_kernel<BITS, BM, true, false>;
         int clusters = 0;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  Cfg::kSmemBytes) == cudaSuccess) {
@@ -819,12 +837,14 @@ void plan_bm(const TcGemmArgs &a, int64_t *main_tiles, int *split) {
     }
 }
 
-template <int BITS, int BM>
+template <int BITS, int BM, bool F16>
 cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
     using Cfg = TcCfg<BITS, BM>;
+    constexpr CUtensorMapDataType kT16 =
+        F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     CUtensorMap mx, mw;
     const uint64_t Kw = (uint64_t)a.K * BITS / 32;
-    if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M,
+    if (!make_map_2d(&mx, kT16, a.x, (uint64_t)a.K, (uint64_t)a.M,
                      (uint64_t)a.x_ld * 2, kBlockK, BM, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
     if (!make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w, Kw, (uint64_t)a.N, Kw * 4,
@@ -833,7 +853,7 @@ cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
         return cudaErrorInvalidValue;
     CUtensorMap my;
     const bool y_map = !a.push && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 && a.y_ld % 8 == 0 &&
-                       make_map_2d(&my, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.y, (uint64_t)a.N,
+                       make_map_2d(&my, kT16, a.y, (uint64_t)a.N,
                                    (uint64_t)a.M, (uint64_t)a.y_ld * 2, kBlockW, BM,
                                    CU_TENSOR_MAP_SWIZZLE_NONE);
     if (!y_map) my = mx;  // unused
@@ -863,7 +883,7 @@ cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
     // work on the stream), then the whole tiles on the (weight tile, token tile)
     // grid as its programmatic dependent, so that they run beside the tail.
     if (prm.split > 1) {
-        cudaError_t e = cudaFuncSetAttribute(tc_qgemm_kernel<BITS, BM, true>,
+        cudaError_t e = cudaFuncSetAttribute(tc_qgemm_kernel<BITS, BM, true, F16>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Cfg::kSmemBytes);
         if (e != cudaSuccess) return e;
@@ -879,13 +899,13 @@ cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
         attr.val.clusterDim.z = 1;
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, tc_qgemm_kernel<BITS, BM, true>, mx, mw, my, prm);
+        e = cudaLaunchKernelEx(&cfg, tc_qgemm_kernel<BITS, BM, true, F16>, mx, mw, my, prm);
         if (e != cudaSuccess) return e;
     }
     // Whole 256-token tiles go to the CTA-pair kernel when the tiles pair up
     // (an even number of 128-row weight tiles per token tile, an even count of
     // whole tiles) and the output leaves through the TMA-store epilogue.
-    if constexpr (BM == kPairTok) {
+    if constexpr (BM == kPairTok && !F16) {
         if (prm.main_tiles > 0 && pair_kernel_enabled() && n_tiles % 2 == 0 &&
             prm.main_tiles % 2 == 0 && prm.tma_store) {
             using PC = PairCfg<BITS>;
@@ -920,7 +940,7 @@ cudaError_t launch_bm(const TcGemmArgs &a, cudaStream_t stream) {
         }
     }
     if (prm.main_tiles > 0) {
-        auto kern = tc_qgemm_kernel<BITS, BM, false>;
+        auto kern = tc_qgemm_kernel<BITS, BM, false, F16>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Cfg::kSmemBytes);
         if (e != cudaSuccess) return e;
@@ -1008,12 +1028,19 @@ int tc_gemm_launches(const TcGemmArgs &a) {
     return a.bits == 4 ? launches_bits<4>(a) : launches_bits<8>(a);
 }
 
+template <bool F16>
+cudaError_t launch_tc_dt(const TcGemmArgs &a, cudaStream_t stream) {
+    if (a.M <= 64)
+        return a.bits == 4 ? launch_bm<4, 64, F16>(a, stream) : launch_bm<8, 64, F16>(a, stream);
+    if (a.M <= 128)
+        return a.bits == 4 ? launch_bm<4, 128, F16>(a, stream) : launch_bm<8, 128, F16>(a, stream);
+    return a.bits == 4 ? launch_bm<4, 256, F16>(a, stream) : launch_bm<8, 256, F16>(a, stream);
+}
+
 cudaError_t launch_tc_gemm(const TcGemmArgs &a, cudaStream_t stream) {
     if (!tc_gemm_supported(a)) return cudaErrorNotSupported;
-    if (a.M <= 64) return a.bits == 4 ? launch_bm<4, 64>(a, stream) : launch_bm<8, 64>(a, stream);
-    if (a.M <= 128)
-        return a.bits == 4 ? launch_bm<4, 128>(a, stream) : launch_bm<8, 128>(a, stream);
-    return a.bits == 4 ? launch_bm<4, 256>(a, stream) : launch_bm<8, 256>(a, stream);
+    if (a.f16 && a.push) return cudaErrorNotSupported;  // the fan-out is bf16 only
+    return a.f16 ? launch_tc_dt<true>(a, stream) : launch_tc_dt<false>(a, stream);
 }
 
 }  // namespace nq

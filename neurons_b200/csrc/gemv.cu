@@ -92,6 +92,15 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void mma16816h(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // Registers of one k-block of work for one warp: RT row tiles x rows {g, g+8}
 // x NACC weight sets.  Scales and biases are kept as zero-extended 16-bit values.
 template <int RT, int NACC>
@@ -1094,7 +1103,7 @@ __device__ __forceinline__ uint4 pair_permute(uint4 v) {
     return o;
 }
 
-template <int KBW>
+template <int KBW, bool F16>
 __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
     constexpr int XCH = KBW * 16;  // 16-byte x chunks per token in a warp's slice
     extern __shared__ __align__(16) uint4 rows_smem[];
@@ -1133,13 +1142,13 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
         const int m = q / XCH, ck = q % XCH;  // chunk ck of the slice covers codes kb0*128 + 8*ck ...
         const uint16_t *xr = p.x + (int64_t)m * p.x_ld + kb0 * 128 + ck * 8;
         uint4 v = ldg16(xr);
-        if (p.pro == kRowsSwiglu) {
+        if (!F16 && p.pro == kRowsSwiglu) {
             const uint4 u = ldg16(xr + p.K);  // x row = [gate (K) | up (K)]
             v.x = swiglu_pair(v.x, u.x);
             v.y = swiglu_pair(v.y, u.y);
             v.z = swiglu_pair(v.z, u.z);
             v.w = swiglu_pair(v.w, u.w);
-        } else if (p.pro == kRowsNorm) {
+        } else if (!F16 && p.pro == kRowsNorm) {
             const uint32_t e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -1151,7 +1160,7 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
         const int kbi = ck >> 4, cc = (ck >> 2) & 3, i = ck & 3;
         xs[m * XCH + kbi * 16 + i * 4 + cc] = pair_permute(v);
     }
-    if (p.pro == kRowsNorm) {
+    if (!F16 && p.pro == kRowsNorm) {
         // mean of x^2 over the whole row: every warp's slice, through shared
         // memory; then each lane normalises the chunks it staged
         __shared__ float ss_warp[16];
@@ -1180,27 +1189,48 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
         uint4 xv[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) xv[i] = xr[kbi * 16 + i * 4];
-        Dq4 da, db;
-        da.s2 = prmt(sv[kbi][0], 0u, 0x1010u);
-        da.b2 = prmt(bv[kbi][0], 0u, 0x1010u);
-        db.s2 = prmt(sv[kbi][1], 0u, 0x1010u);
-        db.b2 = prmt(bv[kbi][1], 0u, 0x1010u);
-        da.n2 = bf2_fma(da.s2, 0xC300C300u, 0x80008000u);  // exact -128*s
-        db.n2 = bf2_fma(db.s2, 0xC300C300u, 0x80008000u);
+        if constexpr (F16) {
+            // fp16 scales and biases: biased codes 1024 + q, exact fp16 dequant
+            const Dq4h da = make_dq4h((uint16_t)sv[kbi][0], (uint16_t)bv[kbi][0]);
+            const Dq4h db = make_dq4h((uint16_t)sv[kbi][1], (uint16_t)bv[kbi][1]);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint32_t w0 = (&wv[kbi][0].x)[i], w1 = (&wv[kbi][1].x)[i];
-            const uint32_t w04 = w0 >> 4, w14 = w1 >> 4;
-            const uint32_t a0 = dq4_pair(lop3_and_or(w0, 0x000F000Fu, 0x43004300u), da);
-            const uint32_t a1 = dq4_pair(lop3_and_or(w1, 0x000F000Fu, 0x43004300u), db);
-            const uint32_t a2 = dq4_pair(lop3_and_or(w04, 0x000F000Fu, 0x43004300u), da);
-            const uint32_t a3 = dq4_pair(lop3_and_or(w14, 0x000F000Fu, 0x43004300u), db);
-            const uint32_t c0 = dq4_pair(lop3_and_or(w0 >> 8, 0x000F000Fu, 0x43004300u), da);
-            const uint32_t c1 = dq4_pair(lop3_and_or(w1 >> 8, 0x000F000Fu, 0x43004300u), db);
-            const uint32_t c2 = dq4_pair(lop3_and_or(w04 >> 8, 0x000F000Fu, 0x43004300u), da);
-            const uint32_t c3 = dq4_pair(lop3_and_or(w14 >> 8, 0x000F000Fu, 0x43004300u), db);
-            mma16816(acc[0], a0, a1, a2, a3, xv[i].x, xv[i].y);
-            mma16816(acc[1], c0, c1, c2, c3, xv[i].z, xv[i].w);
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t w0 = (&wv[kbi][0].x)[i], w1 = (&wv[kbi][1].x)[i];
+                const uint32_t w04 = w0 >> 4, w14 = w1 >> 4;
+                const uint32_t a0 = dqh_pair(lop3_and_or(w0, 0x000F000Fu, 0x64006400u), da);
+                const uint32_t a1 = dqh_pair(lop3_and_or(w1, 0x000F000Fu, 0x64006400u), db);
+                const uint32_t a2 = dqh_pair(lop3_and_or(w04, 0x000F000Fu, 0x64006400u), da);
+                const uint32_t a3 = dqh_pair(lop3_and_or(w14, 0x000F000Fu, 0x64006400u), db);
+                const uint32_t c0 = dqh_pair(lop3_and_or(w0 >> 8, 0x000F000Fu, 0x64006400u), da);
+                const uint32_t c1 = dqh_pair(lop3_and_or(w1 >> 8, 0x000F000Fu, 0x64006400u), db);
+                const uint32_t c2 = dqh_pair(lop3_and_or(w04 >> 8, 0x000F000Fu, 0x64006400u), da);
+                const uint32_t c3 = dqh_pair(lop3_and_or(w14 >> 8, 0x000F000Fu, 0x64006400u), db);
+                mma16816h(acc[0], a0, a1, a2, a3, xv[i].x, xv[i].y);
+                mma16816h(acc[1], c0, c1, c2, c3, xv[i].z, xv[i].w);
+            }
+        } else {
+            Dq4 da, db;
+            da.s2 = prmt(sv[kbi][0], 0u, 0x1010u);
+            da.b2 = prmt(bv[kbi][0], 0u, 0x1010u);
+            db.s2 = prmt(sv[kbi][1], 0u, 0x1010u);
+            db.b2 = prmt(bv[kbi][1], 0u, 0x1010u);
+            da.n2 = bf2_fma(da.s2, 0xC300C300u, 0x80008000u);  // exact -128*s
+            db.n2 = bf2_fma(db.s2, 0xC300C300u, 0x80008000u);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t w0 = (&wv[kbi][0].x)[i], w1 = (&wv[kbi][1].x)[i];
+                const uint32_t w04 = w0 >> 4, w14 = w1 >> 4;
+                const uint32_t a0 = dq4_pair(lop3_and_or(w0, 0x000F000Fu, 0x43004300u), da);
+                const uint32_t a1 = dq4_pair(lop3_and_or(w1, 0x000F000Fu, 0x43004300u), db);
+                const uint32_t a2 = dq4_pair(lop3_and_or(w04, 0x000F000Fu, 0x43004300u), da);
+                const uint32_t a3 = dq4_pair(lop3_and_or(w14, 0x000F000Fu, 0x43004300u), db);
+                const uint32_t c0 = dq4_pair(lop3_and_or(w0 >> 8, 0x000F000Fu, 0x43004300u), da);
+                const uint32_t c1 = dq4_pair(lop3_and_or(w1 >> 8, 0x000F000Fu, 0x43004300u), db);
+                const uint32_t c2 = dq4_pair(lop3_and_or(w04 >> 8, 0x000F000Fu, 0x43004300u), da);
+                const uint32_t c3 = dq4_pair(lop3_and_or(w14 >> 8, 0x000F000Fu, 0x43004300u), db);
+                mma16816(acc[0], a0, a1, a2, a3, xv[i].x, xv[i].y);
+                mma16816(acc[1], c0, c1, c2, c3, xv[i].z, xv[i].w);
+            }
         }
     }
 #pragma unroll
@@ -1215,8 +1245,8 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
         const int m = 2 * c + (j & 1);
         const int64_t n = r0 + g + 8 * (j >> 1);
         if (m < M && n < p.N) {
-            uint16_t out = f32_to_bf16(v);
-            if (p.res)
+            uint16_t out = f32_to_t16<F16>(v);
+            if (!F16 && p.res)
                 out = f32_to_bf16(bf16_to_f32(p.res[(int64_t)m * p.res_ld + n]) + bf16_to_f32(out));
             p.y[(int64_t)m * p.y_ld + n] = out;
         }
@@ -1247,10 +1277,10 @@ int rows_kbw(int64_t kb_total, int64_t row_groups) {
     return 0;
 }
 
-template <int KBW>
+template <int KBW, bool F16>
 cudaError_t launch_rows(const RowsParams &p, int W, cudaStream_t stream) {
     const size_t smem = (size_t)W * p.M * KBW * 16 * 16 + (size_t)W * 4 * 32 * sizeof(float);
-    auto kern = qgemv_rows_kernel<KBW>;
+    auto kern = qgemv_rows_kernel<KBW, F16>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
@@ -1270,7 +1300,8 @@ cudaError_t launch_rows(const RowsParams &p, int W, cudaStream_t stream) {
 }
 
 // Checks shared by both entry points, then the kernel choice and launch.
-cudaError_t launch_rows_checked(RowsParams p, const void *x, cudaStream_t stream) {
+cudaError_t launch_rows_checked(RowsParams p, const void *x, cudaStream_t stream,
+                                bool f16 = false) {
     if (p.M < 1 || p.M > 8 || p.K % 128 || p.N < 1) return cudaErrorNotSupported;
     if ((reinterpret_cast<uintptr_t>(x) & 15) || p.x_ld % 8 || p.N > ((int64_t)1 << 31) * 16)
         return cudaErrorNotSupported;
@@ -1281,12 +1312,22 @@ cudaError_t launch_rows_checked(RowsParams p, const void *x, cudaStream_t stream
     const int kbw = rows_kbw(kb_total, (p.N + 15) / 16);
     if (!kbw) return cudaErrorNotSupported;
     const int W = (int)(kb_total / kbw);
+    if (f16) {
+        if (p.pro != kRowsPlain || p.res) return cudaErrorNotSupported;
+        switch (kbw) {
+            case 2: return launch_rows<2, true>(p, W, stream);
+            case 3: return launch_rows<3, true>(p, W, stream);
+            case 4: return launch_rows<4, true>(p, W, stream);
+            case 6: return launch_rows<6, true>(p, W, stream);
+            default: return launch_rows<8, true>(p, W, stream);
+        }
+    }
     switch (kbw) {
-        case 2: return launch_rows<2>(p, W, stream);
-        case 3: return launch_rows<3>(p, W, stream);
-        case 4: return launch_rows<4>(p, W, stream);
-        case 6: return launch_rows<6>(p, W, stream);
-        default: return launch_rows<8>(p, W, stream);
+        case 2: return launch_rows<2, false>(p, W, stream);
+        case 3: return launch_rows<3, false>(p, W, stream);
+        case 4: return launch_rows<4, false>(p, W, stream);
+        case 6: return launch_rows<6, false>(p, W, stream);
+        default: return launch_rows<8, false>(p, W, stream);
     }
 }
 
@@ -1333,6 +1374,13 @@ cudaError_t try_launch_rows(const GemvProblems &q, cudaStream_t stream) {
 bool rows_fused_supported(int64_t N, int64_t K, int bits) {
     return bits == 4 && N >= 1 && K % 128 == 0 && K * 2 <= 96 * 1024 &&
            N <= ((int64_t)1 << 31) * 16 && rows_kbw(K / 128, (N + 15) / 16) != 0;
+}
+
+cudaError_t launch_rows_f16(const uint16_t *x, int M, const uint32_t *w, const uint16_t *s,
+                            const uint16_t *b, int64_t N, int64_t K, int bits, int gs, uint16_t *y,
+                            cudaStream_t stream) {
+    if (bits != 4) return cudaErrorNotSupported;
+    return launch_rows_checked(rows_params(w, s, b, N, K, gs, x, K, M, y, N), x, stream, true);
 }
 
 cudaError_t launch_rows_fused(const RowsFusedArgs &a, cudaStream_t stream) {

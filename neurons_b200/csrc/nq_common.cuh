@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -125,6 +126,89 @@ __device__ __forceinline__ uint32_t dq8_pair(uint32_t w, int i0, int i1, const D
     const float pa = __fmaf_rn(__uint_as_float(fa), d.s, d.n);
     const float pb = __fmaf_rn(__uint_as_float(fb), d.s, d.n);
     return bf2_add(pack_bf2(pa, pb), d.b2);
+}
+
+// ------------------------------------------------------------------ fp16x2
+// The same exact dequantization for fp16 scales and biases (fp16 checkpoints):
+//   t = fp16x2(1024+q_a, 1024+q_b) (exact for q < 1024), t - 1024 = q exactly,
+//   mul.rn(q, s) = fp16(s*q) (one rounding of the exact product), add.rn(., b)
+//   = fp16(fp16(s*q) + b) -- MLX's dequantized fp16 value bit for bit.
+
+__device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t h2_mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t h2_add(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint16_t f32_to_f16(float f) {
+    const __half h = __float2half_rn(f);
+    return *reinterpret_cast<const uint16_t *>(&h);
+}
+
+__device__ __forceinline__ float f16_to_f32(uint16_t h) {
+    return __half2float(*reinterpret_cast<const __half *>(&h));
+}
+
+// 16-bit storage type T of activations, scales and biases: bf16 or fp16
+template <bool F16>
+__device__ __forceinline__ uint16_t f32_to_t16(float f) {
+    if constexpr (F16) return f32_to_f16(f);
+    else return f32_to_bf16(f);
+}
+
+template <bool F16>
+__device__ __forceinline__ float t16_to_f32(uint16_t h) {
+    if constexpr (F16) return f16_to_f32(h);
+    else return bf16_to_f32(h);
+}
+
+template <bool F16>
+__device__ __forceinline__ uint32_t pack_t2(float lo, float hi) {
+    if constexpr (F16) {
+        uint32_t d;
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+        return d;
+    } else {
+        return pack_bf2(lo, hi);
+    }
+}
+
+struct Dq4h {
+    uint32_t s2, b2;  // (s,s), (b,b) as fp16x2
+};
+
+__device__ __forceinline__ Dq4h make_dq4h(uint16_t s, uint16_t b) {
+    Dq4h d;
+    d.s2 = (uint32_t)s | ((uint32_t)s << 16);
+    d.b2 = (uint32_t)b | ((uint32_t)b << 16);
+    return d;
+}
+
+// biased codes t = (1024 + q_a, 1024 + q_b) -> dequantized fp16x2
+__device__ __forceinline__ uint32_t dqh_pair(uint32_t t, const Dq4h &d) {
+    return h2_add(h2_mul(h2_sub(t, 0x64006400u), d.s2), d.b2);
+}
+
+// pair j of a 4-bit word: (q_j, q_{j+4}) biased to fp16 1024+q
+__device__ __forceinline__ uint32_t q4_pair_biased_h(uint32_t w, int j) {
+    return lop3_and_or(w >> (4 * j), 0x000F000Fu, 0x64006400u);
+}
+
+// bytes i0, i1 of w -> biased fp16x2 (1024 + byte)
+__device__ __forceinline__ uint32_t q8_pair_biased_h(uint32_t w, int i0, int i1) {
+    return prmt(w, 0x64646464u, (uint32_t)i0 | 0x40u | ((uint32_t)i1 << 8) | 0x4000u);
 }
 
 // --------------------------------------------------------------- mbarrier
@@ -291,6 +375,13 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t smem_addr) {
     d |= (uint64_t)1u << 46;              // descriptor version (sm_100)
     d |= (uint64_t)2u << 61;              // SWIZZLE_128B
     return d;
+}
+
+// Instruction descriptor, kind::f16: fp16 A/B (format 0), fp32 D, both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int mma_m, int mma_n) {
+    return (1u << 4)                              // D format f32
+           | ((uint32_t)(mma_n >> 3) << 17)       // N >> 3
+           | ((uint32_t)(mma_m >> 4) << 24);      // M >> 4
 }
 
 // Instruction descriptor, kind::f16: bf16 A/B, fp32 D, both K-major.

@@ -86,6 +86,11 @@ struct RowsFusedArgs {
     int64_t res_ld = 0;
 };
 cudaError_t launch_rows_fused(const RowsFusedArgs &a, cudaStream_t stream);
+// fp16 x, scales, biases and y (an fp16 checkpoint), M <= 8, 4-bit codes:
+// the row-group kernel; cudaErrorNotSupported when it does not serve the shape.
+cudaError_t launch_rows_f16(const uint16_t *x, int M, const uint32_t *w, const uint16_t *s,
+                            const uint16_t *b, int64_t N, int64_t K, int bits, int gs, uint16_t *y,
+                            cudaStream_t stream);
 // Whether launch_rows_fused serves an N x K weight at M == 1 (host only).
 bool rows_fused_supported(int64_t N, int64_t K, int bits);
 
@@ -107,6 +112,7 @@ struct TcGemmArgs {
     uint16_t *y = nullptr;         // [M, N] bf16 (row stride y_ld)
     int64_t y_ld = 0;
     const PushDev *push = nullptr; // tensor-parallel fan-out of the stores
+    bool f16 = false;              // x, scales, biases and y are fp16 (else bf16)
 };
 
 bool tc_gemm_supported(const TcGemmArgs &a);
@@ -153,9 +159,10 @@ cudaError_t launch_tc_moe(const TcMoeArgs &a, cudaStream_t stream);
 cudaError_t launch_quantize(const void *w, int w_dtype, int64_t rows, int64_t K, int bits,
                             int gs, int scheme, uint32_t *wq, uint16_t *s, uint16_t *b,
                             cudaStream_t stream);
+// f16: scales, biases and the output are fp16 (else bf16)
 cudaError_t launch_dequantize(const uint32_t *wq, const uint16_t *s, const uint16_t *b,
                               int64_t rows, int64_t K, int bits, int gs, uint16_t *out,
-                              cudaStream_t stream);
+                              cudaStream_t stream, bool f16 = false);
 
 size_t moe_workspace_bytes(int64_t T, int64_t E, int64_t top_k, int64_t H, int64_t I);
 size_t moe_partial_workspace_bytes(int64_t T, int64_t E, int64_t ne, int64_t top_k, int64_t H,

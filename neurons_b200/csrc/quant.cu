@@ -16,8 +16,9 @@
 namespace nq {
 namespace {
 
-// Quantize: one thread per 8 consecutive values along K.
-template <int BITS, bool IN_BF16>
+// Quantize: one thread per 8 consecutive values along K.  IN: 0 fp32, 1 bf16,
+// 2 fp16 weights; fp16 weights give fp16 scales and biases, the others bf16.
+template <int BITS, int IN>
 __global__ void __launch_bounds__(256) quantize_kernel(const void *__restrict__ w, int64_t rows,
                                                        int64_t K, int gs, int scheme,
                                                        uint32_t *__restrict__ wq,
@@ -35,14 +36,14 @@ __global__ void __launch_bounds__(256) quantize_kernel(const void *__restrict__ 
     const int64_t chunk = tt % chunks_per_row;
 
     float v[8];
-    if (IN_BF16) {
+    if (IN != 0) {
         const uint4 raw = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(w) +
                                                             row * K + chunk * 8);
         const uint32_t r[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            v[2 * i] = __uint_as_float(r[i] << 16);
-            v[2 * i + 1] = __uint_as_float(r[i] & 0xFFFF0000u);
+            v[2 * i] = t16_to_f32<IN == 2>((uint16_t)r[i]);
+            v[2 * i + 1] = t16_to_f32<IN == 2>((uint16_t)(r[i] >> 16));
         }
     } else {
         const float4 *src = reinterpret_cast<const float4 *>(static_cast<const float *>(w) +
@@ -103,20 +104,23 @@ __global__ void __launch_bounds__(256) quantize_kernel(const void *__restrict__ 
     }
     if ((chunk % lanes) == 0) {
         const int64_t gidx = row * (K / gs) + chunk / lanes;
-        scales[gidx] = f32_to_bf16(scale);
-        biases[gidx] = f32_to_bf16(bias);
+        scales[gidx] = f32_to_t16<IN == 2>(scale);
+        biases[gidx] = f32_to_t16<IN == 2>(bias);
     }
 }
 
-// MLX CPU dequantize of one code: bf16(bf16(s*q) + b), each step one rounding.
+// MLX CPU dequantize of one code in the scales' dtype T: T(T(s*q) + b), each
+// step one rounding.
+template <bool F16>
 __device__ __forceinline__ uint16_t dq_one(float s, float b, uint32_t q) {
-    const float p = bf16_to_f32(f32_to_bf16(__fmul_rn(s, (float)q)));
-    return f32_to_bf16(__fadd_rn(p, b));
+    const float p = t16_to_f32<F16>(f32_to_t16<F16>(__fmul_rn(s, (float)q)));
+    return f32_to_t16<F16>(__fadd_rn(p, b));
 }
 
 // Dequantize: one thread per 16 bytes of packed words (32 codes at 4 bits,
-// 16 codes at 8 bits); output 64 or 32 contiguous bytes.
-template <int BITS>
+// 16 codes at 8 bits); output 64 or 32 contiguous bytes of bf16 (fp16 when
+// the scales are fp16).
+template <int BITS, bool F16>
 __global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t *__restrict__ wq,
                                                          const uint16_t *__restrict__ scales,
                                                          const uint16_t *__restrict__ biases,
@@ -132,8 +136,8 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t *__restr
     const uint4 raw = *reinterpret_cast<const uint4 *>(wq + row * Kw + vec * 4);
     const int64_t k0 = vec * kCodes;
     const int64_t gidx = row * (K / gs) + k0 / gs;
-    const float s = bf16_to_f32(scales[gidx]);
-    const float b = bf16_to_f32(biases[gidx]);
+    const float s = t16_to_f32<F16>(scales[gidx]);
+    const float b = t16_to_f32<F16>(biases[gidx]);
     const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
     uint32_t outw[kCodes / 2];
 #pragma unroll
@@ -143,7 +147,7 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t *__restr
         const int c0 = 2 * i, c1 = 2 * i + 1;
         const uint32_t q0 = (words[c0 / per] >> (BITS * (c0 % per))) & mask;
         const uint32_t q1 = (words[c1 / per] >> (BITS * (c1 % per))) & mask;
-        outw[i] = (uint32_t)dq_one(s, b, q0) | ((uint32_t)dq_one(s, b, q1) << 16);
+        outw[i] = (uint32_t)dq_one<F16>(s, b, q0) | ((uint32_t)dq_one<F16>(s, b, q1) << 16);
     }
     uint4 *dst = reinterpret_cast<uint4 *>(out + row * K + k0);
 #pragma unroll
@@ -160,31 +164,36 @@ cudaError_t launch_quantize(const void *w, int w_dtype, int64_t rows, int64_t K,
     if (total == 0) return cudaSuccess;
     const int threads = 256;
     const dim3 grid((unsigned)((total + threads - 1) / threads));
+#define NQ_QUANT(B, IN) \
+    quantize_kernel<B, IN><<<grid, threads, 0, stream>>>(w, rows, K, gs, scheme, wq, s, b)
     if (bits == 4) {
-        if (w_dtype == 1)
-            quantize_kernel<4, true><<<grid, threads, 0, stream>>>(w, rows, K, gs, scheme, wq, s, b);
-        else
-            quantize_kernel<4, false><<<grid, threads, 0, stream>>>(w, rows, K, gs, scheme, wq, s, b);
+        if (w_dtype == 2) NQ_QUANT(4, 2);
+        else if (w_dtype == 1) NQ_QUANT(4, 1);
+        else NQ_QUANT(4, 0);
     } else {
-        if (w_dtype == 1)
-            quantize_kernel<8, true><<<grid, threads, 0, stream>>>(w, rows, K, gs, scheme, wq, s, b);
-        else
-            quantize_kernel<8, false><<<grid, threads, 0, stream>>>(w, rows, K, gs, scheme, wq, s, b);
+        if (w_dtype == 2) NQ_QUANT(8, 2);
+        else if (w_dtype == 1) NQ_QUANT(8, 1);
+        else NQ_QUANT(8, 0);
     }
+#undef NQ_QUANT
     return cudaGetLastError();
 }
 
 cudaError_t launch_dequantize(const uint32_t *wq, const uint16_t *s, const uint16_t *b,
                               int64_t rows, int64_t K, int bits, int gs, uint16_t *out,
-                              cudaStream_t stream) {
+                              cudaStream_t stream, bool f16) {
     const int64_t total = rows * (K * bits / 32 / 4);
     if (total == 0) return cudaSuccess;
     const int threads = 256;
     const dim3 grid((unsigned)((total + threads - 1) / threads));
-    if (bits == 4)
-        dequantize_kernel<4><<<grid, threads, 0, stream>>>(wq, s, b, rows, K, gs, out);
+    if (bits == 4 && f16)
+        dequantize_kernel<4, true><<<grid, threads, 0, stream>>>(wq, s, b, rows, K, gs, out);
+    else if (bits == 4)
+        dequantize_kernel<4, false><<<grid, threads, 0, stream>>>(wq, s, b, rows, K, gs, out);
+    else if (f16)
+        dequantize_kernel<8, true><<<grid, threads, 0, stream>>>(wq, s, b, rows, K, gs, out);
     else
-        dequantize_kernel<8><<<grid, threads, 0, stream>>>(wq, s, b, rows, K, gs, out);
+        dequantize_kernel<8, false><<<grid, threads, 0, stream>>>(wq, s, b, rows, K, gs, out);
     return cudaGetLastError();
 }
 

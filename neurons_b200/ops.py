@@ -57,47 +57,51 @@ def bits(w, s, gs):
 
 
 def quantize(w, group_size=64, bits=4, scheme=SCHEME_MLX_AFFINE, out=None):
-    """MLX affine quantize along the last axis; out: optional (wq, scales, biases)."""
-    _need(w, "w", (torch.float32, torch.bfloat16))
+    """MLX affine quantize along the last axis; out: optional (wq, scales, biases).
+    Scales and biases are bf16, or fp16 for fp16 weights (MLX keeps the dtype)."""
+    _need(w, "w", (torch.float32, torch.bfloat16, torch.float16))
     K = int(w.shape[-1])
     rows = w.numel() // K if K else 0
     lead = tuple(w.shape[:-1])
+    sdt = torch.float16 if w.dtype == torch.float16 else torch.bfloat16
     if out is None:
         wq = torch.empty(lead + (K * bits // 32,), dtype=torch.uint32, device=w.device)
-        s = torch.empty(lead + (K // group_size,), dtype=torch.bfloat16, device=w.device)
+        s = torch.empty(lead + (K // group_size,), dtype=sdt, device=w.device)
         b = torch.empty_like(s)
     else:
         wq, s, b = out
         _need(wq, "wq", _PACKED)
-        _need(s, "scales", (torch.bfloat16,))
-        _need(b, "biases", (torch.bfloat16,))
-    dt = 0 if w.dtype == torch.float32 else 1
+        _need(s, "scales", (sdt,))
+        _need(b, "biases", (sdt,))
+    dt = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}[w.dtype]
     check(lib().nq_quantize(_ptr(w), dt, rows, K, bits, group_size, scheme, _ptr(wq), _ptr(s),
                             _ptr(b), _stream()))
     return wq, s, b
 
 
 def dequantize(wq, scales, biases, group_size=64, bits=4, out=None):
+    """bf16 scales/biases -> bf16 weights; fp16 -> fp16 (MLX keeps the dtype)."""
     _need(wq, "w", _PACKED)
-    _need(scales, "scales", (torch.bfloat16,))
-    _need(biases, "biases", (torch.bfloat16,))
+    _need(scales, "scales", (torch.bfloat16, torch.float16))
+    _need(biases, "biases", (scales.dtype,))
     K = int(wq.shape[-1]) * 32 // bits
     rows = wq.numel() // int(wq.shape[-1])
     if out is None:
-        out = torch.empty(tuple(wq.shape[:-1]) + (K,), dtype=torch.bfloat16, device=wq.device)
-    check(lib().nq_dequantize(_ptr(wq), _ptr(scales), _ptr(biases), rows, K, bits, group_size,
-                              _ptr(out), _stream()))
+        out = torch.empty(tuple(wq.shape[:-1]) + (K,), dtype=scales.dtype, device=wq.device)
+    fn = lib().nq_dequantize_f16 if scales.dtype == torch.float16 else lib().nq_dequantize
+    check(fn(_ptr(wq), _ptr(scales), _ptr(biases), rows, K, bits, group_size, _ptr(out),
+             _stream()))
     return out
 
 
 def quantized_matmul(x, wq, scales, biases=None, transpose=True, group_size=64, bits=4, out=None):
     if not transpose:
         raise NQError(1, "quantized_matmul: only transpose=True (the MLX linear layout) is served")
-    _need(x, "x", (torch.bfloat16,))
+    _need(x, "x", (torch.bfloat16, torch.float16))
     _need(wq, "w", _PACKED)
-    _need(scales, "scales", (torch.bfloat16,))
+    _need(scales, "scales", (x.dtype,))
     if biases is not None:
-        _need(biases, "biases", (torch.bfloat16,))
+        _need(biases, "biases", (x.dtype,))
     K = int(x.shape[-1])
     M = x.numel() // K if K else 0
     N = int(wq.shape[0])
@@ -105,9 +109,10 @@ def quantized_matmul(x, wq, scales, biases=None, transpose=True, group_size=64, 
         raise NQError(1, f"quantized_matmul: x has K={K} but w holds "
                          f"{int(wq.shape[-1]) * 32 // bits} columns at {bits} bits")
     if out is None:
-        out = torch.empty(tuple(x.shape[:-1]) + (N,), dtype=torch.bfloat16, device=x.device)
-    check(lib().nq_quantized_matmul(_ptr(x), M, _ptr(wq), _ptr(scales), _ptr(biases), N, K, bits,
-                                    group_size, _ptr(out), _stream()))
+        out = torch.empty(tuple(x.shape[:-1]) + (N,), dtype=x.dtype, device=x.device)
+    fn = lib().nq_quantized_matmul_f16 if x.dtype == torch.float16 else lib().nq_quantized_matmul
+    check(fn(_ptr(x), M, _ptr(wq), _ptr(scales), _ptr(biases), N, K, bits, group_size,
+             _ptr(out), _stream()))
     return out
 
 

@@ -82,6 +82,53 @@ float or_bf16_to_f32(uint16_t h) {
 
 static float round_bf16(float f) { return or_bf16_to_f32(or_f32_to_bf16(f)); }
 
+/* ---------------------------------------------------------------- fp16
+ * IEEE binary16, round to nearest even (the conversion MLX and CUDA use for
+ * float16 tensors); fp16 checkpoints store scales and biases this way. */
+
+uint16_t or_f32_to_f16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    const uint32_t sign = (u >> 16) & 0x8000u, a = u & 0x7fffffffu;
+    if (a > 0x7f800000u) return (uint16_t)(sign | 0x7e00u);   /* NaN */
+    if (a >= 0x477ff000u) return (uint16_t)(sign | 0x7c00u);  /* >= 65520: inf */
+    if (a < 0x38800000u) {                                    /* below 2^-14: subnormal */
+        float af;
+        memcpy(&af, &a, 4);
+        const float r = rintf(af * 16777216.0f);              /* units of 2^-24, ties to even */
+        return (uint16_t)(sign | (uint32_t)r);
+    }
+    uint32_t h = ((((a >> 23) - 112u)) << 10) | ((a & 0x7fffffu) >> 13);
+    const uint32_t rem = a & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h += 1u;
+    return (uint16_t)(sign | h);
+}
+
+float or_f16_to_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    const uint32_t e = (h >> 10) & 0x1fu, m = h & 0x3ffu;
+    uint32_t u;
+    if (e == 0) {
+        float f = (float)m * (1.0f / 16777216.0f);             /* exact */
+        memcpy(&u, &f, 4);
+        u |= sign;
+    } else if (e == 31) {
+        u = sign | 0x7f800000u | (m << 13);
+    } else {
+        u = sign | ((e + 112u) << 23) | (m << 13);
+    }
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+static float round_f16(float f) { return or_f16_to_f32(or_f32_to_f16(f)); }
+
+/* 16-bit storage types of activations, scales and biases */
+static float half_to_f32(uint16_t v, int f16) { return f16 ? or_f16_to_f32(v) : or_bf16_to_f32(v); }
+static uint16_t f32_to_half(float v, int f16) { return f16 ? or_f32_to_f16(v) : or_f32_to_bf16(v); }
+static float round_half(float v, int f16) { return f16 ? round_f16(v) : round_bf16(v); }
+
 /* mlx_ops::bits (compute/src/compute/model/mlx_ops.h:20-25):
  * bits = round(32 * (w_cols / s_cols) / gs), or 4 when that is not positive. */
 int or_bits_from_shapes(int64_t w_cols, int64_t s_cols, int group_size) {
@@ -142,14 +189,16 @@ static void quantize_group(const float *w, int gs, int bits, int scheme,
     *bias_out = bias;
 }
 
-/* w: [rows, K] fp32 (w_dtype 0) or bf16 bits (w_dtype 1).
- * wq: [rows, K*bits/32] uint32; scales, biases: [rows, K/gs] bf16 bits. */
+/* w: [rows, K] fp32 (w_dtype 0), bf16 bits (w_dtype 1) or fp16 bits
+ * (w_dtype 2).  wq: [rows, K*bits/32] uint32; scales, biases: [rows, K/gs],
+ * bf16 bits (fp16 bits for fp16 weights, as MLX keeps the weights' dtype). */
 int or_quantize(const void *w, int w_dtype, int64_t rows, int64_t K, int bits,
                 int gs, int scheme, uint32_t *wq, uint16_t *scales,
                 uint16_t *biases) {
-    if (check_quant_params(rows, K, bits, gs) || (w_dtype != 0 && w_dtype != 1) ||
+    if (check_quant_params(rows, K, bits, gs) || w_dtype < 0 || w_dtype > 2 ||
         (scheme != 0 && scheme != 1))
         return OR_INVALID;
+    const int f16 = w_dtype == 2;
     const int64_t groups = K / gs;
     const int64_t words = K * bits / 32;
     const int per_word = 32 / bits;
@@ -161,11 +210,11 @@ int or_quantize(const void *w, int w_dtype, int64_t rows, int64_t K, int bits,
             int64_t base = r * K + g * gs;
             for (int j = 0; j < gs; ++j)
                 buf[j] = w_dtype == 0 ? ((const float *)w)[base + j]
-                                      : or_bf16_to_f32(((const uint16_t *)w)[base + j]);
+                                      : half_to_f32(((const uint16_t *)w)[base + j], f16);
             float s, b;
             quantize_group(buf, gs, bits, scheme, codes, &s, &b);
-            scales[r * groups + g] = or_f32_to_bf16(s);
-            biases[r * groups + g] = or_f32_to_bf16(b);
+            scales[r * groups + g] = f32_to_half(s, f16);
+            biases[r * groups + g] = f32_to_half(b, f16);
             for (int wi = 0; wi < gs / per_word; ++wi) {
                 uint32_t word = 0;
                 for (int e = 0; e < per_word; ++e)
@@ -179,29 +228,36 @@ int or_quantize(const void *w, int w_dtype, int64_t rows, int64_t K, int bits,
 
 /* ---------------------------------------------------------- dequantize */
 
-/* MLX-CPU dequantize of one code: bf16(bf16(s*q) + b). */
-static inline float dq_value(float s, float b, uint32_t q) {
-    float p = round_bf16(s * (float)q);
-    return round_bf16(p + b);
+/* MLX-CPU dequantize of one code in the scales' dtype T (bf16 or fp16):
+ * T(T(s*q) + b), each op computed in fp32 and rounded to T. */
+static inline float dq_value_dt(float s, float b, uint32_t q, int f16) {
+    float p = round_half(s * (float)q, f16);
+    return round_half(p + b, f16);
 }
 
-static void dequant_row_f32(const uint32_t *wq_row, const uint16_t *s_row,
-                            const uint16_t *b_row, int64_t K, int bits, int gs,
-                            float *out) {
+static void dequant_row_dt(const uint32_t *wq_row, const uint16_t *s_row,
+                           const uint16_t *b_row, int64_t K, int bits, int gs,
+                           float *out, int f16) {
     const int per_word = 32 / bits;
     const uint32_t mask = (1u << bits) - 1u;
     for (int64_t k = 0; k < K; ++k) {
         uint32_t word = wq_row[k / per_word];
         uint32_t q = (word >> (bits * (k % per_word))) & mask;
-        float s = or_bf16_to_f32(s_row[k / gs]);
-        float b = b_row ? or_bf16_to_f32(b_row[k / gs]) : 0.0f;
-        out[k] = dq_value(s, b, q);
+        float s = half_to_f32(s_row[k / gs], f16);
+        float b = b_row ? half_to_f32(b_row[k / gs], f16) : 0.0f;
+        out[k] = dq_value_dt(s, b, q, f16);
     }
 }
 
-int or_dequantize(const uint32_t *wq, const uint16_t *scales,
-                  const uint16_t *biases, int64_t rows, int64_t K, int bits,
-                  int gs, uint16_t *out) {
+static void dequant_row_f32(const uint32_t *wq_row, const uint16_t *s_row,
+                            const uint16_t *b_row, int64_t K, int bits, int gs,
+                            float *out) {
+    dequant_row_dt(wq_row, s_row, b_row, K, bits, gs, out, 0);
+}
+
+static int dequantize_dt(const uint32_t *wq, const uint16_t *scales,
+                         const uint16_t *biases, int64_t rows, int64_t K, int bits,
+                         int gs, uint16_t *out, int f16) {
     if (check_quant_params(rows, K, bits, gs) || !biases) return OR_INVALID;
     const int64_t words = K * bits / 32, groups = K / gs;
 #pragma omp parallel
@@ -209,13 +265,26 @@ int or_dequantize(const uint32_t *wq, const uint16_t *scales,
         float *row = (float *)malloc(sizeof(float) * (size_t)K);
 #pragma omp for schedule(static)
         for (int64_t r = 0; r < rows; ++r) {
-            dequant_row_f32(wq + r * words, scales + r * groups, biases + r * groups,
-                            K, bits, gs, row);
-            for (int64_t k = 0; k < K; ++k) out[r * K + k] = or_f32_to_bf16(row[k]);
+            dequant_row_dt(wq + r * words, scales + r * groups, biases + r * groups,
+                           K, bits, gs, row, f16);
+            for (int64_t k = 0; k < K; ++k) out[r * K + k] = f32_to_half(row[k], f16);
         }
         free(row);
     }
     return OR_OK;
+}
+
+int or_dequantize(const uint32_t *wq, const uint16_t *scales,
+                  const uint16_t *biases, int64_t rows, int64_t K, int bits,
+                  int gs, uint16_t *out) {
+    return dequantize_dt(wq, scales, biases, rows, K, bits, gs, out, 0);
+}
+
+/* fp16 scales and biases: fp16 output. */
+int or_dequantize_f16(const uint32_t *wq, const uint16_t *scales,
+                      const uint16_t *biases, int64_t rows, int64_t K, int bits,
+                      int gs, uint16_t *out) {
+    return dequantize_dt(wq, scales, biases, rows, K, bits, gs, out, 1);
 }
 
 /* ----------------------------------------------------------------- qmm */
@@ -255,24 +324,24 @@ int or_max_threads(void) {
 
 /* y[M,N] = x[M,K] . w_hat[N,K]^T.  x, y bf16 bits; y32 (optional) receives the
  * unrounded sums as fp32.  nthreads <= 0 keeps the OpenMP default. */
-int or_qmm(const uint16_t *x, int64_t M, const uint32_t *wq,
-           const uint16_t *scales, const uint16_t *biases, int64_t N, int64_t K,
-           int bits, int gs, uint16_t *y, float *y32, int nthreads) {
+static int qmm_dt(const uint16_t *x, int64_t M, const uint32_t *wq,
+                  const uint16_t *scales, const uint16_t *biases, int64_t N, int64_t K,
+                  int bits, int gs, uint16_t *y, float *y32, int nthreads, int f16) {
     if (check_quant_params(N, K, bits, gs) || M < 0 || !biases) return OR_INVALID;
     set_threads(nthreads);
     const int64_t words = K * bits / 32, groups = K / gs;
     float *xf = (float *)malloc(sizeof(float) * (size_t)(M * K + 1));
-    for (int64_t i = 0; i < M * K; ++i) xf[i] = or_bf16_to_f32(x[i]);
+    for (int64_t i = 0; i < M * K; ++i) xf[i] = half_to_f32(x[i], f16);
 #pragma omp parallel
     {
         float *row = (float *)malloc(sizeof(float) * (size_t)K);
 #pragma omp for schedule(dynamic, 4)
         for (int64_t n = 0; n < N; ++n) {
-            dequant_row_f32(wq + n * words, scales + n * groups, biases + n * groups,
-                            K, bits, gs, row);
+            dequant_row_dt(wq + n * words, scales + n * groups, biases + n * groups,
+                           K, bits, gs, row, f16);
             for (int64_t m = 0; m < M; ++m) {
                 double acc = dot_f32_f64(xf + m * K, row, K);
-                if (y) y[m * N + n] = or_f32_to_bf16((float)acc);
+                if (y) y[m * N + n] = f32_to_half((float)acc, f16);
                 if (y32) y32[m * N + n] = (float)acc;
             }
         }
@@ -280,6 +349,19 @@ int or_qmm(const uint16_t *x, int64_t M, const uint32_t *wq,
     }
     free(xf);
     return OR_OK;
+}
+
+int or_qmm(const uint16_t *x, int64_t M, const uint32_t *wq,
+           const uint16_t *scales, const uint16_t *biases, int64_t N, int64_t K,
+           int bits, int gs, uint16_t *y, float *y32, int nthreads) {
+    return qmm_dt(x, M, wq, scales, biases, N, K, bits, gs, y, y32, nthreads, 0);
+}
+
+/* fp16 x, scales, biases and y (an fp16 checkpoint's activations). */
+int or_qmm_f16(const uint16_t *x, int64_t M, const uint32_t *wq,
+               const uint16_t *scales, const uint16_t *biases, int64_t N, int64_t K,
+               int bits, int gs, uint16_t *y, float *y32, int nthreads) {
+    return qmm_dt(x, M, wq, scales, biases, N, K, bits, gs, y, y32, nthreads, 1);
 }
 
 /* MLX gather_qmm with transpose=true:

@@ -40,6 +40,12 @@ def lib():
         _lib.or_moe_combine.argtypes = [P, I64, I64, I64, I64, I64, P, P, P, P, P,
                                         I, I, I, P, I]
         _lib.or_max_threads.argtypes = []
+        _lib.or_f32_to_f16.restype = ctypes.c_uint16
+        _lib.or_f32_to_f16.argtypes = [ctypes.c_float]
+        _lib.or_f16_to_f32.restype = ctypes.c_float
+        _lib.or_f16_to_f32.argtypes = [ctypes.c_uint16]
+        _lib.or_dequantize_f16.argtypes = [P, P, P, I64, I64, I, I, P]
+        _lib.or_qmm_f16.argtypes = [P, I64, P, P, P, I64, I64, I, I, P, P, I]
     return _lib
 
 
@@ -64,15 +70,16 @@ def bits_from_shapes(w_cols: int, s_cols: int, group_size: int) -> int:
     return lib().or_bits_from_shapes(w_cols, s_cols, group_size)
 
 
-def quantize(w, bits=4, group_size=64, scheme=SCHEME_MLX):
-    """w: [rows, K] float32 or bf16-bits uint16 -> (wq uint32, scales u16, biases u16)."""
+def quantize(w, bits=4, group_size=64, scheme=SCHEME_MLX, f16=False):
+    """w: [rows, K] float32, bf16-bits uint16, or (f16=True) fp16-bits uint16 ->
+    (wq uint32, scales u16, biases u16); fp16 weights give fp16 scales/biases."""
     w = np.ascontiguousarray(w)
     if w.dtype == np.float32:
         dt = 0
     elif w.dtype == np.uint16:
-        dt = 1
+        dt = 2 if f16 else 1
     else:
-        raise TypeError("w must be float32 or bf16 bits (uint16)")
+        raise TypeError("w must be float32 or 16-bit bit patterns (uint16)")
     rows, K = w.shape
     wq = np.zeros((rows, K * bits // 32), np.uint32)
     s = np.zeros((rows, K // group_size), np.uint16)
@@ -82,26 +89,40 @@ def quantize(w, bits=4, group_size=64, scheme=SCHEME_MLX):
     return wq, s, b
 
 
-def dequantize(wq, scales, biases, bits=4, group_size=64):
+def dequantize(wq, scales, biases, bits=4, group_size=64, f16=False):
+    """f16=True: fp16 scales/biases bit patterns, fp16 output."""
     wq, scales, biases = _c(wq, np.uint32), _c(scales, np.uint16), _c(biases, np.uint16)
     rows = wq.shape[0]
     K = wq.shape[1] * 32 // bits
     out = np.zeros((rows, K), np.uint16)
-    _check(lib().or_dequantize(_p(wq), _p(scales), _p(biases), rows, K, bits,
-                               group_size, _p(out)), "dequantize")
+    fn = lib().or_dequantize_f16 if f16 else lib().or_dequantize
+    _check(fn(_p(wq), _p(scales), _p(biases), rows, K, bits, group_size, _p(out)), "dequantize")
     return out
 
 
-def qmm(x, wq, scales, biases, bits=4, group_size=64, nthreads=0, want_f32=False):
-    """y = x . dequant(w)^T ; x [M,K] bf16 bits -> y [M,N] bf16 bits (and fp32 sums)."""
+def f32_to_f16(a):
+    """fp32 -> fp16 bit patterns, round to nearest even (the oracle's C conversion)."""
+    a = np.asarray(a, np.float32)
+    f = lib().or_f32_to_f16
+    return np.array([f(float(v)) for v in a.reshape(-1)], np.uint16).reshape(a.shape)
+
+
+def f16_to_f32(h):
+    return np.ascontiguousarray(h, np.uint16).view(np.float16).astype(np.float32)
+
+
+def qmm(x, wq, scales, biases, bits=4, group_size=64, nthreads=0, want_f32=False, f16=False):
+    """y = x . dequant(w)^T ; x [M,K] bf16 bits -> y [M,N] bf16 bits (and fp32 sums);
+    f16=True: x, scales, biases and y are fp16 bit patterns."""
     x, wq = _c(x, np.uint16), _c(wq, np.uint32)
     scales, biases = _c(scales, np.uint16), _c(biases, np.uint16)
     M, K = x.shape
     N = wq.shape[0]
     y = np.zeros((M, N), np.uint16)
     y32 = np.zeros((M, N), np.float32) if want_f32 else None
-    _check(lib().or_qmm(_p(x), M, _p(wq), _p(scales), _p(biases), N, K, bits,
-                        group_size, _p(y), _p(y32), nthreads), "qmm")
+    fn = lib().or_qmm_f16 if f16 else lib().or_qmm
+    _check(fn(_p(x), M, _p(wq), _p(scales), _p(biases), N, K, bits,
+              group_size, _p(y), _p(y32), nthreads), "qmm")
     return (y, y32) if want_f32 else y
 
 

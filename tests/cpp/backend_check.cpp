@@ -109,7 +109,11 @@ int main(int argc, char **argv) {
         cudaMalloc(&xd, xh.size() * 2);
         cudaMalloc(&yd, (size_t)M * N * 2);
         cudaMemcpy(xd, xh.data(), xh.size() * 2, cudaMemcpyHostToDevice);
-        DeviceTensor x{xd, {M, K}, DType::BF16}, y{yd, {M, N}, DType::BF16};
+        // activations take the scales' dtype (bf16, or fp16 for an fp16 checkpoint)
+        auto sit = w->map().find(key + ".scales");
+        const DType act = sit != w->map().end() && sit->second.dtype == DType::F16 ? DType::F16
+                                                                                  : DType::BF16;
+        DeviceTensor x{xd, {M, K}, act}, y{yd, {M, N}, act};
         const auto &qc = load_quantization_config(argv[2]);
         const int gs = qc && *qc ? (*qc)->group_size : 64;
         auto r = cuda_ops::lin(x, key, w->map(), gs, y, be.stream());

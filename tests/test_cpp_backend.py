@@ -168,3 +168,26 @@ def test_lin_dense_weight_falls_back_to_matmul(checker, oracle, tmp_path):
     y = np.fromfile(tmp_path / "y.bin", np.uint16).reshape(M, N)
     ref = oracle.bf16_to_f32(x).astype(np.float64) @ oracle.bf16_to_f32(w).astype(np.float64).T
     assert_close(y, oracle.f32_to_bf16(ref.astype(np.float32)), "dense lin")
+
+
+@pytest.mark.gpu
+def test_lin_over_f16_checkpoint(checker, oracle, tmp_path):
+    """A checkpoint whose scales and biases are F16 goes through cuda_ops::lin
+    with fp16 activations (M=5: the tcgen05 path; the C++ checker passes x in
+    the scales' dtype)."""
+    from test_gpu_f16 import assert_close_f16, f16_bits
+    rng = np.random.default_rng(21)
+    N, K, M, bits, gs = 192, 1024, 5, 4, 64
+    wq, s, b = oracle.quantize(f16_bits(weights(rng, N, K)), bits, gs, 0, f16=True)
+    key = "model.layers.0.self_attn.o_proj"
+    write_safetensors(tmp_path / "model.safetensors",
+                      {key + ".weight": ("U32", wq), key + ".scales": ("F16", s),
+                       key + ".biases": ("F16", b)})
+    (tmp_path / "config.json").write_text(json.dumps(
+        {"model_type": "llama", "quantization": {"group_size": gs, "bits": bits}}))
+    x = f16_bits(rng.standard_normal((M, K)))
+    x.tofile(tmp_path / "x.bin")
+    out = checker("lin", tmp_path, key, tmp_path / "x.bin", M, K, tmp_path / "y.bin")
+    assert out[-1][:2] == ["lin", "ok"], out
+    y = np.fromfile(tmp_path / "y.bin", np.uint16).reshape(M, N)
+    assert_close_f16(y, oracle.qmm(x, wq, s, b, bits, gs, f16=True), "fp16 checkpoint lin")

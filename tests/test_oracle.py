@@ -153,3 +153,35 @@ def test_route_ties_prefer_lower_index(oracle):
     idx, sc = oracle.moe_route(logits, 2)
     np.testing.assert_array_equal(idx, [[1, 2]])
     np.testing.assert_allclose(sc, [[0.5, 0.5]], rtol=1e-7)
+
+
+def test_f16_conversion_matches_ieee_rne(oracle):
+    """The oracle's fp32 -> fp16 conversion (fp16 checkpoints) is IEEE
+    round-to-nearest-even, checked against numpy's float16 over normal,
+    subnormal, overflow and tie cases."""
+    rng = np.random.default_rng(5)
+    v = (rng.standard_normal(20000) * 10.0 ** rng.integers(-9, 6, 20000)).astype(np.float32)
+    edges = np.array([65504, 65519, 65520, 65536, 1e-8, 6e-8, 2.98e-8, 6.1e-5, 6.09e-5,
+                      1 + 2 ** -11, 1 + 3 * 2 ** -11, -0.0, 0.0, np.inf, -np.inf], np.float32)
+    v = np.concatenate([v, edges])
+    with np.errstate(over="ignore"):
+        ref = v.astype(np.float16).view(np.uint16)
+    np.testing.assert_array_equal(oracle.f32_to_f16(v), ref)
+
+
+def test_f16_dequant_and_qmm_follow_the_definition(oracle):
+    """fp16 dequant = fp16(fp16(s*q) + b) (numpy float16 ops round the same
+    way), and the fp16 qmm equals an fp64 dot over those values."""
+    rng = np.random.default_rng(6)
+    w = (rng.standard_normal((16, 256)) * 0.05).astype(np.float16)
+    wq, s, b = oracle.quantize(w.view(np.uint16), 4, 64, 0, f16=True)
+    dq = oracle.dequantize(wq, s, b, 4, 64, f16=True).view(np.float16)
+    codes = np.stack([(wq >> (4 * i)) & 15 for i in range(8)], axis=-1).reshape(16, 256)
+    sf = np.repeat(s.view(np.float16).astype(np.float32), 64, axis=1)
+    bf = np.repeat(b.view(np.float16).astype(np.float32), 64, axis=1)
+    ref = ((sf * codes).astype(np.float16).astype(np.float32) + bf).astype(np.float16)
+    np.testing.assert_array_equal(dq.view(np.uint16), ref.view(np.uint16))
+    x = rng.standard_normal((3, 256)).astype(np.float16)
+    y = oracle.qmm(x.view(np.uint16), wq, s, b, 4, 64, f16=True).view(np.float16)
+    yr = (x.astype(np.float64) @ dq.astype(np.float64).T).astype(np.float32).astype(np.float16)
+    np.testing.assert_array_equal(y, yr)
