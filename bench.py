@@ -426,7 +426,7 @@ def time_llama_step(prompt, tokens, world, seed, pk):
             "frac": byts * tokens_g / sec / 1e9 / pk["hbm_gbs"],
             "note": f"steps replayed from a CUDA graph of {per_graph} steps; launched from the "
                     f"host one by one: {sec_stream / tokens * 1e6:.0f} us/token",
-            "launches_per_token": 5 * c["layers"] + 3}
+            "launches_per_token": 5 * c["layers"] + 4}
 
 
 def replay_summary(t, tokens, rp, world, pk):
@@ -944,6 +944,12 @@ def ours(args):
     pk = peaks()
     if args.workload == "llama3b-decode":
         return ours_replay(args, world, rank, local, pk)
+    if args.workload == "quant":
+        # quantize and dequantize of the prefill weight alone
+        q = time_quant(args.steps, args.warmup, world, rank, pk)
+        if rank == 0:
+            print(json.dumps({"workload": "quant", **q}), flush=True)
+        return
     if args.workload == "llama3b-step":
         # the decode step alone (--steps tokens after a 128-token prompt)
         ls = time_llama_step(128, args.steps, world, rank, pk)
@@ -1213,7 +1219,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="prefill", choices=sorted(WORKLOADS) + ["llama3b-decode", "llama3b-step",
-                                                             "moe-1", "moe-64", "moe-2048"])
+                                                             "quant", "moe-1", "moe-64",
+                                                             "moe-2048"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-lines")
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE sub-line")

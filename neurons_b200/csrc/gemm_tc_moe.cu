@@ -68,6 +68,15 @@ struct MoeTcParams {
     int64_t y_ld;
     int h_map;                        // up: h leaves through tmap_h (16-row TMA stores)
     unsigned int *err;
+    // down, fused combine (fuse != 0): the last of a token's routed pairs to
+    // land in an n-block sums them (see the epilogue)
+    int fuse;
+    const int32_t *idx;               // [T, top_k] routing
+    const float *scores;              // [T, top_k]
+    int top_k, e0, ne;                // this call's experts [e0, e0 + ne)
+    int32_t *cnt;                     // [T, n-blocks] arrivals, zero at the start of the call
+    uint16_t *out;                    // y [T, N] bf16 (when ro.n == 0)
+    MoeRowsOut ro;                    // fp32 rows into other ranks' buffers (ro.n > 0)
 };
 
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
@@ -336,6 +345,67 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
+            if (prm.fuse) {
+                // Fused score-weighted combine.  Each of this tile's pairs
+                // counts itself in for its token and this n-block; the CTA
+                // that brings a token's count to its number of routed pairs
+                // sums the token's pairs, in slot order, exactly as the
+                // separate combine did -- so the result does not depend on
+                // which CTA finishes last.  No CTA waits for another.
+                int *list = reinterpret_cast<int *>(xs);  // the ring is idle now
+                int *nlist = list + kMaxTok;
+                __threadfence();  // this thread's d stores before its arrivals
+                if (threadIdx.x == 0) *nlist = 0;
+                bar_sync(9, 16 * 32);
+                if (ok && (int)threadIdx.x < cnt) {
+                    const int p = rows[threadIdx.x];
+                    const int t = p / prm.top_k;
+                    int kv = 0;
+                    for (int j = 0; j < prm.top_k; ++j) {
+                        const int l = prm.idx[(int64_t)t * prm.top_k + j] - prm.e0;
+                        kv += (l >= 0 && l < prm.ne) ? 1 : 0;
+                    }
+                    const int64_t ci = (int64_t)t * gridDim.x + blockIdx.x;
+                    if (atomicAdd(&prm.cnt[ci], 1) == kv - 1) {
+                        list[atomicAdd(nlist, 1)] = t;
+                        prm.cnt[ci] = 0;  // ready for the next call
+                    }
+                }
+                bar_sync(9, 16 * 32);
+                __threadfence();
+                const int L = *nlist;
+                const int64_t n = nbase + lane * 4;  // 4 columns per lane, 128 per warp
+                for (int i = warp; i < L; i += 16) {
+                    const int t = list[i];
+                    if (n >= prm.N) continue;
+                    float *ro_dst = nullptr;
+                    if (prm.ro.n > 0) {
+                        const int64_t q = t / prm.ro.per, r = t % prm.ro.per;
+                        if (r >= prm.ro.count[q]) continue;  // padding row
+                        ro_dst = prm.ro.dst[q] + (prm.ro.row0 + r) * prm.N + n;
+                    }
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int j = 0; j < prm.top_k; ++j) {
+                        const int64_t pj = (int64_t)t * prm.top_k + j;
+                        const int l = prm.idx[pj] - prm.e0;
+                        if (l < 0 || l >= prm.ne) continue;
+                        const float sc = bf16_to_f32(f32_to_bf16(prm.scores[pj]));
+                        const float4 v = __ldcg(reinterpret_cast<const float4 *>(dout + pj * prm.y_ld + n));
+                        acc.x = __fmaf_rn(sc, v.x, acc.x);
+                        acc.y = __fmaf_rn(sc, v.y, acc.y);
+                        acc.z = __fmaf_rn(sc, v.z, acc.z);
+                        acc.w = __fmaf_rn(sc, v.w, acc.w);
+                    }
+                    if (ro_dst) {
+                        *reinterpret_cast<float4 *>(ro_dst) = acc;
+                    } else {
+                        uint2 o;
+                        o.x = (uint32_t)f32_to_bf16(acc.x) | ((uint32_t)f32_to_bf16(acc.y) << 16);
+                        o.y = (uint32_t)f32_to_bf16(acc.z) | ((uint32_t)f32_to_bf16(acc.w) << 16);
+                        *reinterpret_cast<uint2 *>(prm.out + (int64_t)t * prm.N + n) = o;
+                    }
+                }
+            }
         }
     }
 
@@ -396,6 +466,15 @@ cudaError_t launch_cfg(const TcMoeArgs &a, cudaStream_t stream) {
     prm.y = a.y;
     prm.y_ld = a.y_ld;
     prm.err = device_error_word();
+    prm.fuse = !UP && a.fuse_cnt ? 1 : 0;
+    prm.idx = a.idx;
+    prm.scores = a.scores;
+    prm.top_k = a.top_k;
+    prm.e0 = a.e0;
+    prm.ne = (int)a.E;
+    prm.cnt = a.fuse_cnt;
+    prm.out = a.out;
+    prm.ro = a.ro;
     auto kern = tc_moe_kernel<BITS, UP>;
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);

@@ -1255,15 +1255,16 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
 
 // k-blocks per warp for the row-group kernel, 0 when it does not serve the
 // problem.  Few rows: short slices (more warps per row group finish the
-// post-dependency work sooner); many rows (several CTAs per SM anyway): long
-// slices, fewer warps and fewer partial sums.
+// post-dependency work sooner); many rows (at least 4 row groups per SM, so
+// several CTAs per SM anyway): long slices, fewer warps and fewer partial
+// sums.
 int rows_kbw(int64_t kb_total, int64_t row_groups) {
     static const int kShort[] = {2, 3, 4, 6, 8};
     static const int kLong[] = {8, 6, 4, 3, 2};
     auto fits = [&](int kbw, int64_t wmax) {
         return kb_total % kbw == 0 && kb_total / kbw >= 4 && kb_total / kbw <= wmax;
     };
-    if (row_groups >= 8 * (int64_t)sm_count()) {
+    if (row_groups >= 4 * (int64_t)sm_count()) {
         for (int kbw : kLong)
             if (fits(kbw, 16)) return kbw;
         return 0;

@@ -18,7 +18,8 @@
 // creation, so each is one GEMV launch; RMSNorm runs inside the following
 // GEMV's staging of x, SwiGLU inside the down projection's, and both
 // residual adds in the GEMVs' stores (launch_rows_fused).  Five launches per
-// layer: qkv, attention, o, gate/up, down.
+// layer: qkv, attention, o, gate/up, down; then the final norm, the LM head
+// and the argmax.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -35,7 +36,11 @@ namespace nq {
 namespace {
 
 constexpr int kAttnThreads = 128;
-constexpr int kAttnChunk = 64;  // positions per attention CTA
+// Positions per attention CTA, 8 per warp.  Measured per layer at the
+// Llama-3.2-3B dims, positions ~130-190, CUDA graph: chunks of 32 / 64 / 128
+// positions (8 / 16 / 32 per warp) take 7.9 / 11.3 / 17.5 us: the per-warp
+// chain of dependent work, not the merge of more partials, sets the time.
+constexpr int kAttnChunk = 32;
 constexpr int kMaxGroup = 8;     // query heads per KV head
 
 template <typename... Args>
@@ -255,6 +260,17 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
 #pragma unroll
     for (int k = 0; k < kDpl; ++k) vred[warp][dim0 + k] = acc[k];
     __syncthreads();
+    if (n_active == 1) {
+        // one chunk holds every position: its sums are the result (the merge
+        // below would compute the same values: a factor exp(0) = 1)
+        for (int d = tid; d < HD; d += kAttnThreads) {
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) v += vred[w][d];
+            a.out[(size_t)hq * HD + d] = f32_to_bf16(v / l);
+        }
+        return;
+    }
     const size_t pb = (size_t)hq * a.splits + s;
     for (int d = tid; d < HD; d += kAttnThreads) {
         float v = 0.f;
@@ -371,6 +387,30 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(
 
 __global__ void set_pos_kernel(int32_t *pos, int32_t v) { *pos = v; }
 
+// xn = bf16(w * bf16(x * 1/sqrt(mean(x^2) + eps))) for one row (MLX rms_norm
+// rounding, as the GEMV's fused prologue), one CTA.  Used before the LM head,
+// whose thousands of CTAs would each recompute the norm in a fused prologue.
+__global__ void __launch_bounds__(1024) rmsnorm_kernel(const uint16_t *x, const uint16_t *w,
+                                                       int64_t n, float eps, uint16_t *y) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ float part[32];
+    float ss = 0.f;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = bf16_to_f32(x[i]);
+        ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += part[i];
+    const float inv = 1.0f / sqrtf(tot / (float)n + eps);
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x)
+        y[i] = f32_to_bf16(bf16_to_f32(w[i]) * bf16_to_f32(f32_to_bf16(bf16_to_f32(x[i]) * inv)));
+}
+
 }  // namespace
 
 struct LlamaDecoder {
@@ -394,6 +434,7 @@ struct LlamaDecoder {
     // device state
     uint16_t *kc = nullptr, *vc = nullptr;  // [layers][n_kv][max_ctx][hd]
     uint16_t *h = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *logits = nullptr;
+    uint16_t *xn = nullptr;  // the final norm's output (LM head input)
     float *pm = nullptr, *pl = nullptr, *pacc = nullptr;
     int32_t *counter = nullptr, *pos = nullptr, *tok = nullptr;
     float *part_v = nullptr;  // argmax partials [kArgmaxBlocks]
@@ -521,8 +562,11 @@ cudaError_t llama_step(LlamaDecoder &d, const int32_t *tok_src, float *logits_f3
             cudaSuccess)
             return e;
     }
-    if ((e = gemv(d, d.h, H, d.head.w, d.head.scales, d.head.biases, c.vocab, H, d.logits, 1,
-                  d.final_norm, nullptr, st)) != cudaSuccess)
+    if ((e = launch_pdl_ll(rmsnorm_kernel, dim3(1), 1024, 0, st, (const uint16_t *)d.h,
+                           d.final_norm, H, c.rms_eps, d.xn)) != cudaSuccess)
+        return e;
+    if ((e = gemv(d, d.xn, H, d.head.w, d.head.scales, d.head.biases, c.vocab, H, d.logits, 0,
+                  nullptr, nullptr, st)) != cudaSuccess)
         return e;
     const unsigned ablocks =
         (unsigned)std::min<int64_t>(kArgmaxBlocks, (c.vocab + kArgmaxThreads - 1) / kArgmaxThreads);
@@ -603,6 +647,7 @@ cudaError_t llama_create(LlamaDecoder &d, const nq_llama_config_t &c,
     d.splits = (c.max_context + kAttnChunk - 1) / kAttnChunk;
     const size_t cache = (size_t)c.n_layers * c.n_kv_heads * c.max_context * hd;
     if ((e = d.alloc(&d.kc, cache)) || (e = d.alloc(&d.vc, cache)) || (e = d.alloc(&d.h, H)) ||
+        (e = d.alloc(&d.xn, H)) ||
         (e = d.alloc(&d.qkv, nq_ + 2 * nkv)) || (e = d.alloc(&d.attn, nq_)) ||
         (e = d.alloc(&d.gu, 2 * I)) || (e = d.alloc(&d.logits, (size_t)c.vocab)) ||
         (e = d.alloc(&d.pm, (size_t)c.n_heads * d.splits)) ||

@@ -6,10 +6,12 @@
 // (router :36-48, gather_qmm :69-74, SwiGLU :71, weighted sum :77-78), batched
 // over T tokens instead of the per-token loop at :479-486.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
 #include "nq.h"
+
 #include "nq_common.cuh"
 #include "nq_internal.h"
 
@@ -209,6 +211,11 @@ __global__ void combine_kernel(const float *__restrict__ d, const float *__restr
 
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
+bool fused_combine_enabled() {
+    const char *v = std::getenv("NQ_MOE_FUSED_COMBINE");
+    return v && v[0] == '1';
+}
+
 // Launch as a programmatic dependent of the previous kernel on the stream:
 // the kernel may start early and waits (griddepcontrol.wait) before it reads
 // what that kernel produced.
@@ -245,6 +252,7 @@ struct MoeWorkspace {
     uint16_t *h;
     float *d;
     uint16_t *xg;
+    int32_t *arrivals;  // [T, ceil(H/128)]: the tensor-core down kernel's fused combine
     size_t bytes;
 };
 
@@ -276,6 +284,9 @@ MoeWorkspace carve(void *base, int64_t T, int64_t E, int64_t top_k, int64_t H, i
     w.d = reinterpret_cast<float *>(take(sizeof(float) * P * H));
     w.xg = tc_pairs(P, E_total) ? reinterpret_cast<uint16_t *>(take(sizeof(uint16_t) * P * H))
                                 : nullptr;
+    w.arrivals = tc_pairs(P, E_total)
+                     ? reinterpret_cast<int32_t *>(take(sizeof(int32_t) * T * ((H + 127) / 128)))
+                     : nullptr;
     w.bytes = off;
     return w;
 }
@@ -349,6 +360,10 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
     if (grouped) {
         if ((e = cudaMemsetAsync(ws.counts, 0, sizeof(int32_t) * E, stream)) != cudaSuccess)
             return e;
+        if (use_tc && (e = cudaMemsetAsync(ws.arrivals, 0,
+                                           sizeof(int32_t) * T * ((H + 127) / 128), stream)) !=
+                          cudaSuccess)
+            return e;
         count_kernel<<<pblocks, thr, 0, stream>>>(idx, P, (int)E_total, (int)e0, (int)E, ws.counts,
                                                    err);
         scan_kernel<<<1, 1024, 0, stream>>>(ws.counts, (int)E, ws.offsets, ws.cursor,
@@ -389,7 +404,29 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
             d.rows = ws.pos_pair;
             d.y = ws.d;
             d.y_ld = H;
+            // The score-weighted combine can run in the down kernel itself
+            // (NQ_MOE_FUSED_COMBINE=1) when every token it must write has a
+            // routed pair there: the whole switch step (y) and the
+            // expert-parallel rows (ro; a token is sent only where one of its
+            // experts lives).  The fp32 partial of a shard (y_partial) keeps
+            // the combine kernel, which also writes the zero rows of tokens
+            // routed elsewhere.  Off by default: measured at T = 2048 (Qwen3
+            // dims) the fused step takes 512 us against 466 us, because each
+            // down CTA's arrival count and combine add round trips to its
+            // tail and the kernel is not persistent, so the tails of its ~14
+            // waves do not overlap.
+            const bool fuse = y_partial == nullptr && H % 4 == 0 && fused_combine_enabled();
+            if (fuse) {
+                d.fuse_cnt = ws.arrivals;
+                d.idx = idx;
+                d.scores = scores;
+                d.top_k = (int)top_k;
+                d.e0 = (int)e0;
+                d.out = y;
+                d.ro = ro;
+            }
             if ((e = launch_tc_moe(d, stream)) != cudaSuccess) return e;
+            if (fuse) return cudaSuccess;
             return launch_pdl(combine_kernel, cblocks, thr, stream, (const float *)ws.d, scores, idx,
                               (int)e0, (int)E, T, H, (int)top_k, y, y_partial, ro);
         }

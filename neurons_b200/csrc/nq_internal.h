@@ -131,6 +131,17 @@ int tc_gemm_launches(const TcGemmArgs &a);
 // True when cuTensorMapEncodeTiled could be resolved from the driver.
 bool tensor_maps_available();
 
+// Where the switch step of one expert shard writes its fp32 partial sums when
+// they go straight to the tokens' owners: the call's tokens are n regions of
+// `per` rows; token q * per + i goes to row row0 + i of dst[q] (rows i >=
+// count[q] are padding and are not written).  n == 0: not used.
+struct MoeRowsOut {
+    int n = 0;
+    int64_t per = 0, row0 = 0;
+    const int32_t *count = nullptr;  // [n], device memory
+    float *dst[8] = {};
+};
+
 // Expert-grouped tcgen05 GEMMs of the MoE switch step (gemm_tc_moe.cu).
 // A tile is {expert, first grouped row, token count <= kMoeTileTokens, 0}.
 constexpr int kMoeTileTokens = 256;
@@ -151,6 +162,15 @@ struct TcMoeArgs {
     int64_t max_tiles = 0;           // grid bound; CTAs past *n_tiles exit at once
     void *y = nullptr;               // up: h [P, N] bf16; down: d [P, N] fp32 (rows by pair)
     int64_t y_ld = 0;
+    // down: fused score-weighted combine when fuse_cnt != nullptr ([T, ceil(N/128)]
+    // arrival counters, zero at the start of the call); the tokens' sums go to
+    // out [T, N] bf16, or through ro (ro.n > 0)
+    int32_t *fuse_cnt = nullptr;
+    const int32_t *idx = nullptr;
+    const float *scores = nullptr;
+    int top_k = 0, e0 = 0;
+    uint16_t *out = nullptr;
+    MoeRowsOut ro;
 };
 bool tc_moe_supported(int bits, int gs, int64_t H, int64_t I, int64_t E, const void *x,
                       int64_t x_ld);
@@ -167,17 +187,6 @@ cudaError_t launch_dequantize(const uint32_t *wq, const uint16_t *s, const uint1
 size_t moe_workspace_bytes(int64_t T, int64_t E, int64_t top_k, int64_t H, int64_t I);
 size_t moe_partial_workspace_bytes(int64_t T, int64_t E, int64_t ne, int64_t top_k, int64_t H,
                                    int64_t I);
-// Where the switch step of one expert shard writes its fp32 partial sums when
-// they go straight to the tokens' owners: the call's tokens are n regions of
-// `per` rows; token q * per + i goes to row row0 + i of dst[q] (rows i >=
-// count[q] are padding and are not written).  n == 0: not used.
-struct MoeRowsOut {
-    int n = 0;
-    int64_t per = 0, row0 = 0;
-    const int32_t *count = nullptr;  // [n], device memory
-    float *dst[8] = {};
-};
-
 // The switch step for experts [e0, e0 + ne) of E_total (weights: those ne
 // experts).  y: bf16 result (all experts); y_partial: fp32 partial sums;
 // rows_out (non-null, n > 0): fp32 partial sums into other ranks' buffers.

@@ -109,17 +109,12 @@ __global__ void __launch_bounds__(256) quantize_kernel(const void *__restrict__ 
     }
 }
 
-// MLX CPU dequantize of one code in the scales' dtype T: T(T(s*q) + b), each
-// step one rounding.
-template <bool F16>
-__device__ __forceinline__ uint16_t dq_one(float s, float b, uint32_t q) {
-    const float p = t16_to_f32<F16>(f32_to_t16<F16>(__fmul_rn(s, (float)q)));
-    return f32_to_t16<F16>(__fadd_rn(p, b));
-}
-
 // Dequantize: one thread per 16 bytes of packed words (32 codes at 4 bits,
-// 16 codes at 8 bits); output 64 or 32 contiguous bytes of bf16 (fp16 when
-// the scales are fp16).
+// 16 codes at 8 bits, always inside one group); output 64 or 32 contiguous
+// bytes of bf16 (fp16 when the scales are fp16).  Codes are dequantized in
+// packed pairs exactly as the matmul kernels do it (nq_common.cuh): biased
+// codes, one packed fma or sub/mul and one packed add per two codes, each
+// rounding the exact value once -- the same bits as T(T(s*q) + b).
 template <int BITS, bool F16>
 __global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t *__restrict__ wq,
                                                          const uint16_t *__restrict__ scales,
@@ -136,18 +131,34 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t *__restr
     const uint4 raw = *reinterpret_cast<const uint4 *>(wq + row * Kw + vec * 4);
     const int64_t k0 = vec * kCodes;
     const int64_t gidx = row * (K / gs) + k0 / gs;
-    const float s = t16_to_f32<F16>(scales[gidx]);
-    const float b = t16_to_f32<F16>(biases[gidx]);
+    const uint16_t sv = scales[gidx], bv = biases[gidx];
     const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
     uint32_t outw[kCodes / 2];
+    if constexpr (BITS == 4) {
+        const Dq4 d = F16 ? Dq4{} : make_dq4(sv, bv);
+        const Dq4h dh = make_dq4h(sv, bv);
 #pragma unroll
-    for (int i = 0; i < kCodes / 2; ++i) {
-        constexpr int per = 32 / BITS;
-        constexpr uint32_t mask = (1u << BITS) - 1u;
-        const int c0 = 2 * i, c1 = 2 * i + 1;
-        const uint32_t q0 = (words[c0 / per] >> (BITS * (c0 % per))) & mask;
-        const uint32_t q1 = (words[c1 / per] >> (BITS * (c1 % per))) & mask;
-        outw[i] = (uint32_t)dq_one<F16>(s, b, q0) | ((uint32_t)dq_one<F16>(s, b, q1) << 16);
+        for (int i = 0; i < 4; ++i) {
+            uint32_t p[4];  // (q_j, q_{j+4}) for j = 0..3
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                p[j] = F16 ? dqh_pair(q4_pair_biased_h(words[i], j), dh)
+                           : dq4_pair(q4_pair_biased(words[i], j), d);
+            outw[4 * i + 0] = prmt(p[0], p[1], 0x5410u);  // (q0, q1)
+            outw[4 * i + 1] = prmt(p[2], p[3], 0x5410u);  // (q2, q3)
+            outw[4 * i + 2] = prmt(p[0], p[1], 0x7632u);  // (q4, q5)
+            outw[4 * i + 3] = prmt(p[2], p[3], 0x7632u);  // (q6, q7)
+        }
+    } else {
+        const Dq4h dh = make_dq4h(sv, bv);
+        const Dq8 d8 = F16 ? Dq8{} : make_dq8(sv, bv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            outw[2 * i + 0] = F16 ? dqh_pair(q8_pair_biased_h(words[i], 0, 1), dh)
+                                  : dq8_pair(words[i], 0, 1, d8);
+            outw[2 * i + 1] = F16 ? dqh_pair(q8_pair_biased_h(words[i], 2, 3), dh)
+                                  : dq8_pair(words[i], 2, 3, d8);
+        }
     }
     uint4 *dst = reinterpret_cast<uint4 *>(out + row * K + k0);
 #pragma unroll

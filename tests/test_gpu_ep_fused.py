@@ -29,10 +29,13 @@ def comm1():
     c.close()
 
 
-@pytest.mark.parametrize("T", [1, 20, 300])
-def test_ep_fused_one_rank_equals_switch(oracle, nqlib, comm1, T):
+@pytest.mark.parametrize("T,fused_combine", [(1, "0"), (20, "0"), (300, "0"), (300, "1")])
+def test_ep_fused_one_rank_equals_switch(oracle, nqlib, comm1, monkeypatch, T, fused_combine):
+    """fused_combine "1": the combine folded into the down kernel writes the
+    returned rows (NQ_MOE_FUSED_COMBINE)."""
     import neurons_b200 as nb
     from neurons_b200 import dist
+    monkeypatch.setenv("NQ_MOE_FUSED_COMBINE", fused_combine)
     E, k, H, I = 128, 8, 2048, 768
     rng = np.random.default_rng(700 + T)
     (gh, gd), (uh, ud), (dh, dd) = (_experts(oracle, rng, E, I, H), _experts(oracle, rng, E, I, H),

@@ -228,3 +228,35 @@ def test_switch_qwen3_T2048_sampled_tokens(oracle, nqlib):
                                                  down, 4, 64, rounding=rounding))
         r = r.astype(np.float64)
         assert np.linalg.norm(yy - r) / np.linalg.norm(r) < 1e-2, rounding
+
+
+@pytest.mark.parametrize("T", [512, 2048])
+def test_fused_combine_matches_combine_kernel(oracle, nqlib, monkeypatch, T):
+    """The score-weighted combine folded into the tensor-core down kernel
+    (NQ_MOE_FUSED_COMBINE=1: the last pair of a token to land in an n-block
+    sums the token's pairs in slot order) gives the same bits as the separate
+    combine kernel, on two calls in a row (arrival counters reset), and the
+    oracle's combine stage applied to the GPU's h."""
+    import neurons_b200 as nb
+    E, k, H, I = 128, 8, 2048, 768
+    rng = np.random.default_rng(900 + T)
+    gate, up, down = (experts(oracle, rng, E, I, H), experts(oracle, rng, E, I, H),
+                      experts(oracle, rng, E, H, I))
+    for call in range(2):
+        x = acts(rng, T, H)
+        idx, sc = oracle.moe_route(acts(rng, T, E), k)
+        args = (dev_bf16(x), dev_i32(idx), dev_f32(sc), dev3(gate), dev3(up), dev3(down), 64, 4)
+        monkeypatch.setenv("NQ_MOE_FUSED_COMBINE", "0")
+        ref = nb.moe_switch(*args)
+        monkeypatch.setenv("NQ_MOE_FUSED_COMBINE", "1")
+        ws = torch.zeros(nb.moe_workspace_size(T, E, k, H, I), dtype=torch.uint8, device="cuda")
+        y = nb.moe_switch(*args, workspace=ws)
+        torch.cuda.synchronize()
+        assert nb.take_device_error() == 0
+        assert torch.equal(y, ref), f"T={T} call {call}"
+        if call == 0:
+            rows = np.random.default_rng(T).choice(T, 32, replace=False)
+            h = workspace_hidden(ws, T, E, k, H, I).reshape(T, k, I)[rows].reshape(-1, I)
+            assert_close(host_u16(y)[rows],
+                         oracle.moe_combine(h, idx[rows], sc[rows], down, 4, 64, rounding=1),
+                         f"T={T} fused combine vs oracle")
