@@ -36,11 +36,12 @@ namespace nq {
 namespace {
 
 constexpr int kAttnThreads = 128;
-// Positions per attention CTA, 8 per warp.  Measured per layer at the
-// Llama-3.2-3B dims, positions ~130-190, CUDA graph: chunks of 32 / 64 / 128
-// positions (8 / 16 / 32 per warp) take 7.9 / 11.3 / 17.5 us: the per-warp
-// chain of dependent work, not the merge of more partials, sets the time.
-constexpr int kAttnChunk = 32;
+// Positions per attention CTA, 4 per warp.  Measured per layer at the
+// Llama-3.2-3B dims, positions ~130-190, CUDA graph: chunks of 16 / 32 / 64 /
+// 128 positions (4 / 8 / 16 / 32 per warp) take 6.9 / 7.9 / 11.3 / 17.5 us,
+// and 2-warp CTAs are slower than 4-warp ones: the per-warp chain of
+// dependent work, not the merge of more partials, sets the time.
+constexpr int kAttnChunk = 16;
 constexpr int kMaxGroup = 8;     // query heads per KV head
 
 template <typename... Args>
