@@ -1253,24 +1253,70 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
     }
 }
 
+size_t rows_smem_bytes(int kbw, int W, int M) {
+    return (size_t)W * M * kbw * 16 * 16 + (size_t)W * 4 * 32 * sizeof(float);
+}
+
+// CTAs of the row-group kernel (kbw k-blocks per warp, W warps, M tokens) that
+// can be resident at once on this device; asked once per device and shape.
+int64_t rows_resident(int kbw, int W, int M) {
+    constexpr int kDev = 16;
+    static std::mutex mu;
+    static int cache[kDev][9][17][9];  // [device][kbw][W][M], 0: not asked yet
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kDev || kbw > 8 || W > 16 || M > 8) {
+        cudaGetLastError();
+        return 0;
+    }
+    std::lock_guard<std::mutex> lk(mu);
+    int &c = cache[d][kbw][W][M];
+    if (c == 0) {
+        const void *kern = nullptr;
+        switch (kbw) {
+            case 2: kern = (const void *)qgemv_rows_kernel<2, false>; break;
+            case 3: kern = (const void *)qgemv_rows_kernel<3, false>; break;
+            case 4: kern = (const void *)qgemv_rows_kernel<4, false>; break;
+            case 6: kern = (const void *)qgemv_rows_kernel<6, false>; break;
+            default: kern = (const void *)qgemv_rows_kernel<8, false>; break;
+        }
+        const size_t smem = rows_smem_bytes(kbw, W, M);
+        int n = 0;
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 32 * W, smem) != cudaSuccess)
+            n = 0;
+        cudaGetLastError();
+        c = n > 0 ? n : -1;
+    }
+    return c > 0 ? (int64_t)c * sm_count() : 0;
+}
+
 // k-blocks per warp for the row-group kernel, 0 when it does not serve the
-// problem.  Few rows: short slices (more warps per row group finish the
-// post-dependency work sooner); many rows (at least 4 row groups per SM, so
-// several CTAs per SM anyway): long slices, fewer warps and fewer partial
-// sums.
-int rows_kbw(int64_t kb_total, int64_t row_groups) {
+// problem.  The weights of every row group are fetched before the dependency
+// release only if all the row groups are resident at once, so slicings that
+// fit one wave come first: short slices (more warps per row group finish the
+// post-dependency work sooner; up to 12 warps with slices of <= 4 k-blocks,
+// measured best on 4096 and 3072 columns), then any slicing of up to 16
+// warps.  Shapes no slicing fits in one wave: with at least 4 row groups per
+// SM long slices (fewer warps, fewer partial sums), else short ones.
+int rows_kbw(int64_t kb_total, int64_t row_groups, int M) {
     static const int kShort[] = {2, 3, 4, 6, 8};
     static const int kLong[] = {8, 6, 4, 3, 2};
     auto fits = [&](int kbw, int64_t wmax) {
         return kb_total % kbw == 0 && kb_total / kbw >= 4 && kb_total / kbw <= wmax;
     };
+    auto one_wave = [&](int kbw) {
+        return rows_resident(kbw, (int)(kb_total / kbw), M) >= row_groups;
+    };
+    for (int kbw : kShort)
+        if (kbw <= 4 && fits(kbw, 12) && one_wave(kbw)) return kbw;
+    for (int kbw : kShort)
+        if (fits(kbw, 16) && one_wave(kbw)) return kbw;
     if (row_groups >= 4 * (int64_t)sm_count()) {
         for (int kbw : kLong)
             if (fits(kbw, 16)) return kbw;
         return 0;
     }
-    // up to 12 warps where a slice of <= 4 k-blocks allows it (measured best on
-    // 4096 and 3072 columns), else up to 16
     for (int kbw : kShort)
         if (kbw <= 4 && fits(kbw, 12)) return kbw;
     for (int kbw : kShort)
@@ -1280,7 +1326,7 @@ int rows_kbw(int64_t kb_total, int64_t row_groups) {
 
 template <int KBW, bool F16>
 cudaError_t launch_rows(const RowsParams &p, int W, cudaStream_t stream) {
-    const size_t smem = (size_t)W * p.M * KBW * 16 * 16 + (size_t)W * 4 * 32 * sizeof(float);
+    const size_t smem = rows_smem_bytes(KBW, W, p.M);
     auto kern = qgemv_rows_kernel<KBW, F16>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1310,7 +1356,7 @@ cudaError_t launch_rows_checked(RowsParams p, const void *x, cudaStream_t stream
     // CTAs of consecutive calls still fit an SM side by side)
     if ((int64_t)p.M * p.K * 2 > 96 * 1024) return cudaErrorNotSupported;
     const int64_t kb_total = p.K / 128;
-    const int kbw = rows_kbw(kb_total, (p.N + 15) / 16);
+    const int kbw = rows_kbw(kb_total, (p.N + 15) / 16, p.M);
     if (!kbw) return cudaErrorNotSupported;
     const int W = (int)(kb_total / kbw);
     if (f16) {
@@ -1374,7 +1420,7 @@ cudaError_t try_launch_rows(const GemvProblems &q, cudaStream_t stream) {
 
 bool rows_fused_supported(int64_t N, int64_t K, int bits) {
     return bits == 4 && N >= 1 && K % 128 == 0 && K * 2 <= 96 * 1024 &&
-           N <= ((int64_t)1 << 31) * 16 && rows_kbw(K / 128, (N + 15) / 16) != 0;
+           N <= ((int64_t)1 << 31) * 16 && rows_kbw(K / 128, (N + 15) / 16, 1) != 0;
 }
 
 cudaError_t launch_rows_f16(const uint16_t *x, int M, const uint32_t *w, const uint16_t *s,
