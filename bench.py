@@ -571,7 +571,10 @@ def _events_time(step, steps, warmup, world, graph=False, clocks=None):
     """Device time of `steps` calls of step(i), bracketed by a barrier and a
     synchronize, CUDA events on the current stream, max over ranks.  With
     graph=True the steps are captured in one CUDA graph and replayed, as a
-    decode loop does, so host submission is not timed."""
+    decode loop does, so host submission is not timed.  The multi-rank steps
+    use it too: their ranks wait for one another inside every step (flag
+    barriers, collectives), so without a graph any rank's host jitter (a
+    launch delayed by another thread of the process) stalls all of them."""
     import torch
     for i in range(warmup):
         step(i)
@@ -630,7 +633,7 @@ def time_tp(comm, M, N, K, steps, warmup, world, rank):
         x, wq, s, b, y, ws = sets[i % 3]
         dist.tp_quantized_matmul(comm, x, wq, s, b, N, GS, BITS, out=y, workspace=ws)
 
-    t = _events_time(step, steps, warmup, world, graph=M <= 32)
+    t = _events_time(step, steps, warmup, world, graph=True)
     assert nb.take_device_error() == 0
     return t
 
@@ -667,7 +670,7 @@ def time_ep(comm, T, steps, warmup, world, rank):
         dist.ep_moe_switch(comm, x, T, idx, sc, W[0], W[1], W[2], E, GS, BITS, workspace=ws,
                            out=y)
 
-    t = _events_time(step, steps, warmup, world)
+    t = _events_time(step, steps, warmup, world, graph=True)
     assert nb.take_device_error() == 0
     return t
 
@@ -702,7 +705,7 @@ def time_ep_fused(comm, T, steps, warmup, world, rank, arena_offset):
         dist.ep_moe_switch_fused(comm, x, T, idx, sc, W[0], W[1], W[2], E, arena_offset, GS, BITS,
                                  workspace=ws, out=y)
 
-    t = _events_time(step, steps, warmup, world)
+    t = _events_time(step, steps, warmup, world, graph=True)
     assert nb.take_device_error() == 0 and comm.take_error() == 0
     return t
 
@@ -728,7 +731,7 @@ def time_tp_fused(comm, M, N, K, steps, warmup, world, rank, clocks=None):
         x, wq, s, b, y = sets[i % 3]
         dist.tp_quantized_matmul_fused(comm, x, wq, s, b, N, y, GS, BITS)
 
-    t = _events_time(step, steps, warmup, world, graph=M <= 32, clocks=clocks)
+    t = _events_time(step, steps, warmup, world, graph=True, clocks=clocks)
     assert nb.take_device_error() == 0 and comm.take_error() == 0
     return t
 
@@ -772,7 +775,9 @@ def tp_headline(M, N, K, steps, warmup, world, rank, local):
     comm = dist.Comm()
     comm.symmetric_alloc(3 * ((M * N * 2 + 255) // 256 * 256))
     clk = ClockSampler(local)
-    t = time_tp_fused(comm, M, N, K, steps, warmup, world, rank, clocks=clk)
+    # a fresh arena: its peer mappings' first touches (remote TLB fills over
+    # NVLink) are warmed up before the timed steps
+    t = time_tp_fused(comm, M, N, K, steps, max(warmup, 10), world, rank, clocks=clk)
     n_e = min(steps, 50)
     t_e, h2d, d2h = time_e2e_tp(comm, M, N, K, n_e, warmup, world, rank)
     comm.close()
