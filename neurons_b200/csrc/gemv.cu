@@ -29,7 +29,9 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "nq_common.cuh"
 #include "nq_internal.h"
@@ -1063,6 +1065,7 @@ struct RowsParams {
     // epilogue: y = bf16(res + bf16(acc)) when res != nullptr (rows res_ld apart)
     const uint16_t *res;
     int64_t res_ld;
+    unsigned int *err;  // device error word (bounded-wait timeouts)
 };
 
 // x = bf16(bf16(bf16(sigmoid(g)) * g) * u) for one bf16 pair each of g, u:
@@ -1103,10 +1106,10 @@ __device__ __forceinline__ uint4 pair_permute(uint4 v) {
     return o;
 }
 
-template <int KBW, bool F16>
+template <int KBW, bool F16, bool PAIR>
 __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
     constexpr int XCH = KBW * 16;  // 16-byte x chunks per token in a warp's slice
-    extern __shared__ __align__(16) uint4 rows_smem[];
+    extern __shared__ __align__(128) uint4 rows_smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int W = blockDim.x >> 5;
     const int g = lane >> 2, c = lane & 3;
@@ -1115,7 +1118,36 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
     float *red = reinterpret_cast<float *>(rows_smem + (size_t)W * M * XCH);  // [W][4][32]
     pdl_launch_dependents();
     const int kb0 = warp * KBW;
-    const int64_t r0 = (int64_t)blockIdx.x * 16;
+    const int64_t r0 = (int64_t)blockIdx.x * (PAIR ? 32 : 16);
+    // PAIR: the CTA's second group of 16 rows (r0 + 16 ...) travels by bulk
+    // copies into shared memory, issued here, before the dependency wait, so
+    // that its weights stream beside the first group's register loads.
+    // Layout after red: 16 rows of packed codes (row stride rs bytes, padded
+    // so that the two rows a quarter-warp reads fall in different banks),
+    // then 16 rows of scales and 16 of biases (G * 2 bytes each), then the
+    // mbarrier.
+    const int64_t rs = (p.K / 2) + (((p.K / 2) & 127) == 0 ? 64 : 0);
+    uint8_t *bsm = reinterpret_cast<uint8_t *>(red + W * 4 * 32);
+    uint8_t *bss = bsm + 16 * rs;
+    uint8_t *bsb = bss + 16 * p.G * 2;
+    uint64_t *bbar = reinterpret_cast<uint64_t *>(bsb + 16 * p.G * 2);
+    if constexpr (PAIR) {
+        if (threadIdx.x == 0) {
+            mbar_init(bbar, 1);
+            fence_barrier_init();
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            mbar_expect_tx(bbar, (uint32_t)(16 * (p.K / 2 + 4 * p.G)));
+            for (int h = 0; h < 16; ++h) {
+                // rows past N copy row N-1 (valid memory) and are never stored
+                const int64_t row = min(r0 + 16 + h, p.N - 1);
+                bulk_g2s(bsm + h * rs, p.w + row * p.Kw, (uint32_t)(p.K / 2), bbar);
+                bulk_g2s(bss + h * p.G * 2, p.s + row * p.G, (uint32_t)(p.G * 2), bbar);
+                bulk_g2s(bsb + h * p.G * 2, p.b + row * p.G, (uint32_t)(p.G * 2), bbar);
+            }
+        }
+    }
     uint4 wv[KBW][2];
     uint32_t sv[KBW][2], bv[KBW][2];
 #pragma unroll
@@ -1183,6 +1215,45 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
     }
     __syncwarp();
     const uint4 *xr = xs + min(g, M - 1) * XCH + c;
+#pragma unroll 1
+  for (int grp2 = 0; grp2 < (PAIR ? 2 : 1); ++grp2) {
+    const int64_t rg0 = r0 + 16 * grp2;  // first row of this group
+    if (PAIR && grp2 == 1) {
+        // the second group: its copies have landed (bounded wait); every warp
+        // is done reading red for the first group's stores
+        bool ok = true;
+        if (!mbar_try_wait(bbar, 0)) {
+            const unsigned long long t0 = global_timer_ns();
+            while (!mbar_try_wait(bbar, 0)) {
+                if (global_timer_ns() - t0 > kWaitLimitNs) {
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        if (!ok) {
+            atomicOr(p.err, kErrWaitTimeout);
+            // let the copies in flight finish (bounded) before the CTA exits
+            const unsigned long long t1 = global_timer_ns();
+            while (!mbar_try_wait(bbar, 0) && global_timer_ns() - t1 < kWaitLimitNs) {
+            }
+        }
+        __syncthreads();
+        if (!ok || rg0 >= p.N) return;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint8_t *wrow = bsm + (8 * h + g) * rs + kb0 * 64 + c * 16;
+            const uint16_t *srow = reinterpret_cast<const uint16_t *>(bss + (8 * h + g) * p.G * 2);
+            const uint16_t *brow = reinterpret_cast<const uint16_t *>(bsb + (8 * h + g) * p.G * 2);
+#pragma unroll
+            for (int i = 0; i < KBW; ++i) {
+                wv[i][h] = *reinterpret_cast<const uint4 *>(wrow + i * 64);
+                const int grp = ((kb0 + i) * 128 + c * 32) >> p.gs_shift;
+                sv[i][h] = srow[grp];
+                bv[i][h] = brow[grp];
+            }
+        }
+    }
     float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int kbi = 0; kbi < KBW; ++kbi) {
@@ -1243,7 +1314,7 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
         float v = 0.f;
         for (int w = 0; w < W; ++w) v += red[(w * 4 + j) * 32 + lane];
         const int m = 2 * c + (j & 1);
-        const int64_t n = r0 + g + 8 * (j >> 1);
+        const int64_t n = rg0 + g + 8 * (j >> 1);
         if (m < M && n < p.N) {
             uint16_t out = f32_to_t16<F16>(v);
             if (!F16 && p.res)
@@ -1251,90 +1322,121 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
             p.y[(int64_t)m * p.y_ld + n] = out;
         }
     }
+  }
 }
 
-size_t rows_smem_bytes(int kbw, int W, int M) {
-    return (size_t)W * M * kbw * 16 * 16 + (size_t)W * 4 * 32 * sizeof(float);
+// Dynamic shared memory of the row-group kernel: x staging and the K-slice
+// sums, plus, for paired groups, the second group's rows, scales, biases and
+// the mbarrier.
+size_t rows_smem_bytes(int kbw, int W, int M, bool pair, int64_t K, int64_t G) {
+    size_t b = (size_t)W * M * kbw * 16 * 16 + (size_t)W * 4 * 32 * sizeof(float);
+    if (pair) {
+        const int64_t rs = K / 2 + ((K / 2) % 128 == 0 ? 64 : 0);
+        b += (size_t)(16 * rs + 16 * G * 2 * 2) + 16;
+    }
+    return b;
 }
 
-// CTAs of the row-group kernel (kbw k-blocks per warp, W warps, M tokens) that
-// can be resident at once on this device; asked once per device and shape.
-int64_t rows_resident(int kbw, int W, int M) {
-    constexpr int kDev = 16;
+template <bool PAIR>
+const void *rows_kernel_ptr(int kbw) {
+    switch (kbw) {
+        case 2: return (const void *)qgemv_rows_kernel<2, false, PAIR>;
+        case 3: return (const void *)qgemv_rows_kernel<3, false, PAIR>;
+        case 4: return (const void *)qgemv_rows_kernel<4, false, PAIR>;
+        case 6: return (const void *)qgemv_rows_kernel<6, false, PAIR>;
+        default: return (const void *)qgemv_rows_kernel<8, false, PAIR>;
+    }
+}
+
+// CTAs of the row-group kernel that can be resident at once on this device
+// (asked once per device and configuration).
+int64_t rows_resident(int kbw, int W, int M, bool pair, size_t smem) {
     static std::mutex mu;
-    static int cache[kDev][9][17][9];  // [device][kbw][W][M], 0: not asked yet
+    static std::map<std::tuple<int, int, int, int, bool, size_t>, int> cache;
     int d = 0;
-    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kDev || kbw > 8 || W > 16 || M > 8) {
+    if (cudaGetDevice(&d) != cudaSuccess) {
         cudaGetLastError();
         return 0;
     }
     std::lock_guard<std::mutex> lk(mu);
-    int &c = cache[d][kbw][W][M];
-    if (c == 0) {
-        const void *kern = nullptr;
-        switch (kbw) {
-            case 2: kern = (const void *)qgemv_rows_kernel<2, false>; break;
-            case 3: kern = (const void *)qgemv_rows_kernel<3, false>; break;
-            case 4: kern = (const void *)qgemv_rows_kernel<4, false>; break;
-            case 6: kern = (const void *)qgemv_rows_kernel<6, false>; break;
-            default: kern = (const void *)qgemv_rows_kernel<8, false>; break;
-        }
-        const size_t smem = rows_smem_bytes(kbw, W, M);
+    const auto key = std::make_tuple(d, kbw, W, M, pair, smem);
+    auto it = cache.find(key);
+    if (it == cache.end()) {
+        const void *kern = pair ? rows_kernel_ptr<true>(kbw) : rows_kernel_ptr<false>(kbw);
         int n = 0;
         if (smem > 48 * 1024)
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 32 * W, smem) != cudaSuccess)
             n = 0;
         cudaGetLastError();
-        c = n > 0 ? n : -1;
+        it = cache.emplace(key, n).first;
     }
-    return c > 0 ? (int64_t)c * sm_count() : 0;
+    return (int64_t)it->second * sm_count();
 }
 
-// k-blocks per warp for the row-group kernel, 0 when it does not serve the
-// problem.  The weights of every row group are fetched before the dependency
-// release only if all the row groups are resident at once, so slicings that
-// fit one wave come first: short slices (more warps per row group finish the
-// post-dependency work sooner; up to 12 warps with slices of <= 4 k-blocks,
-// measured best on 4096 and 3072 columns), then any slicing of up to 16
-// warps.  Shapes no slicing fits in one wave: with at least 4 row groups per
-// SM long slices (fewer warps, fewer partial sums), else short ones.
-int rows_kbw(int64_t kb_total, int64_t row_groups, int M) {
+struct RowsPlan {
+    int kbw = 0;
+    bool pair = false;
+};
+
+// k-blocks per warp (and whether a CTA takes two row groups, the second by
+// bulk copies into shared memory) for the row-group kernel; kbw == 0 when it
+// does not serve the problem.  The weights of every row group are fetched
+// before the dependency release only if all the CTAs are resident at once,
+// so plans that fit one wave come first: one group per CTA with short slices
+// (more warps per row group finish the post-dependency work sooner; up to 12
+// warps with slices of <= 4 k-blocks, measured best on 4096 and 3072
+// columns), then any slicing of up to 16 warps, then two groups per CTA
+// (measured: the decode step's 25 MB gate|up GEMV fits one wave that way).
+// Shapes no plan fits in one wave: with at least 4 row groups per SM long
+// slices (fewer warps, fewer partial sums), else short slices.
+RowsPlan rows_plan(int64_t kb_total, int64_t row_groups, int M, int64_t K, int64_t G,
+                   bool pair_ok) {
     static const int kShort[] = {2, 3, 4, 6, 8};
     static const int kLong[] = {8, 6, 4, 3, 2};
     auto fits = [&](int kbw, int64_t wmax) {
         return kb_total % kbw == 0 && kb_total / kbw >= 4 && kb_total / kbw <= wmax;
     };
-    auto one_wave = [&](int kbw) {
-        return rows_resident(kbw, (int)(kb_total / kbw), M) >= row_groups;
+    auto one_wave = [&](int kbw, bool pair) {
+        const int W = (int)(kb_total / kbw);
+        const int64_t ctas = pair ? (row_groups + 1) / 2 : row_groups;
+        return rows_resident(kbw, W, M, pair, rows_smem_bytes(kbw, W, M, pair, K, G)) >= ctas;
     };
     for (int kbw : kShort)
-        if (kbw <= 4 && fits(kbw, 12) && one_wave(kbw)) return kbw;
+        if (kbw <= 4 && fits(kbw, 12) && one_wave(kbw, false)) return {kbw, false};
     for (int kbw : kShort)
-        if (fits(kbw, 16) && one_wave(kbw)) return kbw;
+        if (fits(kbw, 16) && one_wave(kbw, false)) return {kbw, false};
+    // (paired groups with 8-k-block slices exceed the 128 registers a
+    // 512-thread launch allows and spill)
+    if (pair_ok)
+        for (int kbw : kShort)
+            if (kbw < 8 && fits(kbw, 16) && one_wave(kbw, true)) return {kbw, true};
     if (row_groups >= 4 * (int64_t)sm_count()) {
+        // (two groups per CTA measured slower here: 74.7 against 55-64 us for
+        // the 128256 x 3072 LM head -- each CTA then computes its groups one
+        // after the other in a wave-bound launch)
         for (int kbw : kLong)
-            if (fits(kbw, 16)) return kbw;
-        return 0;
+            if (fits(kbw, 16)) return {kbw, false};
+        return {};
     }
     for (int kbw : kShort)
-        if (kbw <= 4 && fits(kbw, 12)) return kbw;
+        if (kbw <= 4 && fits(kbw, 12)) return {kbw, false};
     for (int kbw : kShort)
-        if (fits(kbw, 16)) return kbw;
-    return 0;
+        if (fits(kbw, 16)) return {kbw, false};
+    return {};
 }
 
-template <int KBW, bool F16>
+template <int KBW, bool F16, bool PAIR>
 cudaError_t launch_rows(const RowsParams &p, int W, cudaStream_t stream) {
-    const size_t smem = rows_smem_bytes(KBW, W, p.M);
-    auto kern = qgemv_rows_kernel<KBW, F16>;
+    const size_t smem = rows_smem_bytes(KBW, W, p.M, PAIR, p.K, p.G);
+    auto kern = qgemv_rows_kernel<KBW, F16, PAIR>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
         if (e != cudaSuccess) return e;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((p.N + 15) / 16), 1, 1);
+    cfg.gridDim = dim3((unsigned)((p.N + (PAIR ? 31 : 15)) / (PAIR ? 32 : 16)), 1, 1);
     cfg.blockDim = dim3(32 * W, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -1356,25 +1458,40 @@ cudaError_t launch_rows_checked(RowsParams p, const void *x, cudaStream_t stream
     // CTAs of consecutive calls still fit an SM side by side)
     if ((int64_t)p.M * p.K * 2 > 96 * 1024) return cudaErrorNotSupported;
     const int64_t kb_total = p.K / 128;
-    const int kbw = rows_kbw(kb_total, (p.N + 15) / 16, p.M);
+    // two row groups per CTA (the second by bulk copies): bf16 only; scale and
+    // bias rows must be whole 16-byte pieces and 16-byte aligned
+    const bool pair_ok = !f16 && (p.G * 2) % 16 == 0 &&
+                         !((reinterpret_cast<uintptr_t>(p.s) | reinterpret_cast<uintptr_t>(p.b) |
+                            reinterpret_cast<uintptr_t>(p.w)) & 15);
+    const RowsPlan plan = rows_plan(kb_total, (p.N + 15) / 16, p.M, p.K, p.G, pair_ok);
+    const int kbw = plan.kbw;
     if (!kbw) return cudaErrorNotSupported;
     const int W = (int)(kb_total / kbw);
     if (f16) {
         if (p.pro != kRowsPlain || p.res) return cudaErrorNotSupported;
         switch (kbw) {
-            case 2: return launch_rows<2, true>(p, W, stream);
-            case 3: return launch_rows<3, true>(p, W, stream);
-            case 4: return launch_rows<4, true>(p, W, stream);
-            case 6: return launch_rows<6, true>(p, W, stream);
-            default: return launch_rows<8, true>(p, W, stream);
+            case 2: return launch_rows<2, true, false>(p, W, stream);
+            case 3: return launch_rows<3, true, false>(p, W, stream);
+            case 4: return launch_rows<4, true, false>(p, W, stream);
+            case 6: return launch_rows<6, true, false>(p, W, stream);
+            default: return launch_rows<8, true, false>(p, W, stream);
+        }
+    }
+    if (plan.pair) {
+        switch (kbw) {
+            case 2: return launch_rows<2, false, true>(p, W, stream);
+            case 3: return launch_rows<3, false, true>(p, W, stream);
+            case 4: return launch_rows<4, false, true>(p, W, stream);
+            case 6: return launch_rows<6, false, true>(p, W, stream);
+            default: return launch_rows<8, false, true>(p, W, stream);
         }
     }
     switch (kbw) {
-        case 2: return launch_rows<2, false>(p, W, stream);
-        case 3: return launch_rows<3, false>(p, W, stream);
-        case 4: return launch_rows<4, false>(p, W, stream);
-        case 6: return launch_rows<6, false>(p, W, stream);
-        default: return launch_rows<8, false>(p, W, stream);
+        case 2: return launch_rows<2, false, false>(p, W, stream);
+        case 3: return launch_rows<3, false, false>(p, W, stream);
+        case 4: return launch_rows<4, false, false>(p, W, stream);
+        case 6: return launch_rows<6, false, false>(p, W, stream);
+        default: return launch_rows<8, false, false>(p, W, stream);
     }
 }
 
@@ -1400,6 +1517,7 @@ RowsParams rows_params(const uint32_t *w, const uint16_t *s, const uint16_t *b, 
     p.eps = 0.f;
     p.res = nullptr;
     p.res_ld = 0;
+    p.err = device_error_word();
     return p;
 }
 
@@ -1420,7 +1538,7 @@ cudaError_t try_launch_rows(const GemvProblems &q, cudaStream_t stream) {
 
 bool rows_fused_supported(int64_t N, int64_t K, int bits) {
     return bits == 4 && N >= 1 && K % 128 == 0 && K * 2 <= 96 * 1024 &&
-           N <= ((int64_t)1 << 31) * 16 && rows_kbw(K / 128, (N + 15) / 16, 1) != 0;
+           N <= ((int64_t)1 << 31) * 16 && rows_plan(K / 128, (N + 15) / 16, 1, K, K / 64, false).kbw != 0;
 }
 
 cudaError_t launch_rows_f16(const uint16_t *x, int M, const uint32_t *w, const uint16_t *s,

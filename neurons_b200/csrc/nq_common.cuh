@@ -256,6 +256,17 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *tmap, ui
         : "memory");
 }
 
+// Untiled bulk copy global -> this CTA's shared memory, completing on an
+// mbarrier (no multicast).  Both addresses 16-byte aligned, bytes a multiple
+// of 16.
+__device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *src, uint32_t bytes,
+                                         uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(smem_dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // TMA store of a 2-D box from shared memory (bulk-group completion).
 __device__ __forceinline__ void tma_store_2d(const void *tmap, const void *smem_src, int32_t c0,
                                              int32_t c1) {

@@ -282,6 +282,27 @@ def test_row_group_gemv_many_rows(oracle, nqlib):
     assert_close(y[:, -16:], oracle.qmm(x, wq[-16:], s[-16:], b[-16:], 4, 64), "last rows")
 
 
+@pytest.mark.parametrize("N,M", [(16400, 1), (16400, 8), (16384, 2)])
+def test_row_group_gemv_paired_groups(oracle, nqlib, N, M):
+    """Two row groups per CTA, the second staged by bulk copies into shared
+    memory (shapes whose single-group CTAs do not fit one wave, here about
+    the decode step's gate|up).  N = 16400: the last CTA's second group lies
+    past the end and must store nothing; every row at the ragged end is
+    checked."""
+    import neurons_b200 as nb
+    rng = np.random.default_rng(N + M)
+    K = 3072
+    wq, s, b = oracle.quantize(weights(rng, N, K), 4, 64, 0)
+    x = acts(rng, M, K)
+    y = host_u16(nb.quantized_matmul(dev_bf16(x), dev_u32(wq), dev_bf16(s), dev_bf16(b), True,
+                                      64, 4))
+    torch.cuda.synchronize()
+    assert nb.take_device_error() == 0
+    rows = np.sort(rng.choice(N, 256, replace=False))
+    assert_close(y[:, rows], oracle.qmm(x, wq[rows], s[rows], b[rows], 4, 64), f"{N}x{K} M={M}")
+    assert_close(y[:, -48:], oracle.qmm(x, wq[-48:], s[-48:], b[-48:], 4, 64), "last rows")
+
+
 def test_row_group_gemv_chained_launches(oracle, nqlib):
     """Back-to-back row-group launches under programmatic dependent launch:
     y2 = W2 y1 right after y1 = W1 x (the second kernel's weight loads run
