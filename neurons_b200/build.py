@@ -24,7 +24,7 @@ ROOT = os.path.dirname(HERE)
 INCLUDE = os.path.join(ROOT, "include")
 
 CU_SOURCES = ["abi.cu", "quant.cu", "gemv.cu", "gemm_tc.cu", "gemm_tc_moe.cu", "moe.cu",
-              "llama.cu"]
+              "moe_small.cu", "llama.cu"]
 CPP_SOURCES = ["cuda_backend.cpp", "model_loader.cpp"]
 HEADERS = ["nq_common.cuh", "nq_internal.h", "cuda_backend.h", "iface/compute_types.h",
            "iface/compute_backend.h", "model_loader.h"]

@@ -450,6 +450,12 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
         dn.max_m = up.max_m;
         dn.tile_m = up.tile_m;
     } else {
+        // a few tokens over all experts: two kernels, the down one forming
+        // the weighted sum (no d round trip, no combine launch)
+        if (y && !y_partial && ro.n == 0 && e0 == 0 && E == E_total &&
+            moe_small_supported(T, H, I, E, top_k, bits, x))
+            return launch_moe_small(x, T, H, I, E, top_k, idx, scores, gw, gs_, gb, uw, us, ub,
+                                    dw, ds, db, gsz, ws.h, y, stream);
         // pair i reads token i / top_k
         up.P = (int)P;
         up.M = 1;

@@ -199,6 +199,18 @@ cudaError_t launch_moe_switch(const uint16_t *x, int64_t T, int64_t H, int64_t I
                               float *y_partial, cudaStream_t stream,
                               const MoeRowsOut *rows_out = nullptr);
 
+// The switch step for a few tokens (every pair its own problem, T * top_k <=
+// E, all experts on this device, 4-bit codes) in two kernels, the down one
+// forming the score-weighted sum itself (moe_small.cu).  h: [T * top_k, I].
+bool moe_small_supported(int64_t T, int64_t H, int64_t I, int64_t E, int64_t top_k, int bits,
+                         const void *x);
+cudaError_t launch_moe_small(const uint16_t *x, int64_t T, int64_t H, int64_t I, int64_t E,
+                             int64_t top_k, const int32_t *idx, const float *scores,
+                             const uint32_t *gw, const uint16_t *gs, const uint16_t *gb,
+                             const uint32_t *uw, const uint16_t *us, const uint16_t *ub,
+                             const uint32_t *dw, const uint16_t *ds, const uint16_t *db, int gsz,
+                             uint16_t *h, uint16_t *y, cudaStream_t stream);
+
 cudaError_t launch_moe_route(const uint16_t *logits, int64_t T, int64_t E, int64_t top_k,
                              int32_t *idx, float *scores, cudaStream_t stream);
 
