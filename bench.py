@@ -1049,10 +1049,10 @@ def ours(args):
         for T, n in ((1, 500), (64, 200), (2048, 20)):
             t_m, b_m, f_m, _ = time_moe(T, n, 3, world, seed=rank + 300 + T)
             moe[f"T{T}"] = moe_summary(T, t_m, n, b_m, f_m, world, pk)
-            # router + (pair mode: up, down, combine | grouped: count, scan,
-            # fill, [group_rows on the tensor-core path], up, down, combine)
+            # router + (a few tokens: up, down-with-combine | grouped: count,
+            # scan, fill, [group_rows on the tensor-core path], up, down, combine)
             P = T * QWEN3_MOE["top_k"]
-            line["gpu_launches"] += n * (4 if P <= QWEN3_MOE["E"] else
+            line["gpu_launches"] += n * (3 if P <= QWEN3_MOE["E"] else
                                          (8 if P >= 8 * QWEN3_MOE["E"] else 7))
         line["moe"] = moe
     if args.workload == "prefill" and not args.no_quant:
