@@ -1039,14 +1039,20 @@ cudaError_t dispatch_tma(const CUtensorMap &m1, const CUtensorMap &m2, const Gem
 //     and its scale/bias values straight into registers before
 //     griddepcontrol.wait, so with programmatic dependent launch the weight
 //     stream of one projection runs under the tail of the previous kernel.
-//     Nothing else is in flight on the critical path: no ring, no mbarrier, no
-//     cluster.
+//     Nothing else is in flight on the critical path: no ring, no cluster.
+//   * PAIR: a CTA takes two groups; the second group's rows, scales and
+//     biases travel by untiled bulk copies into shared memory (one mbarrier,
+//     bounded wait), also issued before griddepcontrol.wait.  Used when that
+//     is what lets every CTA of the launch be resident at once (rows_plan).
 //   * After the wait each warp copies its slice of x into its own shared
 //     memory, pairs permuted to the order of the mma.sync B fragments
 //     ((x0,x4),(x1,x5),(x2,x6),(x3,x7)) and chunks laid out so that the four
 //     lanes of a row read consecutive 16-byte chunks.
 //   * The unrolled main loop dequantizes exactly (as the kernels above) into
 //     mma.sync A fragments; the K-slices are summed in shared memory.
+//   * Optional prologue in the staging of x (RMSNorm of the row, or SwiGLU of
+//     a [gate | up] row) and residual epilogue (launch_rows_fused): the decode
+//     step's norms, activation and residual adds run inside its GEMVs.
 // Measured (B200, CUDA graph of back-to-back calls): 4096x4096 at M=1 5.0 us
 // against 7.9 us for the TMA-fed kernel, 3072x3072 3.7 against 8.5 us.
 // ----------------------------------------------------------------------------
