@@ -1072,6 +1072,10 @@ struct RowsParams {
     const uint16_t *res;
     int64_t res_ld;
     unsigned int *err;  // device error word (bounded-wait timeouts)
+    // epi_swiglu (M == 1): every group of 16 rows is 8 gate rows followed by
+    // the 8 matching up rows; the output is y[8 * group + i] =
+    // swiglu(bf16(gate_i), bf16(up_i)) (N / 2 values)
+    int epi_swiglu;
 };
 
 // x = bf16(bf16(bf16(sigmoid(g)) * g) * u) for one bf16 pair each of g, u:
@@ -1315,7 +1319,20 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
     __syncthreads();
     // warp j (< 4) sums accumulator element j over the K slices and stores it:
     // element j of lane (g, c) is token 2c + (j & 1) of row g + 8 (j >> 1)
-    if (warp < 4) {
+    if (!F16 && p.epi_swiglu) {
+        // the token's gate (row g, element 0) and up (row g + 8, element 2)
+        // values of lanes c == 0, rounded to bf16 like the outputs of two
+        // separate projections, then the SwiGLU op chain
+        if (warp == 0 && c == 0 && rg0 < p.N) {
+            float gv = 0.f, uv = 0.f;
+            for (int w = 0; w < W; ++w) {
+                gv += red[(w * 4 + 0) * 32 + lane];
+                uv += red[(w * 4 + 2) * 32 + lane];
+            }
+            const uint32_t pr = (uint32_t)f32_to_bf16(gv) | ((uint32_t)f32_to_bf16(uv) << 16);
+            p.y[(rg0 / 16) * 8 + g] = (uint16_t)swiglu_pair(pr & 0xFFFFu, pr >> 16);
+        }
+    } else if (warp < 4) {
         const int j = warp;
         float v = 0.f;
         for (int w = 0; w < W; ++w) v += red[(w * 4 + j) * 32 + lane];
@@ -1524,6 +1541,7 @@ RowsParams rows_params(const uint32_t *w, const uint16_t *s, const uint16_t *b, 
     p.res = nullptr;
     p.res_ld = 0;
     p.err = device_error_word();
+    p.epi_swiglu = 0;
     return p;
 }
 
@@ -1560,7 +1578,9 @@ cudaError_t launch_rows_fused(const RowsFusedArgs &a, cudaStream_t stream) {
     if (a.prologue == kRowsSwiglu && (a.x_ld < 2 * a.K)) return cudaErrorNotSupported;
     if (a.prologue == kRowsNorm && (!a.norm_w || (reinterpret_cast<uintptr_t>(a.norm_w) & 15)))
         return cudaErrorNotSupported;
+    if (a.epi_swiglu && (a.M != 1 || a.N % 16 || a.res)) return cudaErrorNotSupported;
     RowsParams p = rows_params(a.w, a.s, a.b, a.N, a.K, a.gs, a.x, a.x_ld, a.M, a.y, a.y_ld);
+    p.epi_swiglu = a.epi_swiglu;
     p.pro = a.prologue;
     p.nw = a.norm_w;
     p.eps = a.eps;

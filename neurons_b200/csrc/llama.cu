@@ -14,10 +14,11 @@
 // previous step's argmax wrote to device memory, so steps queue back to back
 // on the stream (or replay from a CUDA graph) with no host round trip.
 //
-// B200 layout: q/k/v and gate/up weights are concatenated row-wise at
-// creation, so each is one GEMV launch; RMSNorm runs inside the following
-// GEMV's staging of x, SwiGLU inside the down projection's, and both
-// residual adds in the GEMVs' stores (launch_rows_fused).  Five launches per
+// B200 layout: q/k/v weights are concatenated row-wise and gate/up rows
+// interleaved in groups of 8 at creation, so each is one GEMV launch; RMSNorm
+// runs inside the following GEMV's staging of x, SwiGLU in the gate|up GEMV's
+// stores (a CTA holds each gate row with its up row), and both residual adds
+// in the GEMVs' stores (launch_rows_fused).  Five launches per
 // layer: qkv, attention, o, gate/up, down; then the final norm, the LM head
 // and the argmax.
 #include <cuda_runtime.h>
@@ -481,9 +482,40 @@ cudaError_t concat_rows(const nq_qweight_t *parts, const int64_t *rows, int n, i
     return cudaSuccess;
 }
 
+// gate and up rows interleaved in groups of 8 (8 gate rows, the matching 8 up
+// rows, ...): the row-group GEMV then holds each gate row and its up row in one
+// CTA and forms SwiGLU in its stores
+cudaError_t interleave_gate_up(const nq_qweight_t &gate, const nq_qweight_t &up, int64_t I,
+                               int64_t K, int bits, int gs, uint32_t **w, uint16_t **s,
+                               uint16_t **b, LlamaDecoder &d) {
+    const int64_t kw = K * bits / 32, G = K / gs;
+    cudaError_t e;
+    if ((e = d.alloc(w, (size_t)(2 * I * kw))) != cudaSuccess) return e;
+    if ((e = d.alloc(s, (size_t)(2 * I * G))) != cudaSuccess) return e;
+    if ((e = d.alloc(b, (size_t)(2 * I * G))) != cudaSuccess) return e;
+    const nq_qweight_t *src[2] = {&gate, &up};
+    for (int h = 0; h < 2; ++h) {
+        // rows [8i, 8i + 8) of the source -> rows [16i + 8h, 16i + 8h + 8)
+        const size_t wrow = kw * 4, srow = G * 2;
+        if ((e = cudaMemcpy2D(reinterpret_cast<char *>(*w) + 8 * h * wrow, 16 * wrow, src[h]->w,
+                              8 * wrow, 8 * wrow, (size_t)(I / 8), cudaMemcpyDeviceToDevice)))
+            return e;
+        if ((e = cudaMemcpy2D(reinterpret_cast<char *>(*s) + 8 * h * srow, 16 * srow,
+                              src[h]->scales, 8 * srow, 8 * srow, (size_t)(I / 8),
+                              cudaMemcpyDeviceToDevice)))
+            return e;
+        if ((e = cudaMemcpy2D(reinterpret_cast<char *>(*b) + 8 * h * srow, 16 * srow,
+                              src[h]->biases, 8 * srow, 8 * srow, (size_t)(I / 8),
+                              cudaMemcpyDeviceToDevice)))
+            return e;
+    }
+    return cudaSuccess;
+}
+
 cudaError_t gemv(const LlamaDecoder &d, const uint16_t *x, int64_t x_ld, const uint32_t *w,
                  const uint16_t *s, const uint16_t *b, int64_t N, int64_t K, uint16_t *y,
-                 int prologue, const uint16_t *nw, const uint16_t *res, cudaStream_t st) {
+                 int prologue, const uint16_t *nw, const uint16_t *res, cudaStream_t st,
+                 int epi_swiglu = 0) {
     RowsFusedArgs a;
     a.x = x;
     a.x_ld = x_ld;
@@ -502,6 +534,7 @@ cudaError_t gemv(const LlamaDecoder &d, const uint16_t *x, int64_t x_ld, const u
     a.eps = d.c.rms_eps;
     a.res = res;
     a.res_ld = N;
+    a.epi_swiglu = epi_swiglu;
     return launch_rows_fused(a, st);
 }
 
@@ -556,10 +589,12 @@ cudaError_t llama_step(LlamaDecoder &d, const int32_t *tok_src, float *logits_f3
         if ((e = gemv(d, d.attn, nq_, L.o_w, L.o_s, L.o_b, H, nq_, d.h, 0, nullptr, d.h, st)) !=
             cudaSuccess)
             return e;
+        // gate|up (interleaved) with the norm in its prologue and SwiGLU in its
+        // stores: d.gu gets the I activations; down adds the residual
         if ((e = gemv(d, d.h, H, L.gu_w, L.gu_s, L.gu_b, 2 * I, H, d.gu, 1, L.post_norm, nullptr,
-                      st)) != cudaSuccess)
+                      st, 1)) != cudaSuccess)
             return e;
-        if ((e = gemv(d, d.gu, 2 * I, L.d_w, L.d_s, L.d_b, H, I, d.h, 2, nullptr, d.h, st)) !=
+        if ((e = gemv(d, d.gu, I, L.d_w, L.d_s, L.d_b, H, I, d.h, 0, nullptr, d.h, st)) !=
             cudaSuccess)
             return e;
     }
@@ -633,10 +668,8 @@ cudaError_t llama_create(LlamaDecoder &d, const nq_llama_config_t &c,
         if ((e = concat_rows(qkv, qkv_rows, 3, H, c.bits, c.group_size, &L.qkv_w, &L.qkv_s,
                              &L.qkv_b, d)) != cudaSuccess)
             return e;
-        const nq_qweight_t gu[2] = {s.gate, s.up};
-        const int64_t gu_rows[2] = {I, I};
-        if ((e = concat_rows(gu, gu_rows, 2, H, c.bits, c.group_size, &L.gu_w, &L.gu_s, &L.gu_b,
-                             d)) != cudaSuccess)
+        if ((e = interleave_gate_up(s.gate, s.up, I, H, c.bits, c.group_size, &L.gu_w, &L.gu_s,
+                                    &L.gu_b, d)) != cudaSuccess)
             return e;
         L.o_w = s.o.w;
         L.o_s = s.o.scales;

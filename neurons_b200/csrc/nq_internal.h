@@ -63,7 +63,7 @@ struct GemvProblems {
 cudaError_t launch_gemv(const GemvProblems &p, cudaStream_t stream);
 
 // Decode-step GEMV of the row-group kernel (4-bit codes, K % 128 == 0) with a
-// prologue fused into the staging of x and a residual epilogue:
+// prologue fused into the staging of x and a residual or SwiGLU epilogue:
 //   prologue 0: x as is; 1: x = bf16(norm_w * bf16(x * rsqrt(mean(x^2) + eps)))
 //   (MLX rms_norm); 2: x = swiglu(g, u) for the row [g (K) | u (K)];
 //   res != nullptr: y = bf16(res + bf16(x . W^T)).
@@ -84,6 +84,10 @@ struct RowsFusedArgs {
     float eps = 0.f;
     const uint16_t *res = nullptr;
     int64_t res_ld = 0;
+    // 1 (M == 1, N % 16 == 0): the weight rows come in groups of 8 gate rows
+    // followed by the 8 matching up rows, and y gets the N / 2 values
+    // bf16(bf16(bf16(sigmoid(g)) * g) * u) of g, u rounded to bf16
+    int epi_swiglu = 0;
 };
 cudaError_t launch_rows_fused(const RowsFusedArgs &a, cudaStream_t stream);
 // fp16 x, scales, biases and y (an fp16 checkpoint), M <= 8, 4-bit codes:
