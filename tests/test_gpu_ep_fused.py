@@ -3,7 +3,8 @@ communicator of one rank on one GPU: every token is sent to this rank, its
 flags are set by its own kernels (no wait depends on another process), and
 the result must equal the single-GPU switch step nq_moe_switch wherever both
 group the pairs by expert -- the same kernels, the same fp32 sums over the
-same slots in the same order -- and match the oracle normwise.  Shapes: the Qwen3-30B-A3B
+same slots in the same order -- agree with it normwise where it takes its
+few-token kernels, and match the oracle normwise.  Shapes: the Qwen3-30B-A3B
 layer dims (E=128, top-8, H=2048, I=768, 4-bit g64)."""
 import numpy as np
 import pytest
@@ -51,8 +52,12 @@ def test_ep_fused_one_rank_equals_switch(oracle, nqlib, comm1, monkeypatch, T, f
         assert nb.take_device_error() == 0 and comm1.take_error() == 0
         if T * k > E:  # both group the pairs by expert: the same kernels
             assert torch.equal(y, ref), f"T={T} call {call}: differs from nq_moe_switch"
-        else:  # nq_moe_switch takes pair mode here, the expert shard always groups
-            assert_close(host_u16(y), host_u16(ref), f"T={T} call {call}")
+        else:
+            # nq_moe_switch takes its few-token kernels here, the expert shard
+            # always groups: two different roundings of the two-stage step, so
+            # they agree end to end (normwise), as each agrees with the oracle
+            yy, rr = y.float(), ref.float()
+            assert float((yy - rr).norm() / rr.norm()) < 1e-2, f"T={T} call {call}"
         if call == 0:
             r = oracle.moe_switch(x, idx, sc, (gh[0], gh[1], gh[2]), (uh[0], uh[1], uh[2]),
                                   (dh[0], dh[1], dh[2]), 4, 64, rounding=1)
