@@ -1045,7 +1045,9 @@ cudaError_t dispatch_tma(const CUtensorMap &m1, const CUtensorMap &m2, const Gem
 //     bounded wait), also issued before griddepcontrol.wait.  Used when that
 //     is what lets every CTA of the launch be resident at once (rows_plan).
 //   * After the wait each warp copies its slice of x into its own shared
-//     memory, pairs permuted to the order of the mma.sync B fragments
+//     memory (all of a lane's global reads issued at once: its x chunks, the
+//     prologue's second operand, the residual it will add), pairs permuted
+//     to the order of the mma.sync B fragments
 //     ((x0,x4),(x1,x5),(x2,x6),(x3,x7)) and chunks laid out so that the four
 //     lanes of a row read consecutive 16-byte chunks.
 //   * The unrolled main loop dequantizes exactly (as the kernels above) into
@@ -1053,8 +1055,9 @@ cudaError_t dispatch_tma(const CUtensorMap &m1, const CUtensorMap &m2, const Gem
 //   * Optional prologue in the staging of x (RMSNorm of the row, or SwiGLU of
 //     a [gate | up] row) and residual epilogue (launch_rows_fused): the decode
 //     step's norms, activation and residual adds run inside its GEMVs.
-// Measured (B200, CUDA graph of back-to-back calls): 4096x4096 at M=1 5.0 us
-// against 7.9 us for the TMA-fed kernel, 3072x3072 3.7 against 8.5 us.
+// Measured (B200, CUDA graph of back-to-back calls on weight sets larger than
+// L2): 4096x4096 at M=1 6.0 us (the TMA-fed kernel: 7.9 us); 256x4096 3.3 us,
+// the part that does not shrink with the weights.
 // ----------------------------------------------------------------------------
 constexpr int kRowsPlain = 0, kRowsNorm = 1, kRowsSwiglu = 2;
 
@@ -1179,48 +1182,127 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
         }
     }
     pdl_wait();  // x may be the previous kernel's output
-    float ss = 0.f;  // kRowsNorm (M == 1): this lane's share of sum(x^2)
-    for (int q = lane; q < M * XCH; q += 32) {
-        const int m = q / XCH, ck = q % XCH;  // chunk ck of the slice covers codes kb0*128 + 8*ck ...
-        const uint16_t *xr = p.x + (int64_t)m * p.x_ld + kb0 * 128 + ck * 8;
-        uint4 v = ldg16(xr);
-        if (!F16 && p.pro == kRowsSwiglu) {
-            const uint4 u = ldg16(xr + p.K);  // x row = [gate (K) | up (K)]
-            v.x = swiglu_pair(v.x, u.x);
-            v.y = swiglu_pair(v.y, u.y);
-            v.z = swiglu_pair(v.z, u.z);
-            v.w = swiglu_pair(v.w, u.w);
-        } else if (!F16 && p.pro == kRowsNorm) {
-            const uint32_t e[4] = {v.x, v.y, v.z, v.w};
+    // Everything this thread reads from global memory after the wait is
+    // issued at once: its x chunks (with the up half, or the norm weights,
+    // of the prologue) and the residual of the output element it stores, so
+    // that the chain after the dependency release holds one memory round
+    // trip, not one per chunk.
+    const bool swi = !F16 && p.pro == kRowsSwiglu, norm = !F16 && p.pro == kRowsNorm;
+    uint16_t res0 = 0;  // residual of this thread's output element, first group
+    if (!F16 && p.res && warp < 4) {
+        const int m = 2 * c + (warp & 1);
+        const int64_t n = r0 + g + 8 * (warp >> 1);
+        if (m < M && n < p.N) res0 = p.res[(int64_t)m * p.res_ld + n];
+    }
+    constexpr int XPL = (XCH + 31) / 32;  // x chunks per lane and token
+    // (long slices, KBW > 4, keep one chunk in flight at a time: their
+    // registers hold the weights)
+    if constexpr (XPL > 2) {
+        float ss = 0.f;
+        for (int q = lane; q < M * XCH; q += 32) {
+            const int m = q / XCH, ck = q % XCH;
+            const uint16_t *xr = p.x + (int64_t)m * p.x_ld + kb0 * 128 + ck * 8;
+            uint4 v = ldg16(xr);
+            if (swi) {
+                const uint4 u = ldg16(xr + p.K);
+                v.x = swiglu_pair(v.x, u.x);
+                v.y = swiglu_pair(v.y, u.y);
+                v.z = swiglu_pair(v.z, u.z);
+                v.w = swiglu_pair(v.w, u.w);
+            } else if (norm) {
+                const uint32_t e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float lo = bf16_to_f32((uint16_t)e[j]), hi = bf16_to_f32((uint16_t)(e[j] >> 16));
-                ss = fmaf(lo, lo, ss);
-                ss = fmaf(hi, hi, ss);
+                for (int t = 0; t < 4; ++t) {
+                    const float lo = bf16_to_f32((uint16_t)e[t]);
+                    const float hi = bf16_to_f32((uint16_t)(e[t] >> 16));
+                    ss = fmaf(lo, lo, ss);
+                    ss = fmaf(hi, hi, ss);
+                }
+            }
+            const int kbi = ck >> 4, cc = (ck >> 2) & 3, i = ck & 3;
+            xs[m * XCH + kbi * 16 + i * 4 + cc] = pair_permute(v);
+        }
+        if (norm) {
+            __shared__ float ss_warp_l[16];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) ss_warp_l[warp] = ss;
+            __syncthreads();
+            float tot = 0.f;
+            for (int w = 0; w < W; ++w) tot += ss_warp_l[w];
+            const float inv = 1.0f / sqrtf(tot / (float)p.K + p.eps);
+            for (int ck = lane; ck < XCH; ck += 32) {
+                const int kbi = ck >> 4, cc = (ck >> 2) & 3, i = ck & 3;
+                uint4 &o = xs[kbi * 16 + i * 4 + cc];
+                const uint4 wn = pair_permute(ldg16(p.nw + kb0 * 128 + ck * 8));
+                o.x = norm_pair(o.x, wn.x, inv);
+                o.y = norm_pair(o.y, wn.y, inv);
+                o.z = norm_pair(o.z, wn.z, inv);
+                o.w = norm_pair(o.w, wn.w, inv);
             }
         }
-        const int kbi = ck >> 4, cc = (ck >> 2) & 3, i = ck & 3;
-        xs[m * XCH + kbi * 16 + i * 4 + cc] = pair_permute(v);
-    }
-    if (!F16 && p.pro == kRowsNorm) {
-        // mean of x^2 over the whole row: every warp's slice, through shared
-        // memory; then each lane normalises the chunks it staged
-        __shared__ float ss_warp[16];
+    } else
+    for (int m = 0; m < M; ++m) {
+        // chunk ck = lane + 32 j of the slice covers codes kb0*128 + 8*ck ...
+        uint4 v[XPL], u[XPL];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (lane == 0) ss_warp[warp] = ss;
-        __syncthreads();
-        float tot = 0.f;
-        for (int w = 0; w < W; ++w) tot += ss_warp[w];
-        const float inv = 1.0f / sqrtf(tot / (float)p.K + p.eps);
-        for (int ck = lane; ck < XCH; ck += 32) {
-            const int kbi = ck >> 4, cc = (ck >> 2) & 3, i = ck & 3;
-            uint4 &o = xs[kbi * 16 + i * 4 + cc];
-            const uint4 wn = pair_permute(ldg16(p.nw + kb0 * 128 + ck * 8));
-            o.x = norm_pair(o.x, wn.x, inv);
-            o.y = norm_pair(o.y, wn.y, inv);
-            o.z = norm_pair(o.z, wn.z, inv);
-            o.w = norm_pair(o.w, wn.w, inv);
+        for (int j = 0; j < XPL; ++j) {
+            const int ck = lane + 32 * j;
+            if (XCH % 32 == 0 || ck < XCH) {
+                const uint16_t *xr = p.x + (int64_t)m * p.x_ld + kb0 * 128 + ck * 8;
+                v[j] = ldg16(xr);
+                if (swi) u[j] = ldg16(xr + p.K);  // x row = [gate (K) | up (K)]
+                else if (norm) u[j] = ldg16(p.nw + kb0 * 128 + ck * 8);
+            }
+        }
+        if (norm) {
+            // (M == 1) mean of x^2 over the whole row: every warp's slice,
+            // through shared memory; then each lane normalises its chunks
+            __shared__ float ss_warp[16];
+            float ss = 0.f;
+#pragma unroll
+            for (int j = 0; j < XPL; ++j) {
+                if (XCH % 32 == 0 || lane + 32 * j < XCH) {
+                    const uint32_t e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const float lo = bf16_to_f32((uint16_t)e[t]);
+                        const float hi = bf16_to_f32((uint16_t)(e[t] >> 16));
+                        ss = fmaf(lo, lo, ss);
+                        ss = fmaf(hi, hi, ss);
+                    }
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) ss_warp[warp] = ss;
+            __syncthreads();
+            float tot = 0.f;
+            for (int w = 0; w < W; ++w) tot += ss_warp[w];
+            const float inv = 1.0f / sqrtf(tot / (float)p.K + p.eps);
+#pragma unroll
+            for (int j = 0; j < XPL; ++j) {
+                v[j].x = norm_pair(v[j].x, u[j].x, inv);
+                v[j].y = norm_pair(v[j].y, u[j].y, inv);
+                v[j].z = norm_pair(v[j].z, u[j].z, inv);
+                v[j].w = norm_pair(v[j].w, u[j].w, inv);
+            }
+        } else if (swi) {
+#pragma unroll
+            for (int j = 0; j < XPL; ++j) {
+                v[j].x = swiglu_pair(v[j].x, u[j].x);
+                v[j].y = swiglu_pair(v[j].y, u[j].y);
+                v[j].z = swiglu_pair(v[j].z, u[j].z);
+                v[j].w = swiglu_pair(v[j].w, u[j].w);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < XPL; ++j) {
+            const int ck = lane + 32 * j;
+            if (XCH % 32 == 0 || ck < XCH) {
+                const int kbi = ck >> 4, cc = (ck >> 2) & 3, i = ck & 3;
+                xs[m * XCH + kbi * 16 + i * 4 + cc] = pair_permute(v[j]);
+            }
         }
     }
     __syncwarp();
@@ -1340,8 +1422,10 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
         const int64_t n = rg0 + g + 8 * (j >> 1);
         if (m < M && n < p.N) {
             uint16_t out = f32_to_t16<F16>(v);
-            if (!F16 && p.res)
-                out = f32_to_bf16(bf16_to_f32(p.res[(int64_t)m * p.res_ld + n]) + bf16_to_f32(out));
+            if (!F16 && p.res) {
+                const uint16_t r = grp2 == 0 ? res0 : p.res[(int64_t)m * p.res_ld + n];
+                out = f32_to_bf16(bf16_to_f32(r) + bf16_to_f32(out));
+            }
             p.y[(int64_t)m * p.y_ld + n] = out;
         }
     }
