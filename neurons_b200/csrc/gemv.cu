@@ -1162,7 +1162,7 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
         }
     }
     uint4 wv[KBW][2];
-    uint32_t sv[KBW][2], bv[KBW][2];
+    uint32_t sb[KBW][2];  // scale | bias << 16
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         // rows past N read row N-1 (valid memory) and are never stored
@@ -1177,8 +1177,7 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
 #pragma unroll
         for (int i = 0; i < KBW; ++i) {
             const int grp = ((kb0 + i) * 128 + c * 32) >> p.gs_shift;
-            sv[i][h] = ldg_u16z(p.s + row * p.G + grp);
-            bv[i][h] = ldg_u16z(p.b + row * p.G + grp);
+            sb[i][h] = ldg_u16z(p.s + row * p.G + grp) | (ldg_u16z(p.b + row * p.G + grp) << 16);
         }
     }
     pdl_wait();  // x may be the previous kernel's output
@@ -1341,12 +1340,14 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
             for (int i = 0; i < KBW; ++i) {
                 wv[i][h] = *reinterpret_cast<const uint4 *>(wrow + i * 64);
                 const int grp = ((kb0 + i) * 128 + c * 32) >> p.gs_shift;
-                sv[i][h] = srow[grp];
-                bv[i][h] = brow[grp];
+                sb[i][h] = srow[grp] | ((uint32_t)brow[grp] << 16);
             }
         }
     }
-    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    // NACC independent accumulators (short slices: 4, so that each mma waits
+    // on one two steps back); summed at the end
+    constexpr int NACC = (KBW == 3 || KBW == 4) ? 4 : 2;
+    float acc[NACC][4] = {};
 #pragma unroll
     for (int kbi = 0; kbi < KBW; ++kbi) {
         uint4 xv[4];
@@ -1354,8 +1355,8 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
         for (int i = 0; i < 4; ++i) xv[i] = xr[kbi * 16 + i * 4];
         if constexpr (F16) {
             // fp16 scales and biases: biased codes 1024 + q, exact fp16 dequant
-            const Dq4h da = make_dq4h((uint16_t)sv[kbi][0], (uint16_t)bv[kbi][0]);
-            const Dq4h db = make_dq4h((uint16_t)sv[kbi][1], (uint16_t)bv[kbi][1]);
+            const Dq4h da = make_dq4h((uint16_t)sb[kbi][0], (uint16_t)(sb[kbi][0] >> 16));
+            const Dq4h db = make_dq4h((uint16_t)sb[kbi][1], (uint16_t)(sb[kbi][1] >> 16));
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const uint32_t w0 = (&wv[kbi][0].x)[i], w1 = (&wv[kbi][1].x)[i];
@@ -1368,15 +1369,15 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
                 const uint32_t c1 = dqh_pair(lop3_and_or(w1 >> 8, 0x000F000Fu, 0x64006400u), db);
                 const uint32_t c2 = dqh_pair(lop3_and_or(w04 >> 8, 0x000F000Fu, 0x64006400u), da);
                 const uint32_t c3 = dqh_pair(lop3_and_or(w14 >> 8, 0x000F000Fu, 0x64006400u), db);
-                mma16816h(acc[0], a0, a1, a2, a3, xv[i].x, xv[i].y);
-                mma16816h(acc[1], c0, c1, c2, c3, xv[i].z, xv[i].w);
+                mma16816h(acc[(i * 2) % NACC], a0, a1, a2, a3, xv[i].x, xv[i].y);
+                mma16816h(acc[(i * 2 + 1) % NACC], c0, c1, c2, c3, xv[i].z, xv[i].w);
             }
         } else {
             Dq4 da, db;
-            da.s2 = prmt(sv[kbi][0], 0u, 0x1010u);
-            da.b2 = prmt(bv[kbi][0], 0u, 0x1010u);
-            db.s2 = prmt(sv[kbi][1], 0u, 0x1010u);
-            db.b2 = prmt(bv[kbi][1], 0u, 0x1010u);
+            da.s2 = prmt(sb[kbi][0], 0u, 0x1010u);
+            da.b2 = prmt(sb[kbi][0], 0u, 0x3232u);
+            db.s2 = prmt(sb[kbi][1], 0u, 0x1010u);
+            db.b2 = prmt(sb[kbi][1], 0u, 0x3232u);
             da.n2 = bf2_fma(da.s2, 0xC300C300u, 0x80008000u);  // exact -128*s
             db.n2 = bf2_fma(db.s2, 0xC300C300u, 0x80008000u);
 #pragma unroll
@@ -1391,13 +1392,15 @@ __global__ void __launch_bounds__(512) qgemv_rows_kernel(const RowsParams p) {
                 const uint32_t c1 = dq4_pair(lop3_and_or(w1 >> 8, 0x000F000Fu, 0x43004300u), db);
                 const uint32_t c2 = dq4_pair(lop3_and_or(w04 >> 8, 0x000F000Fu, 0x43004300u), da);
                 const uint32_t c3 = dq4_pair(lop3_and_or(w14 >> 8, 0x000F000Fu, 0x43004300u), db);
-                mma16816(acc[0], a0, a1, a2, a3, xv[i].x, xv[i].y);
-                mma16816(acc[1], c0, c1, c2, c3, xv[i].z, xv[i].w);
+                mma16816(acc[(i * 2) % NACC], a0, a1, a2, a3, xv[i].x, xv[i].y);
+                mma16816(acc[(i * 2 + 1) % NACC], c0, c1, c2, c3, xv[i].z, xv[i].w);
             }
         }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) red[(warp * 4 + j) * 32 + lane] = acc[0][j] + acc[1][j];
+    for (int j = 0; j < 4; ++j)
+        red[(warp * 4 + j) * 32 + lane] =
+            NACC == 4 ? (acc[0][j] + acc[2][j]) + (acc[1][j] + acc[3][j]) : acc[0][j] + acc[1][j];
     __syncthreads();
     // warp j (< 4) sums accumulator element j over the K slices and stores it:
     // element j of lane (g, c) is token 2c + (j & 1) of row g + 8 (j >> 1)
