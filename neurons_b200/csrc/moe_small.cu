@@ -141,8 +141,10 @@ struct SmallArgs {
     int E, top_k, gs_shift;
 };
 
-// grid (I / 16, T * k); W = H / (128 * kUpKbw) warps
-__global__ void __launch_bounds__(512) moe_small_up_kernel(const SmallArgs a) {
+// grid (I / 16, T * k); W = H / (128 * kUpKbw) warps.  80 registers (87
+// uncapped) let three 256-thread CTAs share an SM, so the T = 1 grid at the
+// Qwen3 dims (48 x 8 CTAs) is one wave: measured 21.4 -> 20.7 us per step.
+__global__ void __maxnreg__(80) moe_small_up_kernel(const SmallArgs a) {
     constexpr int KBW = kUpKbw, XCH = KBW * 16;
     extern __shared__ __align__(16) uint4 up_smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
