@@ -9,6 +9,8 @@ quantized with the min/max scheme, activations N(0, 1) in bf16, seeded):
   square   x [2048, 4096] . W[4096, 4096]^T    (TFLOP/s)
   decode   x [1, 4096]    . W[4096, 4096]^T    (GB/s of algorithmic bytes)
   lmhead   x [1, 3072]    . W[128256, 3072]^T  (GB/s; a 4-bit tied LM head)
+  sweep    14336x4096 and 4096x14336, bits 4/8, group 32/64/128, M 1..2048
+           (one line of per-point times and roofline fractions)
 A step is one quantized_matmul call through the C ABI.  Each rank runs its
 own full step on its own GPU (token batches are independent: no collective on
 the data path, weak scaling); the timed region is bracketed by a barrier and a
@@ -167,7 +169,7 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
-def make_inputs(M, N, K, sets, seed):
+def make_inputs(M, N, K, sets, seed, bits=BITS, gs=GS):
     """R independent (x, W) sets quantized on the device (min/max scheme)."""
     import torch
     import neurons_b200 as nb
@@ -175,7 +177,7 @@ def make_inputs(M, N, K, sets, seed):
     out = []
     for _ in range(sets):
         w = torch.randn(N, K, device="cuda", generator=g) * 0.02
-        wq, s, b = nb.quantize(w, GS, BITS, nb.SCHEME_MINMAX)
+        wq, s, b = nb.quantize(w, gs, bits, nb.SCHEME_MINMAX)
         del w
         x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
         y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
@@ -184,7 +186,7 @@ def make_inputs(M, N, K, sets, seed):
     return out
 
 
-def time_device(M, N, K, steps, warmup, world, seed, clocks=None):
+def time_device(M, N, K, steps, warmup, world, seed, clocks=None, bits=BITS, gs=GS):
     """Device-resident inputs.  Returns (seconds for `steps` launches, max over
     ranks; mean seconds per launch on this rank; input sets used).
 
@@ -195,14 +197,14 @@ def time_device(M, N, K, steps, warmup, world, seed, clocks=None):
     replays a captured step."""
     import torch
     import neurons_b200 as nb
-    per_set = algo_bytes(M, N, K) + M * N * 2
+    per_set = algo_bytes(M, N, K, bits, gs) + M * N * 2
     sets = max(2, -(-3 * L2_BYTES // per_set))
     sets = min(sets, 64)
-    data = make_inputs(M, N, K, sets, seed)
+    data = make_inputs(M, N, K, sets, seed, bits, gs)
     stream = torch.cuda.current_stream()
     for i in range(warmup):
         x, wq, s, b, y = data[i % sets]
-        nb.quantized_matmul(x, wq, s, b, True, GS, BITS, out=y)
+        nb.quantized_matmul(x, wq, s, b, True, gs, bits, out=y)
     torch.cuda.synchronize()
     graph = None
     if M <= 32:
@@ -210,7 +212,7 @@ def time_device(M, N, K, steps, warmup, world, seed, clocks=None):
         with torch.cuda.graph(graph):
             for i in range(steps):
                 x, wq, s, b, y = data[i % sets]
-                nb.quantized_matmul(x, wq, s, b, True, GS, BITS, out=y)
+                nb.quantized_matmul(x, wq, s, b, True, gs, bits, out=y)
         for _ in range(max(1, warmup // steps + 1)):
             graph.replay()
         torch.cuda.synchronize()
@@ -226,7 +228,7 @@ def time_device(M, N, K, steps, warmup, world, seed, clocks=None):
     else:
         for i in range(steps):
             x, wq, s, b, y = data[i % sets]
-            nb.quantized_matmul(x, wq, s, b, True, GS, BITS, out=y)
+            nb.quantized_matmul(x, wq, s, b, True, gs, bits, out=y)
     t1.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop() if clocks is not None else None
@@ -941,6 +943,34 @@ def torch_cpu_baseline(M, N, K, target_s=5.0):
             "tflops": algo_flops(M, N, K) / sec / 1e12, "gbs": algo_bytes(M, N, K) / sec / 1e9}
 
 
+SWEEP_SHAPES = ((14336, 4096), (4096, 14336))
+SWEEP_M = (1, 8, 32, 128, 512, 2048)
+
+
+def time_sweep(steps, warmup, world, seed, pk):
+    """The quantized-matmul sweep: N x K in {14336 x 4096, 4096 x 14336}, bits
+    {4, 8}, group size {32, 64, 128}, M {1, 8, 32, 128, 512, 2048}; per point
+    the time per call (device-resident inputs, rotating sets larger than L2,
+    the same timing as the headline) and the fraction of its roofline,
+    max(bytes / HBM peak, flops / bf16 peak) / time."""
+    pts = []
+    for N, K in SWEEP_SHAPES:
+        for bits in (4, 8):
+            for gs in (32, 64, 128):
+                for M in SWEEP_M:
+                    n = steps if M <= 32 else max(10, steps // 10)
+                    _, per, _, _ = time_device(M, N, K, n, warmup, world, seed, bits=bits, gs=gs)
+                    byts, flops = algo_bytes(M, N, K, bits, gs), algo_flops(M, N, K)
+                    roof = max(byts / (pk["hbm_gbs"] * 1e9), flops / (pk["bf16_tflops"] * 1e12))
+                    pts.append({"N": N, "K": K, "bits": bits, "gs": gs, "M": M,
+                                "us": per * 1e6, "gbs": byts / per / 1e9,
+                                "tflops": flops / per / 1e12, "frac": roof / per,
+                                "bound": "hbm" if byts / (pk["hbm_gbs"] * 1e9) >=
+                                flops / (pk["bf16_tflops"] * 1e12) else "tensor"})
+    return {"workload": "sweep", "points": pts, "peaks": {"hbm_gbs": pk["hbm_gbs"],
+                                                          "bf16_tflops": pk["bf16_tflops"]}}
+
+
 def ours(args):
     import torch
     world, rank, local = dist_setup(args.gpus)
@@ -954,6 +984,11 @@ def ours(args):
         q = time_quant(args.steps, args.warmup, world, rank, pk)
         if rank == 0:
             print(json.dumps({"workload": "quant", **q}), flush=True)
+        return
+    if args.workload == "sweep":
+        sw = time_sweep(args.steps, args.warmup, world, rank, pk)
+        if rank == 0:
+            print(json.dumps(sw), flush=True)
         return
     if args.workload == "llama3b-step":
         # the decode step alone (--steps tokens after a 128-token prompt)
@@ -1225,7 +1260,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="prefill", choices=sorted(WORKLOADS) + ["llama3b-decode", "llama3b-step",
                                                              "quant", "moe-1", "moe-64",
-                                                             "moe-2048"])
+                                                             "moe-2048", "sweep"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-lines")
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE sub-line")

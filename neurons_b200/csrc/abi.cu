@@ -226,8 +226,28 @@ int nq_quantized_matmul_f16(const uint16_t *x, int64_t M, const uint32_t *wq,
     return from_cuda(nq::launch_tc_gemm(a, st), what);
 }
 
-// M at or above which the tcgen05 GEMM replaces the mma.sync GEMV.
-static int64_t tc_threshold() { return 33; }
+// Whether the tcgen05 GEMM serves a plain M x N x K call instead of the
+// mma.sync GEMVs.  The GEMM streams the weights in about the same time for
+// any M up to its 64-token tile (B200, 4-bit g64: 30 us at 14336 x 4096, 14 us
+// at 4096^2, 11 us at 3072^2), while a GEMV's time grows with M; measured
+// crossovers:
+//   * 8-bit: the GEMV only at M = 1 (4096 x 14336: 43 against 31 us at M = 2),
+//     with group size 128 up to M = 8 (its GEMV stays near 28 us there);
+//   * 4-bit: the row-group GEMV up to M = 8, except on weights of 32 M codes or
+//     more with 8192 rows or more (14336 x 4096, M = 8: 39.8 against 30.7 us);
+//     for M = 9..16 the GEMV on weights below 32 M codes (4096^2, M = 16: 11.4
+//     against 14.0 us); the GEMM from M = 17 (M = 32: 105 against 31 us).
+static bool tc_preferred(int64_t M, int64_t N, int64_t K, int bits, int gs) {
+    if (bits != 4) return M >= (gs == 128 ? 9 : 2);
+    const bool big = N * K >= ((int64_t)1 << 25);
+    if (M >= 17) return true;
+    if (M >= 9) return big;
+    return M == 8 && big && N >= 8192;
+}
+
+// M at or above which the tensor-parallel fan-out (push) calls take the
+// tcgen05 GEMM.
+static int64_t tc_push_threshold() { return 33; }
 
 int nq_quantized_matmul(const uint16_t *x, int64_t M, const uint32_t *wq, const uint16_t *scales,
                         const uint16_t *biases, int64_t N, int64_t K, int bits, int group_size,
@@ -246,7 +266,7 @@ int nq_quantized_matmul(const uint16_t *x, int64_t M, const uint32_t *wq, const 
         return fail(NQ_INVALID_INPUT, "nq_quantized_matmul: shape too large");
     if (int rc = need_device("nq_quantized_matmul")) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (M >= tc_threshold()) {
+    if (tc_preferred(M, N, K, bits, group_size)) {
         nq::TcGemmArgs a;
         a.x = x; a.x_ld = K; a.M = M;
         a.w = wq; a.s = scales; a.b = biases;
@@ -269,7 +289,7 @@ int nq_quantized_matmul_launches(int64_t M, int64_t N, int64_t K, int bits, int 
     if (M < 0) return fail(NQ_INVALID_INPUT, "nq_quantized_matmul_launches: M must be >= 0");
     if (M == 0 || N == 0) return 0;
     if (int rc = need_device("nq_quantized_matmul_launches")) return rc;
-    if (M >= tc_threshold()) {
+    if (tc_preferred(M, N, K, bits, group_size)) {
         // the shape alone decides; any 16-byte aligned operands take the same path
         static const uint4 aligned_probe[1] = {};
         nq::TcGemmArgs a;
@@ -305,7 +325,7 @@ static int push_validate(const char *what, const uint16_t *x, int64_t M, const u
         if (!push->dst[q]) return fail(NQ_INVALID_INPUT, std::string(what) + ": NULL destination");
     if (!aligned16(x) || !aligned16(wq))
         return fail(NQ_INVALID_INPUT, std::string(what) + ": x and wq must be 16-byte aligned");
-    if (M >= tc_threshold()) {
+    if (M >= tc_push_threshold()) {
         nq::TcGemmArgs a;
         a.x = x; a.x_ld = K; a.M = M;
         a.w = wq; a.s = scales; a.b = biases;
@@ -358,7 +378,7 @@ int nq_quantized_matmul_push(const uint16_t *x, int64_t M, const uint32_t *wq,
     for (int q = 0; q < pd.n; ++q) pd.delta[q] = static_cast<const char *>(push->dst[q]) - self;
     uint16_t *y = static_cast<uint16_t *>(push->dst[push->rank]) + col0;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (M >= tc_threshold()) {
+    if (M >= tc_push_threshold()) {
         nq::TcGemmArgs a;
         a.x = x; a.x_ld = K; a.M = M;
         a.w = wq; a.s = scales; a.b = biases;

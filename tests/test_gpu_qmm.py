@@ -1,5 +1,6 @@
 """GPU parity: quantized_matmul through the C ABI against the oracle, on both
-kernel paths (mma.sync GEMV for M <= 32, TMA + tcgen05 GEMM above), ragged
+kernel paths (mma.sync GEMVs for a few tokens, TMA + tcgen05 GEMM otherwise;
+the choice follows bits, M and the weight size), ragged
 shapes, both bit widths and every group size, the golden fixtures, and the
 full-size workloads (decode 4096x4096 at M=1; prefill 2048x14336x4096)."""
 import os
