@@ -245,9 +245,20 @@ static bool tc_preferred(int64_t M, int64_t N, int64_t K, int bits, int gs) {
     return M == 8 && big && N >= 8192;
 }
 
-// M at or above which the tensor-parallel fan-out (push) calls take the
-// tcgen05 GEMM.
-static int64_t tc_push_threshold() { return 33; }
+// Whether a tensor-parallel fan-out (push) call takes the tcgen05 GEMM: always
+// from 33 tokens (the GEMV fan-out serves at most 32), and below that wherever
+// the plain call on the same shard would, so that the fused and the NCCL
+// tensor-parallel paths run the same kernel and give the same bits.
+static bool push_uses_tc(int64_t M, int64_t N, int64_t K, int bits, int group_size,
+                         const uint16_t *x, const uint32_t *wq) {
+    if (M >= 33) return true;
+    if (!tc_preferred(M, N, K, bits, group_size)) return false;
+    nq::TcGemmArgs a;
+    a.x = x; a.x_ld = K; a.M = M;
+    a.w = wq;
+    a.N = N; a.K = K; a.bits = bits; a.gs = group_size;
+    return nq::tc_gemm_supported(a);
+}
 
 int nq_quantized_matmul(const uint16_t *x, int64_t M, const uint32_t *wq, const uint16_t *scales,
                         const uint16_t *biases, int64_t N, int64_t K, int bits, int group_size,
@@ -325,7 +336,7 @@ static int push_validate(const char *what, const uint16_t *x, int64_t M, const u
         if (!push->dst[q]) return fail(NQ_INVALID_INPUT, std::string(what) + ": NULL destination");
     if (!aligned16(x) || !aligned16(wq))
         return fail(NQ_INVALID_INPUT, std::string(what) + ": x and wq must be 16-byte aligned");
-    if (M >= tc_push_threshold()) {
+    if (push_uses_tc(M, N, K, bits, group_size, x, wq)) {
         nq::TcGemmArgs a;
         a.x = x; a.x_ld = K; a.M = M;
         a.w = wq; a.s = scales; a.b = biases;
@@ -378,7 +389,7 @@ int nq_quantized_matmul_push(const uint16_t *x, int64_t M, const uint32_t *wq,
     for (int q = 0; q < pd.n; ++q) pd.delta[q] = static_cast<const char *>(push->dst[q]) - self;
     uint16_t *y = static_cast<uint16_t *>(push->dst[push->rank]) + col0;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (M >= tc_push_threshold()) {
+    if (push_uses_tc(M, N, K, bits, group_size, x, wq)) {
         nq::TcGemmArgs a;
         a.x = x; a.x_ld = K; a.M = M;
         a.w = wq; a.s = scales; a.b = biases;

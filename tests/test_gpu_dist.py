@@ -43,8 +43,12 @@ def _worker(rank, world, port, q):
             r0, rows = dist.tp_shard(N, world, rank)
             y = dist.tp_quantized_matmul(comm, x, wq[r0:r0 + rows], s[r0:r0 + rows],
                                          b[r0:r0 + rows], N, 64, bits)
+            # this rank's columns are exactly the single-GPU call on its shard
+            # (the full-width call may plan its K split differently)
+            mine = nb.quantized_matmul(x, wq[r0:r0 + rows], s[r0:r0 + rows], b[r0:r0 + rows],
+                                       True, 64, bits)
             torch.cuda.synchronize()
-            out[f"tp{M}"] = (_rel(y, ref), torch.equal(y[:, r0:r0 + rows], ref[:, r0:r0 + rows]))
+            out[f"tp{M}"] = (_rel(y, ref), torch.equal(y[:, r0:r0 + rows], mine))
             # the fused variant: every rank's columns pushed over NVLink; three
             # calls on the same symmetric buffer (epochs, buffer reuse)
             yf = comm.symmetric_tensor(0, (M, N))
